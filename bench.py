@@ -1,0 +1,355 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 token sampler (the hot path of BASELINE.json).
+
+Headline workload (config C3): one full-vocabulary sampling pass over
+B=256 rows x V=262144 bf16 logits, top-k disabled, T=1, top-p 0.95, one draw
+per row -- a streaming, HBM-bound pass.  `value` is sampled rows/s of the whole
+job (all ranks; rows are independent, so N GPUs each sample their own 256 rows:
+weak scaling, no collective on the data path).  Also reported:
+  latency_b1   p50/p90 device us/step of config C1 (B=1 fp32, top-k 64, top-p 0.95)
+  roofline     algorithmic bytes / mean launch time of the sampling kernel vs
+               the measured HBM copy bandwidth (MEASURED_PEAKS.json)
+  e2e          rows/s through g4s_sample_host from pinned host memory (PCIe in
+               the timed region)
+  cpu_baseline the reference algorithm (oracle port of DoSample) on host cores
+
+`--impl reference` times the reference's own algorithm for the path (the C
+oracle port: the Delphi reference cannot be built here) on all host cores, on
+the same config and metric.
+"""
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "gemma4.pas_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "sampled rows/s at V=262144 B=256 (% HBM peak); p50 µs/step at B=1"
+ROWS, VOCAB, SOFTCAP = 256, 262144, 30.0
+BYTES_PER_ROW = VOCAB * 2  # bf16 logits read once
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def load_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic():
+    """DRAM bytes per launch of the full-path kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "full_chunk_kernel_c3.md")
+    try:
+        m = re.search(r"dram_bytes_per_launch:\s*([0-9]+)", open(path).read())
+        return int(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
+class Clocks:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(5)
+        except Exception:
+            self.proc.kill()
+        self.f.flush()
+        rows = []
+        for line in open(self.f.name):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        pw = [float(r[3]) for r in rows if re.match(r"^[0-9.]+$", r[3])]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None}
+
+
+def dist_setup(n):
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n:
+        raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}")
+    if n > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def allreduce_max(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_reference(rows_bf16, u, nthreads, min_cpu_s=10.0):
+    """The reference algorithm (oracle port of DoSample, fp32 transcription) on host
+    threads; repeats the sample until ~min_cpu_s of CPU work.  Returns rows/s."""
+    from oracle import oracle as O
+
+    p = O.params(1.0, 0, 0.95)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        O.sample_batch(rows_bf16, O.DTYPE_BF16, p, SOFTCAP, u, O.VARIANT_F32, O.TIE_HEAP, nthreads)
+        done += rows_bf16.shape[0]
+        el = time.perf_counter() - t0
+        if el * nthreads >= min_cpu_s:
+            return done / el, done, el
+
+
+def run_reference(args):
+    """--impl reference: the reference's algorithm for the path on the host cores."""
+    import numpy as np
+
+    import synth
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    nthreads = host_threads()
+    xb = synth.c3_logits(ROWS, step=0)
+    u = synth.uniforms(ROWS * (args.steps + args.warmup), synth.SEEDS["c3"]).reshape(-1, ROWS)
+    from oracle import oracle as O
+
+    O.load()
+    p = O.params(1.0, 0, 0.95)
+    for w in range(args.warmup):
+        O.sample_batch(xb[:nthreads], O.DTYPE_BF16, p, SOFTCAP, u[w][:nthreads], O.VARIANT_F32, O.TIE_HEAP, nthreads)
+    t0 = time.perf_counter()
+    for s in range(args.steps):
+        O.sample_batch(xb, O.DTYPE_BF16, p, SOFTCAP, u[args.warmup + s], O.VARIANT_F32, O.TIE_HEAP, nthreads)
+    el = time.perf_counter() - t0
+    value = ROWS * args.steps / el
+    line = {
+        "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": el * 1e3 / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": "C3 full-vocab sampling, B=256 x V=262144 bf16, top_k=0, T=1, top_p=0.95, softcap 30",
+                   "global_batch": ROWS, "seq_len": VOCAB, "parallelism": "host threads"},
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": nthreads, "kind": "port",
+                         "sample": f"all {ROWS} rows per step, {args.steps} steps; C oracle port of "
+                                   "TModel.DoSample (the Delphi reference does not build here)"},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import numpy as np
+    import torch
+
+    import g4sampler as g4
+    import synth
+
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    K, W = args.steps, args.warmup
+    peak, peak_kind = load_peak()
+
+    # ---- inputs: 4 rotating sets of C3 rows (4 x 128 MiB > 126 MB L2) ----
+    base = synth.c3_logits(ROWS, step=rank)
+    sets = [torch.from_numpy(np.roll(base, k, axis=0).view(np.int16).copy()).to(dev) for k in range(4)]
+    u_all = torch.from_numpy(synth.uniforms(ROWS * (K + W), synth.SEEDS["c3"], 100 + rank)).to(dev).view(K + W, ROWS)
+    out = torch.empty(ROWS, dtype=torch.int32, device=dev)
+    s = g4.Sampler(local, ROWS, VOCAB, g4.FLAG_HOST_STAGING)
+    ext = torch.cuda.ExternalStream(s.stream, device=dev)
+    p = g4.make_params(1.0, 0, 0.95)
+
+    def step(i):
+        s.sample(sets[i % 4].data_ptr(), g4.BF16, ROWS, VOCAB, VOCAB, p, SOFTCAP, u_all[i].data_ptr(),
+                 out.data_ptr())
+
+    torch.cuda.synchronize()
+    for i in range(W):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = Clocks(local)
+    clocks.start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    torch.cuda.synchronize()
+    barrier(world)
+    for i in range(K):
+        ev[i][0].record(ext)
+        step(W + i)
+        ev[i][1].record(ext)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    total_ms = ev[0][0].elapsed_time(ev[-1][1])
+    launch_ms = [a.elapsed_time(b) for a, b in ev]
+    total_ms_max = allreduce_max(total_ms, world)
+    value = world * ROWS * K / (total_ms_max / 1e3)
+    mean_launch_s = statistics.mean(launch_ms) / 1e3
+    achieved = ROWS * BYTES_PER_ROW / mean_launch_s / 1e9
+    tokens_ok = bool(((out >= 0) & (out < VOCAB)).all().item())
+
+    # ---- latency at B=1 (config C1: fp32, top_k 64, top_p 0.95) ----
+    lat = None
+    if rank == 0:
+        c1 = torch.from_numpy(np.stack([synth.c1_logits(i) for i in range(64)])).to(dev)
+        u1 = torch.from_numpy(synth.uniforms(64, synth.SEEDS["c1"])).to(dev)
+        p1 = g4.make_params(1.0, 64, 0.95)
+        o1 = torch.empty(1, dtype=torch.int32, device=dev)
+        evl = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(200)]
+        for i in range(20):
+            s.sample(c1[i % 64].data_ptr(), g4.F32, 1, VOCAB, VOCAB, p1, SOFTCAP, u1[i % 64].data_ptr(), o1.data_ptr())
+        torch.cuda.synchronize()
+        for i in range(200):
+            evl[i][0].record(ext)
+            s.sample(c1[i % 64].data_ptr(), g4.F32, 1, VOCAB, VOCAB, p1, SOFTCAP, u1[i % 64].data_ptr(), o1.data_ptr())
+            evl[i][1].record(ext)
+            evl[i][1].synchronize()
+        lt = sorted(a.elapsed_time(b) * 1e3 for a, b in evl)
+        lat = {"p50_us": lt[len(lt) // 2], "p90_us": lt[int(len(lt) * 0.9)], "steps": 200,
+               "config": "C1: B=1 x V=262144 fp32, top_k 64, T=1, top_p 0.95 (device time per call)"}
+
+    # ---- end to end through g4s_sample_host (pinned host memory, PCIe inside) ----
+    e2e = None
+    if not args.no_e2e:
+        hb = torch.from_numpy(base.view(np.int16)).pin_memory()
+        hn = hb.numpy().view(np.uint16)
+        hu = synth.uniforms(ROWS, 7, rank)
+        htok = torch.empty(ROWS, dtype=torch.int32).pin_memory().numpy()
+        ke = max(3, min(K, 20))
+        for _ in range(2):
+            s.sample_host(hn, g4.BF16, p, SOFTCAP, hu, htok)
+        barrier(world)
+        t0 = time.perf_counter()
+        for _ in range(ke):
+            s.sample_host(hn, g4.BF16, p, SOFTCAP, hu, htok)
+        el = allreduce_max(time.perf_counter() - t0, world)
+        e2e = {"value": world * ROWS * ke / el, "unit": "rows/s",
+               "h2d_bytes_per_step": ROWS * BYTES_PER_ROW + ROWS * 8, "d2h_bytes_per_step": ROWS * 4,
+               "steps": ke, "timing": "host wall clock around synchronous g4s_sample_host calls"}
+
+    # ---- CPU baseline: the reference algorithm on host cores (rank 0, N=1) ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        nt = host_threads()
+        sample = base[:64]
+        rps, done, el = cpu_reference(sample, synth.uniforms(64, 3), nt)
+        cpu = {"value": rps, "unit": "rows/s", "cores": nt, "kind": "port",
+               "sample": f"{done} C3 rows ({64}-row sample repeated, {el:.1f} s wall on {nt} threads); "
+                         "C oracle port of TModel.DoSample, fp32 transcription"}
+
+    s.close()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": total_ms_max / K, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "C3 full-vocab sampling, B=256 x V=262144 bf16 per GPU, top_k=0, T=1, "
+                                   "top_p=0.95, softcap 30",
+                       "global_batch": ROWS * world, "seq_len": VOCAB,
+                       "parallelism": f"row-sharded x{world} (independent rows, no collective)",
+                       "l2": "4 rotating input sets of 128 MiB (512 MiB > 126 MB L2)"},
+            "hbm_frac_of_peak": achieved / peak,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": profiled_traffic(),
+                         "kernel": "full_chunk_kernel<bf16, 32>",
+                         "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
+                         "algorithmic_bytes_per_launch": ROWS * BYTES_PER_ROW,
+                         "mean_launch_us": mean_launch_s * 1e6},
+            "latency_b1": lat,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "gpu_launches": K,
+            "clocks": clk,
+            "tokens_in_range": tokens_ok,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,389 @@
+// g4s_topk.cu -- top-K path of the sampler (rows with 0 < top_k < vocab).
+//
+// Follows DoSample's top-K branch (src/Gemma4.Model.pas:2765-2826) with
+// DoSelectTopKIndices (src/Gemma4.Model.pas:2615-2689) replaced by an exact
+// parallel selection whose ties at the K-th place go to the lower vocab id.
+//
+// One CTA per (row, chunk of `chunk` ids):
+//   stage 1  the chunk is read once into registers (16-byte streaming loads),
+//            a lower bound t on the chunk's K-th largest key is taken from the
+//            per-thread maxima (each warp's ceil(K/8)-th largest thread max,
+//            minimum over the 8 warps: at least K elements lie at or above it),
+//            the elements >= t are compacted to shared memory, bitonic-sorted by
+//            (value desc, id asc) and the first K written to the workspace.
+//   stage 2  the last CTA of the row (atomic arrival counter) merges the
+//            per-chunk lists: with j = ceil(K / nch), the ceil(K/j)-th largest
+//            of the chunks' j-th entries is again a lower bound on the row's
+//            K-th largest; the entries above it are gathered, sorted, cut to K,
+//            re-sorted by id and handed to the tail.
+//   tail     one warp: softcap, temperature, max, exp, the reference's serial
+//            fp32 sum in ascending-id order, division, argmax, the serial
+//            cumulative draw -- the same fp32 operation sequence as the
+//            reference, so probabilities and tokens are bit-identical to the
+//            oracle's transcription.
+#include "g4s_device.cuh"
+#include "g4s_kernels.cuh"
+
+namespace g4s {
+
+struct TopkSmem {
+    uint64_t L[CAP2];
+    float tv[KMAX];
+    int32_t ids[KMAX];
+    uint32_t hist[256];
+    uint32_t wthr[NWARPS];
+    int scan[NWARPS + 1];
+    int misc[4];
+    float fmisc[2];
+};
+
+// Radix selection of the K-th largest 64-bit composite among the candidates a
+// visitor enumerates (8 passes of 8 bits; composites are unique, so the result
+// is exact).  for_each(fn) must call fn(composite) for each of this thread's
+// candidates.  Requires at least K candidates in total.
+template <class ForEach>
+__device__ uint64_t radix_kth(ForEach for_each, int K, TopkSmem &sm)
+{
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint64_t prefix = 0, mask = 0;
+    int rem = K;
+    for (int pass = 0; pass < 8; pass++) {
+        const int shift = 56 - 8 * pass;
+        for (int i = tid; i < 256; i += NTHREADS) sm.hist[i] = 0;
+        __syncthreads();
+        for_each([&](uint64_t c) {
+            if ((c & mask) == prefix) atomicAdd(&sm.hist[(c >> shift) & 255u], 1u);
+        });
+        __syncthreads();
+        if (warp == 0) {
+            // lane l owns bins 255-8l .. 248-8l (descending)
+            int cnt[8], s = 0;
+#pragma unroll
+            for (int r = 0; r < 8; r++) {
+                cnt[r] = (int)sm.hist[255 - 8 * lane - r];
+                s += cnt[r];
+            }
+            int inc = warp_incl_scan(s);
+            unsigned hit = __ballot_sync(FULLMASK, inc >= rem);
+            int L = __ffs(hit) - 1;
+            if (lane == L) {
+                int cum = inc - s;
+#pragma unroll
+                for (int r = 0; r < 8; r++) {
+                    if (cum + cnt[r] >= rem) {
+                        sm.misc[1] = 255 - 8 * lane - r;
+                        sm.misc[2] = cum;
+                        break;
+                    }
+                    cum += cnt[r];
+                }
+            }
+        }
+        __syncthreads();
+        const int d = sm.misc[1];
+        rem -= sm.misc[2];
+        prefix |= (uint64_t)d << shift;
+        mask |= 0xFFull << shift;
+        __syncthreads();
+    }
+    return prefix;
+}
+
+// The tail of the top-K path on kw survivors (sm.tv = raw logits, sm.ids =
+// vocab ids, ascending ids).  Runs on warp 0 only.
+__device__ void topk_tail(const SampleArgs &a, int row, const g4s_params &p, int kw,
+                          TopkSmem &sm)
+{
+    const int lane = threadIdx.x & 31;
+    int32_t flags = p.temperature > 0.0f ? 0 : G4S_ROW_GREEDY;
+    int32_t token = -1;
+    float tprob = 0.0f;
+    if (kw == 0) {
+        flags |= G4S_ROW_EMPTY;
+    } else {
+        const float cap = a.softcap;
+        const bool use_t = p.temperature > 0.0f && p.temperature != 1.0f;
+        const float invT = use_t ? __fdiv_rn(1.0f, p.temperature) : 1.0f;
+        // softcap cap * tanh(v / cap) and temperature (src/Gemma4.Model.pas:2768-2785)
+        for (int i = lane; i < kw; i += 32) {
+            float v = sm.tv[i];
+            if (cap > 0.0f) v = __fmul_rn(cap, g4_tanhf(__fdiv_rn(v, cap)));
+            if (use_t) v = __fmul_rn(v, invT);
+            sm.tv[i] = v;
+        }
+        __syncwarp();
+        // LMax := LVals[0]; strictly-greater scan (NaN at position 0 sticks)
+        float mx = -__uint_as_float(0x7f800000u);
+        for (int i = lane; i < kw; i += 32) mx = fmaxf(mx, sm.tv[i]);
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULLMASK, mx, d));
+        const float v0 = sm.tv[0];
+        if (v0 != v0) mx = v0;
+        for (int i = lane; i < kw; i += 32) sm.tv[i] = g4_expf(__fsub_rn(sm.tv[i], mx));
+        __syncwarp();
+        // serial fp32 sum in ascending-id order (src/Gemma4.Model.pas:2794-2799)
+        if (lane == 0) {
+            float s = 0.0f;
+            for (int i = 0; i < kw; i++) s = __fadd_rn(s, sm.tv[i]);
+            sm.fmisc[0] = s;
+        }
+        __syncwarp();
+        const float sum = sm.fmisc[0];
+        for (int i = lane; i < kw; i += 32) sm.tv[i] = __fdiv_rn(sm.tv[i], sum);
+        __syncwarp();
+        // argmax, first maximum wins (src/Gemma4.Model.pas:2803-2807)
+        float bv = -1.0f;
+        int bi = 0x7fffffff;
+        for (int i = lane; i < kw; i += 32) {
+            float q = sm.tv[i];
+            if (q > bv) { bv = q; bi = i; }
+        }
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) {
+            float ov = __shfl_xor_sync(FULLMASK, bv, d);
+            int oi = __shfl_xor_sync(FULLMASK, bi, d);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        int best = (sm.tv[0] != sm.tv[0] || bi == 0x7fffffff) ? 0 : bi;
+        // index-order cumulative draw against fl32(Random * TopP) (src/Gemma4.Model.pas:2809-2824)
+        if (p.temperature > 0.0f) {
+            if (lane == 0) {
+                const float thr = __double2float_rn(a.u[row] * (double)p.top_p);
+                float cum = 0.0f;
+                int found = -1;
+                for (int i = 0; i < kw; i++) {
+                    cum = __fadd_rn(cum, sm.tv[i]);
+                    if (cum >= thr) { found = i; break; }
+                }
+                sm.misc[3] = found;
+            }
+            __syncwarp();
+            const int found = sm.misc[3];
+            if (found >= 0) best = found;
+            else flags |= G4S_ROW_FALLBACK;
+        }
+        token = sm.ids[best];
+        tprob = sm.tv[best];
+    }
+    if (lane == 0) {
+        a.out_tokens[row] = token;
+        if (a.token_prob) a.token_prob[row] = tprob;
+        if (a.row_flags) a.row_flags[row] = flags;
+    }
+    if (a.cand_ids || a.cand_probs) {
+        for (int i = lane; i < a.cand_stride; i += 32) {
+            if (a.cand_ids) a.cand_ids[(int64_t)row * a.cand_stride + i] = i < kw ? sm.ids[i] : -1;
+            if (a.cand_probs) a.cand_probs[(int64_t)row * a.cand_stride + i] = i < kw ? sm.tv[i] : 0.0f;
+        }
+    }
+}
+
+// Sorts sm.L[0..n) descending (pads to a power of two with zeros).
+__device__ __forceinline__ void sort_list_desc(TopkSmem &sm, int n)
+{
+    const int P = next_pow2(n > 1 ? n : 1);
+    for (int i = n + threadIdx.x; i < P; i += NTHREADS) sm.L[i] = 0;
+    __syncthreads();
+    block_bitonic_desc(sm.L, P);
+}
+
+// Stage 2 of a row (last-arriving CTA): merge the per-chunk lists and sample.
+__device__ void topk_merge(const SampleArgs &a, int row, const g4s_params &p, TopkSmem &sm)
+{
+    const int K = p.top_k, nch = a.nch, tid = threadIdx.x;
+    const uint64_t *C = a.cand + (int64_t)row * nch * KMAX;
+    const int32_t *CC = a.cand_cnt + (int64_t)row * nch;
+    const int j = (K + nch - 1) / nch;
+    const int mm = (K + j - 1) / j;
+    // lower bound t2: the mm-th largest of the chunks' j-th entries
+    {
+        const int P = next_pow2(nch);
+        for (int c = tid; c < P; c += NTHREADS) {
+            uint64_t h = 0;
+            if (c < nch && __ldcg(&CC[c]) >= j) h = __ldcg(&C[(int64_t)c * KMAX + j - 1]);
+            sm.L[c] = h;
+        }
+        __syncthreads();
+        block_bitonic_desc(sm.L, P);
+    }
+    uint64_t t2 = sm.L[mm - 1];
+    if (t2 == 0) t2 = 1;  // every list entry is a valid candidate
+    __syncthreads();
+    const int slots = nch * K;
+    int cnt = 0;
+    for (int s = tid; s < slots; s += NTHREADS) {
+        const int c = s / K, i = s - c * K;
+        if (i < __ldcg(&CC[c]) && __ldcg(&C[(int64_t)c * KMAX + i]) >= t2) cnt++;
+    }
+    int total;
+    int off = block_excl_scan(cnt, &total, sm.scan);
+    int kw;
+    if (total <= CAP2) {
+        for (int s = tid; s < slots; s += NTHREADS) {
+            const int c = s / K, i = s - c * K;
+            if (i < __ldcg(&CC[c])) {
+                const uint64_t v = __ldcg(&C[(int64_t)c * KMAX + i]);
+                if (v >= t2) sm.L[off++] = v;
+            }
+        }
+        __syncthreads();
+        sort_list_desc(sm, total);
+        kw = total < K ? total : K;
+    } else {
+        // heavy ties: exact radix selection over all list entries
+        const uint64_t kth = radix_kth(
+            [&](auto fn) {
+                for (int s = tid; s < slots; s += NTHREADS) {
+                    const int c = s / K, i = s - c * K;
+                    if (i < __ldcg(&CC[c])) fn(__ldcg(&C[(int64_t)c * KMAX + i]));
+                }
+            },
+            K, sm);
+        int c2 = 0;
+        for (int s = tid; s < slots; s += NTHREADS) {
+            const int c = s / K, i = s - c * K;
+            if (i < __ldcg(&CC[c]) && __ldcg(&C[(int64_t)c * KMAX + i]) >= kth) c2++;
+        }
+        int tot2;
+        int o2 = block_excl_scan(c2, &tot2, sm.scan);
+        for (int s = tid; s < slots; s += NTHREADS) {
+            const int c = s / K, i = s - c * K;
+            if (i < __ldcg(&CC[c])) {
+                const uint64_t v = __ldcg(&C[(int64_t)c * KMAX + i]);
+                if (v >= kth) sm.L[o2++] = v;
+            }
+        }
+        __syncthreads();
+        sort_list_desc(sm, tot2);
+        kw = K;
+    }
+    // the kw winners, re-sorted by ascending vocab id: key (~id << 32 | key) descending
+    static_assert(KMAX <= NTHREADS, "one winner per thread");
+    __syncthreads();
+    const uint64_t mine = tid < kw ? sm.L[tid] : 0;
+    __syncthreads();
+    if (tid < kw) sm.L[tid] = ((uint64_t)comp_id(mine) ^ 0xffffffffull) << 32 | comp_key(mine);
+    __syncthreads();
+    sort_list_desc(sm, kw);
+    for (int i = tid; i < kw; i += NTHREADS) {
+        const uint64_t v = sm.L[i];
+        sm.ids[i] = (int32_t)(~(uint32_t)(v >> 32));
+        sm.tv[i] = key2f((uint32_t)v);
+    }
+    __syncthreads();
+    if (tid < 32) topk_tail(a, row, p, kw, sm);
+    if (tid == 0) a.counters_topk[row] = 0;  // ready for the next call
+}
+
+template <int DT, int EPT, bool VEC>
+__global__ void __launch_bounds__(NTHREADS) topk_chunk_kernel(SampleArgs a)
+{
+    __shared__ TopkSmem sm;
+    using T = DtypeTraits<DT>;
+    constexpr int VW = T::VW;
+    const int row = blockIdx.y, chunk = blockIdx.x, tid = threadIdx.x;
+    const g4s_params p = a.params.get(row);
+    const int K = p.top_k;
+    if (!(K > 0 && K < a.vocab && K <= KMAX)) return;
+    const int64_t c0 = (int64_t)chunk * a.chunk;
+    const int n = (int)min((int64_t)a.chunk, (int64_t)a.vocab - c0);
+    const void *rowp = (const char *)a.logits + (int64_t)row * a.row_stride * T::ESIZE;
+
+    float x[EPT];
+    load_chunk<DT, EPT, VEC>(rowp, c0, n, x);
+    uint32_t key[EPT];
+    uint32_t tmax = 0;
+#pragma unroll
+    for (int i = 0; i < EPT; i++) {
+        key[i] = cand_key(x[i]);
+        tmax = key[i] > tmax ? key[i] : tmax;
+    }
+    auto idof = [&](int i) -> uint32_t {
+        return (uint32_t)(c0 + (i / VW) * (NTHREADS * VW) + tid * VW + (i % VW));
+    };
+
+    // lower bound on the chunk's K-th largest key
+    const int lane = tid & 31, warp = tid >> 5;
+    const uint32_t srt = warp_sort_desc_u32(tmax);
+    const int kp = (K + NWARPS - 1) / NWARPS;
+    const uint32_t wthr = __shfl_sync(FULLMASK, srt, kp - 1);
+    if (lane == 0) sm.wthr[warp] = wthr;
+    __syncthreads();
+    uint32_t t = sm.wthr[0];
+#pragma unroll
+    for (int w = 1; w < NWARPS; w++) t = sm.wthr[w] < t ? sm.wthr[w] : t;
+    if (t == 0) t = 1;
+
+    int cnt = 0;
+#pragma unroll
+    for (int i = 0; i < EPT; i++) cnt += key[i] >= t;
+    int total;
+    int off = block_excl_scan(cnt, &total, sm.scan);
+    int m;
+    if (total <= CAP1) {
+#pragma unroll
+        for (int i = 0; i < EPT; i++)
+            if (key[i] >= t) sm.L[off++] = composite(key[i], idof(i));
+        __syncthreads();
+        sort_list_desc(sm, total);
+        m = total < K ? total : K;
+    } else {
+        const uint64_t kth = radix_kth(
+            [&](auto fn) {
+#pragma unroll
+                for (int i = 0; i < EPT; i++)
+                    if (key[i] >= 1) fn(composite(key[i], idof(i)));
+            },
+            K, sm);
+        int c2 = 0;
+#pragma unroll
+        for (int i = 0; i < EPT; i++) c2 += key[i] >= 1 && composite(key[i], idof(i)) >= kth;
+        int tot2;
+        int o2 = block_excl_scan(c2, &tot2, sm.scan);
+#pragma unroll
+        for (int i = 0; i < EPT; i++) {
+            if (key[i] >= 1) {
+                const uint64_t v = composite(key[i], idof(i));
+                if (v >= kth) sm.L[o2++] = v;
+            }
+        }
+        __syncthreads();
+        sort_list_desc(sm, tot2);
+        m = K;
+    }
+    uint64_t *out = a.cand + ((int64_t)row * a.nch + chunk) * KMAX;
+    for (int i = tid; i < m; i += NTHREADS) out[i] = sm.L[i];
+    if (tid == 0) a.cand_cnt[(int64_t)row * a.nch + chunk] = m;
+
+    // last-arriving CTA of the row merges (threadfence reduction pattern)
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) sm.misc[0] = atomicAdd(&a.counters_topk[row], 1u) == (unsigned)(a.nch - 1);
+    __syncthreads();
+    if (!sm.misc[0]) return;
+    __threadfence();
+    topk_merge(a, row, p, sm);
+}
+
+// ---------------------------------------------------------------------------
+// launcher
+// ---------------------------------------------------------------------------
+template <int DT, int EPT, bool VEC>
+static cudaError_t launch_topk_t(const SampleArgs &a, cudaStream_t s)
+{
+    dim3 grid(a.nch, a.rows);
+    topk_chunk_kernel<DT, EPT, VEC><<<grid, NTHREADS, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_topk(const SampleArgs &a, int ept, bool vec, cudaStream_t s)
+{
+    if (a.dtype == G4S_F32) {
+        if (ept == 8) return vec ? launch_topk_t<G4S_F32, 8, true>(a, s) : launch_topk_t<G4S_F32, 8, false>(a, s);
+        return vec ? launch_topk_t<G4S_F32, 32, true>(a, s) : launch_topk_t<G4S_F32, 32, false>(a, s);
+    }
+    if (ept == 8) return vec ? launch_topk_t<G4S_BF16, 8, true>(a, s) : launch_topk_t<G4S_BF16, 8, false>(a, s);
+    return vec ? launch_topk_t<G4S_BF16, 32, true>(a, s) : launch_topk_t<G4S_BF16, 32, false>(a, s);
+}
+
+}  // namespace g4s

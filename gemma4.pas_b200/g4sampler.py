@@ -1,0 +1,169 @@
+"""ctypes binding of libg4sampler.so, the C ABI declared in include/g4sampler.h.
+
+This is how the test suite and bench.py reach the CUDA sampler: exactly the
+calls an Object Pascal host makes through its `external 'libg4sampler.so'`
+declarations (pascal/G4Sampler.pas).  Device buffers are passed as raw
+pointers (for example torch tensors' data_ptr()).  There is no fallback: if
+the shared library is missing or no B200 is present, the calls fail loudly.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_char_p, c_double, c_float, c_int32, c_int64, c_uint32, c_void_p
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libg4sampler.so")
+
+F32, BF16 = 0, 1
+OK, ERR_ARG, ERR_CUDA, ERR_NOMEM, ERR_CAPACITY, ERR_NCCL, ERR_TIMEOUT, ERR_STATE, ERR_UNAVAILABLE = (
+    0, -1, -2, -3, -4, -5, -6, -7, -8)
+ROW_FALLBACK, ROW_EMPTY, ROW_FULL_PATH, ROW_GREEDY = 1, 2, 4, 8
+FLAG_HOST_STAGING = 1
+
+
+class Params(ctypes.Structure):
+    """TSamplingParams (src/Gemma4.Model.pas:70-76), 16 bytes."""
+
+    _fields_ = [("temperature", c_float), ("top_k", c_int32), ("top_p", c_float),
+                ("repetition_penalty", c_float)]
+
+    def __repr__(self):
+        return (f"Params(T={self.temperature}, K={self.top_k}, P={self.top_p}, "
+                f"rp={self.repetition_penalty})")
+
+
+class Outputs(ctypes.Structure):
+    _fields_ = [("token_prob", c_void_p), ("row_flags", c_void_p), ("cand_ids", c_void_p),
+                ("cand_probs", c_void_p), ("cand_stride", c_int32), ("reserved", c_int32),
+                ("full_probs", c_void_p)]
+
+
+# every entry point include/g4sampler.h declares, with (restype, argtypes)
+SIGNATURES = {
+    "g4s_version": (c_int32, []),
+    "g4s_params_defaults": (None, [POINTER(Params)]),
+    "g4s_create": (c_int32, [c_int32, c_int32, c_int32, c_uint32, POINTER(c_void_p)]),
+    "g4s_destroy": (c_int32, [c_void_p]),
+    "g4s_last_error": (c_char_p, [c_void_p]),
+    "g4s_stream": (c_void_p, [c_void_p]),
+    "g4s_workspace_bytes": (c_int64, [c_void_p]),
+    "g4s_sample": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int64, POINTER(Params),
+                             c_int32, c_float, c_void_p, c_void_p, c_void_p]),
+    "g4s_sample_ex": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int64,
+                                POINTER(Params), c_int32, c_float, c_void_p, c_void_p,
+                                POINTER(Outputs), c_void_p]),
+    "g4s_sample_host": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int64,
+                                  POINTER(Params), c_int32, c_float, c_void_p, c_void_p]),
+}
+
+_lib = None
+
+
+def load(path: str = LIB_PATH):
+    """Loads the shared library (once) and declares every signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise RuntimeError(f"{path} is not built: run `python -c 'import __graft_entry__ as g; g.build()'`")
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+class G4SError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"g4s error {code}: {msg}")
+        self.code = code
+
+
+def make_params(temperature=1.0, top_k=64, top_p=0.95, repetition_penalty=1.0) -> Params:
+    return Params(float(temperature), int(top_k), float(top_p), float(repetition_penalty))
+
+
+def params_array(rows):
+    """ctypes array of Params from a sequence of (T, K, P) or Params."""
+    arr = (Params * len(rows))()
+    for i, r in enumerate(rows):
+        arr[i] = r if isinstance(r, Params) else make_params(*r)
+    return arr
+
+
+class Sampler:
+    """RAII wrapper of one g4s_ctx."""
+
+    def __init__(self, device: int = 0, max_rows: int = 256, max_vocab: int = 262144, flags: int = 0):
+        self.lib = load()
+        h = c_void_p()
+        rc = self.lib.g4s_create(device, max_rows, max_vocab, flags, ctypes.byref(h))
+        if rc != OK:
+            raise G4SError(rc, self.lib.g4s_last_error(None).decode())
+        self.h = h
+        self.max_rows, self.max_vocab = max_rows, max_vocab
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.g4s_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def last_error(self) -> str:
+        return self.lib.g4s_last_error(self.h).decode()
+
+    @property
+    def stream(self) -> int:
+        return self.lib.g4s_stream(self.h) or 0
+
+    def _check(self, rc):
+        if rc != OK:
+            raise G4SError(rc, self.last_error())
+
+    def sample(self, logits_ptr: int, dtype: int, rows: int, vocab: int, row_stride: int, params,
+               softcap: float, u_ptr: int, out_ptr: int, stream: int | None = None,
+               outputs: Outputs | None = None, check: bool = True) -> int:
+        """g4s_sample_ex on device pointers.  params: one Params (broadcast) or a list."""
+        if isinstance(params, Params):
+            parr, pstride = (Params * 1)(params), 0
+        else:
+            parr, pstride = params_array(params), 1
+        rc = self.lib.g4s_sample_ex(self.h, c_void_p(logits_ptr), dtype, rows, vocab, row_stride,
+                                    parr, pstride, softcap, c_void_p(u_ptr), c_void_p(out_ptr),
+                                    ctypes.byref(outputs) if outputs is not None else None,
+                                    c_void_p(stream) if stream else None)
+        if check:
+            self._check(rc)
+        return rc
+
+    def sample_host(self, logits, dtype: int, params, softcap: float, u, tokens_out=None):
+        """g4s_sample_host on numpy arrays (logits [rows, row_stride] f32 or uint16 bf16 bits)."""
+        import numpy as np
+
+        rows, stride = logits.shape
+        vocab = stride
+        if isinstance(params, Params):
+            parr, pstride = (Params * 1)(params), 0
+        else:
+            parr, pstride = params_array(params), 1
+        out = tokens_out if tokens_out is not None else np.empty(rows, dtype=np.int32)
+        u = np.ascontiguousarray(u, dtype=np.float64)
+        rc = self.lib.g4s_sample_host(self.h, c_void_p(logits.ctypes.data), dtype, rows, vocab, stride,
+                                      parr, pstride, softcap, c_void_p(u.ctypes.data),
+                                      c_void_p(out.ctypes.data))
+        self._check(rc)
+        return out

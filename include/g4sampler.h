@@ -1,0 +1,164 @@
+/*
+ * g4sampler.h -- C ABI of the B200 token sampler for Gemma4.pas.
+ *
+ * The sampler replaces the reference's private sampling stage
+ *   function TModel.DoSample(const AParams: TSamplingParams): Integer
+ *   (src/Gemma4.Model.pas:277, 2739-2827)
+ * which TModel.Generate calls once per decode step (src/Gemma4.Model.pas:2889, 2923)
+ * on the host copy of the logits (FLogits, src/Gemma4.Model.pas:131, 1382-1385).
+ * Here the logits stay in device memory and one call samples a whole batch of
+ * rows on the GPU.  Semantics per row are exactly DoSample's:
+ *   - top_k <= 0 or top_k >= vocab: full-vocabulary path -- softcap
+ *     tanh(v * (1/cap)) * cap (src/Gemma4.Layers.pas:300-316), * (1/T) when
+ *     T > 0 and T != 1, softmax, argmax, then the INDEX-ORDER cumulative draw
+ *     against fl32(u * top_p) (src/Gemma4.Model.pas:2691-2737);
+ *   - otherwise the top-K path -- K largest raw logits (ties at the K-th place
+ *     go to the lower vocab id), softcap cap * tanh(v / cap) on the survivors,
+ *     * (1/T), softmax with a serial fp32 sum in ascending-id order, argmax,
+ *     index-order draw (src/Gemma4.Model.pas:2615-2689, 2765-2826);
+ *   - temperature <= 0: greedy (argmax, no draw);
+ *   - when the cumulative sum never reaches the threshold the argmax is kept.
+ *
+ * Conventions (mirroring the reference's error style, src/Gemma4.Model.pas:57-59:
+ * a status result plus a per-object error text, never an exception):
+ *   - every function returns an int32 status: G4S_OK (0) or a negative code;
+ *   - g4s_last_error(ctx) returns the text of the context's last failure;
+ *   - nothing throws across the ABI; a context is not thread-safe, distinct
+ *     contexts are independent;
+ *   - the context owns all device workspace, sized at g4s_create; sampling
+ *     calls allocate nothing.
+ */
+#ifndef G4SAMPLER_H
+#define G4SAMPLER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define G4S_ABI_VERSION 1
+
+/* Byte-compatible with TSamplingParams (src/Gemma4.Model.pas:70-76):
+   four 4-byte fields at offsets 0/4/8/12.  repetition_penalty is declared
+   and defaulted by the reference but never read (src/Gemma4.Model.pas:74, 351);
+   it is accepted and ignored here too. */
+typedef struct g4s_params {
+    float   temperature;
+    int32_t top_k;
+    float   top_p;
+    float   repetition_penalty;
+} g4s_params;
+
+typedef struct g4s_ctx g4s_ctx;
+
+enum g4s_status {
+    G4S_OK              = 0,
+    G4S_ERR_ARG         = -1,  /* invalid argument (null pointer, bad size...)  */
+    G4S_ERR_CUDA        = -2,  /* a CUDA runtime call failed                    */
+    G4S_ERR_NOMEM       = -3,  /* device or pinned allocation failed at create  */
+    G4S_ERR_CAPACITY    = -4,  /* rows / vocab above what the context was built for */
+    G4S_ERR_NCCL        = -5,  /* NCCL init or collective failed                */
+    G4S_ERR_TIMEOUT     = -6,  /* a bounded wait expired                        */
+    G4S_ERR_STATE       = -7,  /* call not valid in the context's state         */
+    G4S_ERR_UNAVAILABLE = -8   /* feature not built / no device                 */
+};
+
+enum g4s_dtype { G4S_F32 = 0, G4S_BF16 = 1 };
+
+/* g4s_create flags */
+#define G4S_FLAG_HOST_STAGING 1u  /* allocate the device staging of g4s_sample_host at
+                                     create time instead of on its first call */
+
+/* Row flags written to g4s_outputs.row_flags. */
+enum g4s_row_flag {
+    G4S_ROW_FALLBACK   = 1,  /* T > 0 but the cumsum never reached thr: argmax kept */
+    G4S_ROW_EMPTY      = 2,  /* top-K path with no logit above -1e30: token -1      */
+    G4S_ROW_FULL_PATH  = 4,  /* row took the full-vocabulary path                   */
+    G4S_ROW_GREEDY     = 8   /* T <= 0                                              */
+};
+
+/* Optional per-row outputs (all device pointers; any may be NULL). */
+typedef struct g4s_outputs {
+    float   *token_prob;   /* [rows] probability of the sampled token             */
+    int32_t *row_flags;    /* [rows] G4S_ROW_* bits                                */
+    int32_t *cand_ids;     /* [rows * cand_stride] top-K rows: survivor ids, ascending,
+                              padded with -1                                       */
+    float   *cand_probs;   /* [rows * cand_stride] their probabilities, 0-padded   */
+    int32_t  cand_stride;  /* >= largest top_k of the top-K rows when cand_* used  */
+    int32_t  reserved;
+    float   *full_probs;   /* [rows * vocab] full-path rows: every probability (a
+                              second pass; meant for verification)                 */
+} g4s_outputs;
+
+/* ABI version of the loaded library (G4S_ABI_VERSION). */
+int32_t g4s_version(void);
+
+/* TSamplingParams.SetDefaults (src/Gemma4.Model.pas:346-352): 1.0 / 64 / 0.95 / 1.0. */
+void g4s_params_defaults(g4s_params *p);
+
+/* Creates a sampler on CUDA device `device` able to take up to max_rows rows of
+   up to max_vocab logits per call.  flags: reserved, pass 0.
+   Replaces the sampler state TModel keeps implicitly (FLogits buffer and the
+   temporary arrays DoSample allocates per call, src/Gemma4.Model.pas:2740-2752). */
+int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t flags,
+                   g4s_ctx **out_ctx);
+
+/* Releases the context and its device memory.  NULL is accepted. */
+int32_t g4s_destroy(g4s_ctx *ctx);
+
+/* Text of the last failure on ctx (ctx == NULL: the last failure of
+   g4s_create on this thread).  Never NULL; "" when there was none.
+   Mirrors GetErrors() (src/vendor/StdApp/StdApp.Base.pas:212-230). */
+const char *g4s_last_error(const g4s_ctx *ctx);
+
+/* The context's CUDA stream (cudaStream_t), used when a call passes stream NULL. */
+void *g4s_stream(g4s_ctx *ctx);
+
+/* Device bytes the context holds. */
+int64_t g4s_workspace_bytes(const g4s_ctx *ctx);
+
+/*
+ * Samples `rows` rows of logits on the device, asynchronously on `stream`
+ * (cudaStream_t; NULL = the context stream).  Replaces TModel.DoSample
+ * (src/Gemma4.Model.pas:2739-2827) for a batch.
+ *   logits        device pointer, rows x row_stride elements of `dtype`
+ *                 (G4S_F32, or G4S_BF16 widened exactly as TBFloat16.ToSingle,
+ *                 src/Gemma4.Types.pas:417-424)
+ *   vocab         logits per row (FConfig.VocabSize)
+ *   row_stride    elements between row starts (>= vocab)
+ *   params        HOST pointer: params_stride == 0 -> params[0] for every row,
+ *                 else row r uses params[r] (params_stride must be 1)
+ *   softcap       FConfig.FinalLogitSoftcapping (<= 0 disables the softcap)
+ *   u             device pointer, one double in [0,1) per row: the value the
+ *                 reference draws with `Random` (src/Gemma4.Model.pas:2726, 2813)
+ *   out_tokens    device pointer, one int32 per row
+ */
+int32_t g4s_sample(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t rows,
+                   int32_t vocab, int64_t row_stride, const g4s_params *params,
+                   int32_t params_stride, float softcap, const double *u,
+                   int32_t *out_tokens, void *stream);
+
+/* g4s_sample plus the optional outputs in *extra (NULL = none). */
+int32_t g4s_sample_ex(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t rows,
+                      int32_t vocab, int64_t row_stride, const g4s_params *params,
+                      int32_t params_stride, float softcap, const double *u,
+                      int32_t *out_tokens, const g4s_outputs *extra, void *stream);
+
+/*
+ * Synchronous host-memory form, the literal drop-in for DoSample on FLogits:
+ * copies `rows` rows of host logits and the host draws to the device, samples,
+ * copies the tokens back to host memory and waits.  Pinned host buffers
+ * (cudaHostAlloc / cudaHostRegister) give full PCIe bandwidth; pageable
+ * memory works too.  Device staging is part of the context.
+ */
+int32_t g4s_sample_host(g4s_ctx *ctx, const void *host_logits, int32_t dtype, int32_t rows,
+                        int32_t vocab, int64_t row_stride, const g4s_params *params,
+                        int32_t params_stride, float softcap, const double *host_u,
+                        int32_t *host_tokens);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* G4SAMPLER_H */
