@@ -1,0 +1,94 @@
+unit G4Sampler;
+
+{ Object Pascal binding of libg4sampler.so -- the B200 token sampler that
+  replaces TModel.DoSample (src/Gemma4.Model.pas:2739-2827 of Gemma4.pas).
+
+  Mirrors include/g4sampler.h one to one: cdecl entry points, plain pointers
+  and sizes, Int32 status results (G4S_OK = 0, negative on error) and a
+  per-context error text (g4s_last_error), in the same spirit as the
+  reference's Boolean results plus GetErrors().
+
+  Targets Free Pascal ({$MODE DELPHI}) and Delphi for Linux64.  It does not
+  include StdApp.Defines.inc, which rejects non-Win64 targets
+  (src/vendor/StdApp/StdApp.Defines.inc:33-35). }
+
+{$IFDEF FPC}{$MODE DELPHI}{$ENDIF}
+
+interface
+
+const
+  G4SLib = 'libg4sampler.so';
+
+  G4S_ABI_VERSION = 1;
+
+  G4S_OK              = 0;
+  G4S_ERR_ARG         = -1;
+  G4S_ERR_CUDA        = -2;
+  G4S_ERR_NOMEM       = -3;
+  G4S_ERR_CAPACITY    = -4;
+  G4S_ERR_NCCL        = -5;
+  G4S_ERR_TIMEOUT     = -6;
+  G4S_ERR_STATE       = -7;
+  G4S_ERR_UNAVAILABLE = -8;
+
+  G4S_F32  = 0;
+  G4S_BF16 = 1;
+
+  G4S_FLAG_HOST_STAGING = 1;
+
+  G4S_ROW_FALLBACK  = 1;
+  G4S_ROW_EMPTY     = 2;
+  G4S_ROW_FULL_PATH = 4;
+  G4S_ROW_GREEDY    = 8;
+
+type
+  { Same layout as TSamplingParams (src/Gemma4.Model.pas:70-76): four 4-byte
+    fields at offsets 0/4/8/12, so a TSamplingParams can be passed by address. }
+  TG4SParams = record
+    Temperature: Single;
+    TopK: Int32;
+    TopP: Single;
+    RepetitionPenalty: Single;
+  end;
+  PG4SParams = ^TG4SParams;
+
+  TG4SOutputs = record
+    TokenProb: PSingle;
+    RowFlags: PInt32;
+    CandIds: PInt32;
+    CandProbs: PSingle;
+    CandStride: Int32;
+    Reserved: Int32;
+    FullProbs: PSingle;
+  end;
+  PG4SOutputs = ^TG4SOutputs;
+
+  PG4SCtx = Pointer;
+
+function g4s_version(): Int32; cdecl; external G4SLib;
+procedure g4s_params_defaults(P: PG4SParams); cdecl; external G4SLib;
+function g4s_create(Device, MaxRows, MaxVocab: Int32; Flags: UInt32;
+  out Ctx: PG4SCtx): Int32; cdecl; external G4SLib;
+function g4s_destroy(Ctx: PG4SCtx): Int32; cdecl; external G4SLib;
+function g4s_last_error(Ctx: PG4SCtx): PAnsiChar; cdecl; external G4SLib;
+function g4s_stream(Ctx: PG4SCtx): Pointer; cdecl; external G4SLib;
+function g4s_workspace_bytes(Ctx: PG4SCtx): Int64; cdecl; external G4SLib;
+
+{ Device-pointer form (logits, U and OutTokens in GPU memory; Params on the host). }
+function g4s_sample(Ctx: PG4SCtx; Logits: Pointer; DType, Rows, Vocab: Int32;
+  RowStride: Int64; Params: PG4SParams; ParamsStride: Int32; Softcap: Single;
+  U: PDouble; OutTokens: PInt32; Stream: Pointer): Int32; cdecl; external G4SLib;
+function g4s_sample_ex(Ctx: PG4SCtx; Logits: Pointer; DType, Rows, Vocab: Int32;
+  RowStride: Int64; Params: PG4SParams; ParamsStride: Int32; Softcap: Single;
+  U: PDouble; OutTokens: PInt32; Extra: PG4SOutputs;
+  Stream: Pointer): Int32; cdecl; external G4SLib;
+
+{ Host-memory form: the literal drop-in for DoSample on FLogits (synchronous). }
+function g4s_sample_host(Ctx: PG4SCtx; HostLogits: Pointer; DType, Rows,
+  Vocab: Int32; RowStride: Int64; Params: PG4SParams; ParamsStride: Int32;
+  Softcap: Single; HostU: PDouble; HostTokens: PInt32): Int32; cdecl;
+  external G4SLib;
+
+implementation
+
+end.
