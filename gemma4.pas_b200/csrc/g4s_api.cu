@@ -105,6 +105,13 @@ void g4s_params_defaults(g4s_params *p)
 
 const char *g4s_last_error(const g4s_ctx *ctx) { return ctx ? ctx->err.c_str() : g_create_err.c_str(); }
 
+// error text of the context-free entry point (g4s_noalloc.cu), read with g4s_last_error(NULL)
+int32_t g4s_noalloc_set_error(const char *msg)
+{
+    g_create_err = msg ? msg : "";
+    return 0;
+}
+
 void *g4s_stream(g4s_ctx *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
 
 int64_t g4s_workspace_bytes(const g4s_ctx *ctx) { return ctx ? (int64_t)ctx->ws_bytes : 0; }

@@ -55,6 +55,8 @@ SIGNATURES = {
                                 POINTER(Outputs), c_void_p]),
     "g4s_sample_host": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int64,
                                   POINTER(Params), c_int32, c_float, c_void_p, c_void_p]),
+    "g4s_sample_topk_noalloc": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_int64, POINTER(Params),
+                                          c_float, c_void_p, c_void_p, c_void_p]),
 }
 
 _lib = None

@@ -109,7 +109,8 @@ int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t
 int32_t g4s_destroy(g4s_ctx *ctx);
 
 /* Text of the last failure on ctx (ctx == NULL: the last failure of
-   g4s_create on this thread).  Never NULL; "" when there was none.
+   g4s_create or g4s_sample_topk_noalloc on this thread).  Never NULL; ""
+   when there was none.
    Mirrors GetErrors() (src/vendor/StdApp/StdApp.Base.pas:212-230). */
 const char *g4s_last_error(const g4s_ctx *ctx);
 
@@ -157,6 +158,32 @@ int32_t g4s_sample_host(g4s_ctx *ctx, const void *host_logits, int32_t dtype, in
                         int32_t vocab, int64_t row_stride, const g4s_params *params,
                         int32_t params_stride, float softcap, const double *host_u,
                         int32_t *host_tokens);
+
+/* Limits of g4s_sample_topk_noalloc (its static scratch is 2,101,504 bytes). */
+#define G4S_NOALLOC_MAX_ROWS  64
+#define G4S_NOALLOC_MAX_LISTS 1024 /* rows x chunks; a chunk is 2048 ids for small
+                                      batches, else 8192 (V=262144: up to 32 rows) */
+
+/*
+ * Top-K sampling that allocates nothing.  No counterpart in the reference:
+ * it exists for callers that cannot call cudaMalloc when they sample (a host
+ * that forbids allocations after start-up, a decode loop inside a memory pool
+ * it does not own, code that must avoid cudaMalloc/cudaFree's implicit
+ * synchronisation) and therefore cannot create a g4s_ctx.
+ * Same semantics as g4s_sample for rows on the top-K path; params[0] is used
+ * for every row and must have 1 <= top_k <= 256 and top_k < vocab.  logits, u
+ * and out_tokens are device pointers; stream NULL is the legacy default stream.
+ * Scratch comes from one fixed array inside the library (held on every GPU
+ * that loads it until exit).  The first call on a device, with that device
+ * current, looks up the array's device address (cudaGetSymbolAddress): make
+ * that first call before any stream capture.  All calls share the array, so
+ * calls that overlap on the GPU race; issue them one after another.
+ * Sizes above G4S_NOALLOC_MAX_ROWS rows or G4S_NOALLOC_MAX_LISTS lists return
+ * G4S_ERR_CAPACITY; errors are read with g4s_last_error(NULL).
+ */
+int32_t g4s_sample_topk_noalloc(const void *logits, int32_t dtype, int32_t rows, int32_t vocab,
+                                int64_t row_stride, const g4s_params *params, float softcap,
+                                const double *u, int32_t *out_tokens, void *stream);
 
 #ifdef __cplusplus
 }
