@@ -67,8 +67,8 @@ def load_peak():
 
 
 def profiled_traffic():
-    """DRAM bytes per launch of the full-path kernel from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "full_chunk_kernel_c3.md")
+    """DRAM bytes per launch of the full-path streaming kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "full_stream_kernel_c3.md")
     try:
         m = re.search(r"dram_bytes_per_launch:\s*([0-9]+)", open(path).read())
         return int(m.group(1)) if m else None
@@ -238,57 +238,80 @@ def main():
     u_all = torch.from_numpy(synth.uniforms(ROWS * (K + W), synth.SEEDS["c3"], 100 + rank)).to(dev).view(K + W, ROWS)
     out = torch.empty(ROWS, dtype=torch.int32, device=dev)
     s = g4.Sampler(local, ROWS, VOCAB, g4.FLAG_HOST_STAGING)
-    ext = torch.cuda.ExternalStream(s.stream, device=dev)
     p = g4.make_params(1.0, 0, 0.95)
 
-    def step(i):
+    def step(i, stream=None):
         s.sample(sets[i % 4].data_ptr(), g4.BF16, ROWS, VOCAB, VOCAB, p, SOFTCAP, u_all[i].data_ptr(),
-                 out.data_ptr())
+                 out.data_ptr(), stream=stream)
 
     torch.cuda.synchronize()
     for i in range(W):
         step(i)
     torch.cuda.synchronize()
+    # The K timed steps are captured in one CUDA graph and replayed: a Python
+    # loop of ctypes calls cannot enqueue a ~25 us step as fast as the GPU runs
+    # it, and per-call events would time the host.  The graph is replayed once
+    # untimed (upload), then once timed.
+    cap = torch.cuda.Stream(device=dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=cap):
+        for i in range(K):
+            step(W + i, stream=cap.cuda_stream)
+    graph.replay()
+    torch.cuda.synchronize()
     barrier(world)
     clocks = Clocks(local)
     clocks.start()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     barrier(world)
-    for i in range(K):
-        ev[i][0].record(ext)
-        step(W + i)
-        ev[i][1].record(ext)
+    t0.record()
+    graph.replay()
+    t1.record()
     torch.cuda.synchronize()
     barrier(world)
     clk = clocks.stop()
-    total_ms = ev[0][0].elapsed_time(ev[-1][1])
-    launch_ms = [a.elapsed_time(b) for a, b in ev]
+    total_ms = t0.elapsed_time(t1)
     total_ms_max = allreduce_max(total_ms, world)
     value = world * ROWS * K / (total_ms_max / 1e3)
-    mean_launch_s = statistics.mean(launch_ms) / 1e3
+    mean_launch_s = total_ms / K / 1e3
     achieved = ROWS * BYTES_PER_ROW / mean_launch_s / 1e9
     tokens_ok = bool(((out >= 0) & (out < VOCAB)).all().item())
+    del graph
 
     # ---- latency at B=1 (config C1: fp32, top_k 64, top_p 0.95) ----
+    # one call per CUDA graph (8 graphs over 8 rows, as a decode loop would
+    # replay it), device time of each replay
     lat = None
     if rank == 0:
-        c1 = torch.from_numpy(np.stack([synth.c1_logits(i) for i in range(64)])).to(dev)
-        u1 = torch.from_numpy(synth.uniforms(64, synth.SEEDS["c1"])).to(dev)
+        c1 = torch.from_numpy(np.stack([synth.c1_logits(i) for i in range(8)])).to(dev)
+        u1 = torch.from_numpy(synth.uniforms(8, synth.SEEDS["c1"])).to(dev)
         p1 = g4.make_params(1.0, 64, 0.95)
         o1 = torch.empty(1, dtype=torch.int32, device=dev)
-        evl = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(200)]
-        for i in range(20):
-            s.sample(c1[i % 64].data_ptr(), g4.F32, 1, VOCAB, VOCAB, p1, SOFTCAP, u1[i % 64].data_ptr(), o1.data_ptr())
+        for i in range(5):
+            s.sample(c1[i % 8].data_ptr(), g4.F32, 1, VOCAB, VOCAB, p1, SOFTCAP, u1[i % 8].data_ptr(), o1.data_ptr())
         torch.cuda.synchronize()
+        graphs = []
+        for i in range(8):
+            gi = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gi, stream=cap):
+                s.sample(c1[i].data_ptr(), g4.F32, 1, VOCAB, VOCAB, p1, SOFTCAP, u1[i].data_ptr(), o1.data_ptr(),
+                         stream=cap.cuda_stream)
+            graphs.append(gi)
+        for gi in graphs:
+            gi.replay()
+        torch.cuda.synchronize()
+        evl = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(200)]
         for i in range(200):
-            evl[i][0].record(ext)
-            s.sample(c1[i % 64].data_ptr(), g4.F32, 1, VOCAB, VOCAB, p1, SOFTCAP, u1[i % 64].data_ptr(), o1.data_ptr())
-            evl[i][1].record(ext)
+            evl[i][0].record()
+            graphs[i % 8].replay()
+            evl[i][1].record()
             evl[i][1].synchronize()
         lt = sorted(a.elapsed_time(b) * 1e3 for a, b in evl)
         lat = {"p50_us": lt[len(lt) // 2], "p90_us": lt[int(len(lt) * 0.9)], "steps": 200,
-               "config": "C1: B=1 x V=262144 fp32, top_k 64, T=1, top_p 0.95 (device time per call)"}
+               "config": "C1: B=1 x V=262144 fp32, top_k 64, T=1, top_p 0.95; device time of one "
+                         "CUDA-graph replay of one g4s_sample call"}
+        del graphs
 
     # ---- end to end through g4s_sample_host (pinned host memory, PCIe inside) ----
     e2e = None
@@ -329,18 +352,20 @@ def main():
                                    "top_p=0.95, softcap 30",
                        "global_batch": ROWS * world, "seq_len": VOCAB,
                        "parallelism": f"row-sharded x{world} (independent rows, no collective)",
-                       "l2": "4 rotating input sets of 128 MiB (512 MiB > 126 MB L2)"},
+                       "l2": "4 rotating input sets of 128 MiB (512 MiB > 126 MB L2)",
+                       "timing": "K steps captured in one CUDA graph; one untimed replay, then one "
+                                 "replay timed with CUDA events"},
             "hbm_frac_of_peak": achieved / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": profiled_traffic(),
-                         "kernel": "full_chunk_kernel<bf16, 32>",
+                         "kernel": "full_stream_kernel<bf16> (+ full_combine_kernel in the timed call)",
                          "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                          "algorithmic_bytes_per_launch": ROWS * BYTES_PER_ROW,
-                         "mean_launch_us": mean_launch_s * 1e6},
+                         "mean_step_us": mean_launch_s * 1e6},
             "latency_b1": lat,
             "e2e": e2e,
             "cpu_baseline": cpu,
-            "gpu_launches": K,
+            "gpu_launches": 2 * K,
             "clocks": clk,
             "tokens_in_range": tokens_ok,
         }

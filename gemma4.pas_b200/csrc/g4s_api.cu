@@ -29,12 +29,11 @@ struct g4s_ctx {
     void *ws = nullptr;
     size_t ws_bytes = 0;
     int64_t lists_cap = 0;  // per-chunk candidate lists available
-    int64_t stats_cap = 0;  // per-chunk statistics available
     uint64_t *cand = nullptr;
     int32_t *cand_cnt = nullptr;
     uint32_t *counters_topk = nullptr;
-    uint32_t *counters_full = nullptr;
-    ChunkStat *stats = nullptr;
+    float4 *istat = nullptr;
+    int persist[2][2] = {{0, 0}, {0, 0}};  // full-path streaming CTAs per SM [dtype][vec]
     RowStat *rowstat = nullptr;
     int32_t *lk_idx = nullptr;
     float *lk_val = nullptr;
@@ -175,19 +174,18 @@ int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t
     int64_t lists = (int64_t)max_rows * nch_big;
     if (nch_small <= NCH_MAX_ && small_rows * nch_small > lists) lists = small_rows * nch_small;
     ctx->lists_cap = lists;
-    ctx->stats_cap = lists;
 
     auto align = [](size_t x) { return (x + 255u) & ~(size_t)255u; };
     size_t off = 0;
     const size_t o_cand = off; off = align(off + (size_t)lists * KMAX_ * sizeof(uint64_t));
     const size_t o_cnt = off; off = align(off + (size_t)lists * sizeof(int32_t));
     const size_t o_ct = off; off = align(off + (size_t)max_rows * sizeof(uint32_t));
-    const size_t o_cf = off; off = align(off + (size_t)max_rows * sizeof(uint32_t));
-    const size_t o_st = off; off = align(off + (size_t)lists * sizeof(ChunkStat));
+    const int64_t items = (int64_t)max_rows * ceil_div(max_vocab, 1024);  // items of >= 1024 logits
+    const size_t o_st = off; off = align(off + (size_t)items * sizeof(float4));
     const size_t o_rs = off; off = align(off + (size_t)max_rows * sizeof(RowStat));
     const size_t o_li = off; off = align(off + (size_t)LK_SLOTS * max_vocab * sizeof(int32_t));
     const size_t o_lv = off; off = align(off + (size_t)LK_SLOTS * max_vocab * sizeof(float));
-    const size_t o_pd = off; off = align(off + (size_t)max_rows * sizeof(g4s_params));
+    const size_t o_pd = off; off = align(off + (size_t)max_rows * (sizeof(g4s_params) + sizeof(float)));
     ctx->ws_bytes = off;
     if (cudaMalloc(&ctx->ws, off) != cudaSuccess) {
         cudaGetLastError();
@@ -198,15 +196,14 @@ int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t
     ctx->cand = (uint64_t *)(base + o_cand);
     ctx->cand_cnt = (int32_t *)(base + o_cnt);
     ctx->counters_topk = (uint32_t *)(base + o_ct);
-    ctx->counters_full = (uint32_t *)(base + o_cf);
-    ctx->stats = (ChunkStat *)(base + o_st);
+    ctx->istat = (float4 *)(base + o_st);
     ctx->rowstat = (RowStat *)(base + o_rs);
     ctx->lk_idx = (int32_t *)(base + o_li);
     ctx->lk_val = (float *)(base + o_lv);
     ctx->params_dev = (g4s_params *)(base + o_pd);
     if (cudaMemset(ctx->ws, 0, off) != cudaSuccess ||
         cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaHostAlloc((void **)&ctx->params_pinned, (size_t)max_rows * sizeof(g4s_params),
+        cudaHostAlloc((void **)&ctx->params_pinned, (size_t)max_rows * (sizeof(g4s_params) + sizeof(float)),
                       cudaHostAllocDefault) != cudaSuccess ||
         cudaEventCreateWithFlags(&ctx->params_ev, cudaEventDisableTiming) != cudaSuccess) {
         cudaGetLastError();
@@ -303,6 +300,7 @@ int32_t g4s_sample_ex(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t r
     a.nch = nch;
     a.lk_slots = LK_SLOTS;
     a.softcap = softcap;
+    a.invcap = softcap > 0.0f ? 1.0f / softcap : 0.0f;
     a.u = u;
     a.out_tokens = out_tokens;
     a.token_prob = ex.token_prob;
@@ -314,8 +312,12 @@ int32_t g4s_sample_ex(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t r
     a.cand = ctx->cand;
     a.cand_cnt = ctx->cand_cnt;
     a.counters_topk = ctx->counters_topk;
-    a.counters_full = ctx->counters_full;
-    a.stats = ctx->stats;
+    a.istat = ctx->istat;
+    if (any_full) {
+        int &bps = ctx->persist[dtype][vec ? 1 : 0];
+        if (bps == 0) bps = full_stream_blocks_per_sm(dtype, vec);
+        a.persist_blocks = bps * ctx->sm_count;
+    }
     a.rowstat = ctx->rowstat;
     a.lk_idx = ctx->lk_idx;
     a.lk_val = ctx->lk_val;
@@ -324,7 +326,12 @@ int32_t g4s_sample_ex(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t r
         if (ctx->params_ev_pending && cudaEventSynchronize(ctx->params_ev) != cudaSuccess)
             return fail(ctx, G4S_ERR_CUDA, "g4s_sample: waiting on the previous params copy failed");
         memcpy(ctx->params_pinned, params, (size_t)rows * sizeof(g4s_params));
-        if (cudaMemcpyAsync(ctx->params_dev, ctx->params_pinned, (size_t)rows * sizeof(g4s_params),
+        float *inv_t = (float *)(ctx->params_pinned + rows);
+        for (int r = 0; r < rows; r++) {
+            const float T = params[r].temperature;
+            inv_t[r] = (T > 0.0f && T != 1.0f) ? 1.0f / T : 1.0f;  // IEEE division, as on the device
+        }
+        if (cudaMemcpyAsync(ctx->params_dev, ctx->params_pinned, (size_t)rows * (sizeof(g4s_params) + sizeof(float)),
                             cudaMemcpyHostToDevice, s) != cudaSuccess ||
             cudaEventRecord(ctx->params_ev, s) != cudaSuccess) {
             cudaError_t e = cudaGetLastError();
@@ -332,9 +339,12 @@ int32_t g4s_sample_ex(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t r
         }
         ctx->params_ev_pending = true;
         a.params.dev = ctx->params_dev;
+        a.params.inv_t_dev = (const float *)(ctx->params_dev + rows);
     } else {
         a.params.dev = nullptr;
         a.params.p0 = params[0];
+        const float T = params[0].temperature;
+        a.params.inv_t0 = (T > 0.0f && T != 1.0f) ? 1.0f / T : 1.0f;
     }
 
     cudaError_t e = cudaSuccess;

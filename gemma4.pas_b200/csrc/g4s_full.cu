@@ -1,36 +1,54 @@
 // g4s_full.cu -- full-vocabulary path of the sampler (rows with top_k <= 0 or
 // top_k >= vocab): CpuLogitSoftcap (src/Gemma4.Layers.pas:300-316) and
 // DoSampleTopP (src/Gemma4.Model.pas:2691-2737) with CpuSoftmaxF32
-// (src/Gemma4.Tensors.pas:638-674), in one streaming pass over the logits.
+// (src/Gemma4.Tensors.pas:638-674) as one streaming pass plus a per-row combine.
 //
-// Per (row, chunk) CTA: the chunk is read once (16-byte streaming loads) and
-// every logit is softcapped (tanh(v * (1/cap)) * cap, bit-identical to the
-// oracle) and tempered in registers.  The CTA reduces the chunk maximum m and
-// its lowest id, then sums e = 2^(s * log2e - cc), cc = fl32(m * log2e), one
-// FMA and one ex2 per logit, into sums over consecutive 32*VW-id ranges.
+// full_stream_kernel: persistent, independent warps (no block barriers, no
+//   fences).  A warp item is 4 KiB of one row (2048 bf16 or 1024 fp32 logits);
+//   each lane copies its own eight 16-byte vectors of the next item into a
+//   per-warp two-stage shared-memory ring with cp.async while the current item
+//   is processed in two passes over the ring:
+//     1. NaN-propagating min/max of the raw logits (packed bf16x2 or 3-input
+//        fp32 min/max), reduced over the warp.  With no NaN and every
+//        q = v * (1/cap) in [-1, 1] (decided from the two extremes: fl32(v * c)
+//        is monotone in v) the item maximum is s(max v), softcap and
+//        temperature being monotone;
+//     2. each pair of logits: softcap (packed fp32 polynomial) -> temperature ->
+//        e = 2^(s * log2e - cc), cc = fl32(m * log2e) -> packed accumulate.
+//   Items with a NaN, an |q| > 1 or a ragged end take an out-of-line general
+//   path (per element g4_tanhf, NaN -> -inf) that rereads the item.  Each item
+//   writes (m, cc, S): 16 bytes per 4 KiB read.
+// full_combine_kernel: one warp per row.  M = max of the item maxima; item
+//   weights 2^(cc - M * log2e); the index-order prefix of the weighted item sums
+//   locates the item whose mass crosses fl32(u * top_p) * S, and that one item
+//   is rescanned element by element with the identical per-element arithmetic
+//   to pick the first id whose cumulative sum reaches the threshold.  Greedy
+//   rows and the argmax fallback rescan the first item holding M.
 //
-// The last CTA of the row (atomic arrival counter) combines the chunk sums in
-// double with weights 2^(cc - M * log2e), finds the chunk and then the
-// sub-range whose cumulative mass crosses fl32(u * top_p) * S, and rescans that
-// one range (32 * VW ids, L2-resident) to pick the first id whose cumulative
-// sum reaches the threshold -- the reference's index-order draw.  The
-// reference's serial fp32 sums drift by ~1e-4 over 262144 terms; this path
-// matches the fp64 restatement of the reference instead.
+// The reference's serial fp32 sums drift by ~3e-4 over 262144 terms; this path
+// matches the fp64 restatement of the reference (same fp32 per-element values,
+// exact combination) instead.
 #include "g4s_device.cuh"
 #include "g4s_kernels.cuh"
 
 namespace g4s {
 
-struct FullSmem {
-    double w[NCH_MAX];
-    double pref[NCH_MAX];
-    float sub[64];
-    float redv[NWARPS];
-    int redi[NWARPS];
-    double dscan[NWARPS + 1];
-    int misc[8];
-    double dmisc[4];
+constexpr int STREAM_THREADS = 128;  // CTA size of the persistent streaming kernel
+constexpr int NVEC = 8;              // 16-byte vectors per lane per item
+
+// Item geometry: 32 lanes x NVEC vectors x VW logits = 4 KiB.
+template <int DT>
+struct Geo {
+    static constexpr int VW = DtypeTraits<DT>::VW;
+    static constexpr int ITEM = 32 * NVEC * VW;  // 2048 (bf16) or 1024 (fp32)
 };
+
+// Item position of lane-local element (j, k): vector j, component k.
+template <int DT>
+__device__ __forceinline__ int item_pos(int j, int k, int lane)
+{
+    return (j * 32 + lane) * Geo<DT>::VW + k;
+}
 
 struct SParams {
     bool use_cap;
@@ -38,14 +56,16 @@ struct SParams {
     float cap, invcap, invT;
 };
 
-__device__ __forceinline__ SParams make_sparams(float softcap, const g4s_params &p)
+// Softcap/temperature constants of a row: fl32(1/cap) and fl32(1/T) come from the
+// host (the same IEEE division), so no kernel divides per item.
+__device__ __forceinline__ SParams make_sparams(const SampleArgs &a, const g4s_params &p, int row)
 {
     SParams sp;
-    sp.use_cap = softcap > 0.0f;
-    sp.cap = softcap;
-    sp.invcap = sp.use_cap ? __fdiv_rn(1.0f, softcap) : 0.0f;
+    sp.use_cap = a.softcap > 0.0f;
+    sp.cap = a.softcap;
+    sp.invcap = a.invcap;
     sp.use_t = p.temperature > 0.0f && p.temperature != 1.0f;
-    sp.invT = sp.use_t ? __fdiv_rn(1.0f, p.temperature) : 1.0f;
+    sp.invT = sp.use_t ? a.params.inv_t(row) : 1.0f;
     return sp;
 }
 
@@ -59,259 +79,502 @@ __device__ __forceinline__ float s_of(float x, const SParams &sp)
     return s;
 }
 
-// EPT logits in registers -> softcapped/tempered values, paired fp32 math.
-// Lane-for-lane identical to s_of.
-template <int EPT>
-__device__ __forceinline__ void s_of_vec(float *x, const SParams &sp)
+__device__ __forceinline__ float fmax_nan(float a, float b)
 {
-    static_assert(EPT % 2 == 0, "pairs");
-#pragma unroll
-    for (int i = 0; i < EPT; i++)
-        if (x[i] != x[i]) x[i] = -__uint_as_float(0x7f800000u);
-    if (sp.use_cap) {
-        const float2 ic = make_float2(sp.invcap, sp.invcap);
-        bool small = true;
-#pragma unroll
-        for (int i = 0; i < EPT; i += 2) {
-            float2 q = __fmul2_rn(make_float2(x[i], x[i + 1]), ic);
-            x[i] = q.x;
-            x[i + 1] = q.y;
-            small = small && fabsf(q.x) <= 1.0f && fabsf(q.y) <= 1.0f;
-        }
-        if (small) {
-#pragma unroll
-            for (int i = 0; i < EPT; i += 2) {
-                float2 t = tanh_poly2(make_float2(x[i], x[i + 1]));
-                x[i] = t.x;
-                x[i + 1] = t.y;
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < EPT; i++) x[i] = g4_tanhf(x[i]);
-        }
-        const float2 c2 = make_float2(sp.cap, sp.cap);
-#pragma unroll
-        for (int i = 0; i < EPT; i += 2) {
-            float2 s = __fmul2_rn(make_float2(x[i], x[i + 1]), c2);
-            x[i] = s.x;
-            x[i + 1] = s.y;
-        }
-    }
-    if (sp.use_t) {
-        const float2 t2 = make_float2(sp.invT, sp.invT);
-#pragma unroll
-        for (int i = 0; i < EPT; i += 2) {
-            float2 s = __fmul2_rn(make_float2(x[i], x[i + 1]), t2);
-            x[i] = s.x;
-            x[i + 1] = s.y;
-        }
-    }
-}
-
-__device__ __forceinline__ float warp_sum_f(float v)
-{
-#pragma unroll
-    for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(FULLMASK, v, d);
-    return v;
-}
-
-__device__ __forceinline__ double warp_incl_scan_d(double v)
-{
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-        double o = __shfl_up_sync(FULLMASK, v, d);
-        if (lane >= d) v += o;
-    }
-    return v;
-}
-
-__device__ __forceinline__ double block_excl_scan_d(double v, double *total, double *sh)
-{
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    double inc = warp_incl_scan_d(v);
-    if (lane == 31) sh[w] = inc;
-    __syncthreads();
-    if (w == 0) {
-        double s = lane < NWARPS ? sh[lane] : 0.0;
-        double si = warp_incl_scan_d(s);
-        if (lane < NWARPS) sh[lane] = si - s;
-        if (lane == NWARPS - 1) sh[NWARPS] = si;
-    }
-    __syncthreads();
-    double r = sh[w] + (inc - v);
-    *total = sh[NWARPS];
-    __syncthreads();
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
     return r;
 }
-
-// (max, lowest id) over the block; result broadcast to all threads.
-__device__ __forceinline__ void block_argmax(float &v, int &i, FullSmem &sm)
+__device__ __forceinline__ float fmin_nan(float a, float b)
 {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    float r;
+    asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ float fmax3_nan(float a, float b, float c)
+{
+    float r;
+    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+__device__ __forceinline__ float fmin3_nan(float a, float b, float c)
+{
+    float r;
+    asm("min.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+__device__ __forceinline__ uint32_t bmax2_nan(uint32_t a, uint32_t b)
+{
+    uint32_t r;
+    asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+__device__ __forceinline__ uint32_t bmin2_nan(uint32_t a, uint32_t b)
+{
+    uint32_t r;
+    asm("min.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+__device__ __forceinline__ float warp_max_nan(float v)
+{
 #pragma unroll
-    for (int d = 16; d > 0; d >>= 1) {
-        float ov = __shfl_xor_sync(FULLMASK, v, d);
-        int oi = __shfl_xor_sync(FULLMASK, i, d);
-        if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
-    }
-    if (lane == 0) { sm.redv[w] = v; sm.redi[w] = i; }
-    __syncthreads();
-    if (w == 0) {
-        v = lane < NWARPS ? sm.redv[lane] : -__uint_as_float(0x7f800000u);
-        i = lane < NWARPS ? sm.redi[lane] : 0x7fffffff;
+    for (int d = 16; d > 0; d >>= 1) v = fmax_nan(v, __shfl_xor_sync(FULLMASK, v, d));
+    return v;
+}
+__device__ __forceinline__ float warp_min_nan(float v)
+{
 #pragma unroll
-        for (int d = 16; d > 0; d >>= 1) {
-            float ov = __shfl_xor_sync(FULLMASK, v, d);
-            int oi = __shfl_xor_sync(FULLMASK, i, d);
-            if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
-        }
-        if (lane == 0) { sm.redv[0] = v; sm.redi[0] = i; }
-    }
-    __syncthreads();
-    v = sm.redv[0];
-    i = sm.redi[0];
-    __syncthreads();
+    for (int d = 16; d > 0; d >>= 1) v = fmin_nan(v, __shfl_xor_sync(FULLMASK, v, d));
+    return v;
 }
 
-// The row combine and draw (last CTA of the row).
-template <int DT, int EPT>
-__device__ void full_combine(const SampleArgs &a, int row, const g4s_params &p,
-                             const SParams &sp, FullSmem &sm)
+// Item `sub` of a row holds n = min(ITEM, vocab - sub * ITEM) logits.
+template <int DT>
+__device__ __forceinline__ int item_len(int vocab, int sub)
+{
+    return min(Geo<DT>::ITEM, vocab - sub * Geo<DT>::ITEM);
+}
+
+template <int DT>
+__device__ __forceinline__ float load_elem(const void *rowp, int64_t i)
+{
+    return DtypeTraits<DT>::load1(rowp, i);
+}
+
+// Pass 1: warp-uniform fast-path decision and the raw item maximum.  vec(j)
+// returns this lane's vector j.
+template <int DT, class Vec>
+__device__ __forceinline__ bool item_fast(Vec vec, const SParams &sp, float &xmax)
+{
+    float mn, mx;
+    if constexpr (DT == G4S_BF16) {
+        uint4 v = vec(0);
+        uint32_t a = bmax2_nan(bmax2_nan(v.x, v.y), bmax2_nan(v.z, v.w));
+        uint32_t b = bmin2_nan(bmin2_nan(v.x, v.y), bmin2_nan(v.z, v.w));
+#pragma unroll
+        for (int j = 1; j < NVEC; j++) {
+            v = vec(j);
+            a = bmax2_nan(a, bmax2_nan(bmax2_nan(v.x, v.y), bmax2_nan(v.z, v.w)));
+            b = bmin2_nan(b, bmin2_nan(bmin2_nan(v.x, v.y), bmin2_nan(v.z, v.w)));
+        }
+        mx = fmax_nan(__uint_as_float(a << 16), __uint_as_float(a & 0xffff0000u));
+        mn = fmin_nan(__uint_as_float(b << 16), __uint_as_float(b & 0xffff0000u));
+    } else {
+        uint4 v = vec(0);
+        float a = fmax3_nan(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z));
+        float b = fmin3_nan(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z));
+        a = fmax_nan(a, __uint_as_float(v.w));
+        b = fmin_nan(b, __uint_as_float(v.w));
+#pragma unroll
+        for (int j = 1; j < NVEC; j++) {
+            v = vec(j);
+            a = fmax3_nan(a, __uint_as_float(v.x), __uint_as_float(v.y));
+            a = fmax3_nan(a, __uint_as_float(v.z), __uint_as_float(v.w));
+            b = fmin3_nan(b, __uint_as_float(v.x), __uint_as_float(v.y));
+            b = fmin3_nan(b, __uint_as_float(v.z), __uint_as_float(v.w));
+        }
+        mx = a;
+        mn = b;
+    }
+    mx = warp_max_nan(mx);
+    mn = warp_min_nan(mn);
+    xmax = mx;
+    if (mx != mx || mn != mn) return false;  // NaN present
+    if (!sp.use_cap) return true;
+    return fabsf(__fmul_rn(mx, sp.invcap)) <= 1.0f && fabsf(__fmul_rn(mn, sp.invcap)) <= 1.0f;
+}
+
+// Pass 2 of the fast path: each pair of logits goes softcap -> temperature ->
+// exponent -> accumulate.  Returns the lane's sum of e.
+template <int DT, bool CAP, bool TEMP, class Vec>
+__device__ __forceinline__ float fast_exp_sum(Vec vec, const SParams &sp, float cc)
+{
+    constexpr int VW = Geo<DT>::VW;
+    const float2 ic = make_float2(sp.invcap, sp.invcap), c2 = make_float2(sp.cap, sp.cap);
+    const float2 t2 = make_float2(sp.invT, sp.invT);
+    const float2 l2 = make_float2(G4_L2E, G4_L2E), nc = make_float2(-cc, -cc);
+    float2 acc0 = make_float2(0.0f, 0.0f), acc1 = acc0;
+#pragma unroll
+    for (int j = 0; j < NVEC; j++) {
+        float x[VW];
+        DtypeTraits<DT>::unpack(vec(j), x);
+#pragma unroll
+        for (int k = 0; k < VW; k += 2) {
+            float2 v = make_float2(x[k], x[k + 1]);
+            if constexpr (CAP) v = __fmul2_rn(tanh_poly2(__fmul2_rn(v, ic)), c2);
+            if constexpr (TEMP) v = __fmul2_rn(v, t2);
+            const float2 y = __ffma2_rn(v, l2, nc);
+            const float2 e = make_float2(ex2_approx(y.x), ex2_approx(y.y));
+            if ((k >> 1) & 1) acc1 = __fadd2_rn(acc1, e);
+            else acc0 = __fadd2_rn(acc0, e);
+        }
+    }
+    acc0 = __fadd2_rn(acc0, acc1);
+    return acc0.x + acc0.y;
+}
+
+template <int DT, class Vec>
+__device__ __forceinline__ float fast_exp_sum_any(Vec vec, const SParams &sp, float cc)
+{
+    if (sp.use_cap)
+        return sp.use_t ? fast_exp_sum<DT, true, true>(vec, sp, cc) : fast_exp_sum<DT, true, false>(vec, sp, cc);
+    return sp.use_t ? fast_exp_sum<DT, false, true>(vec, sp, cc) : fast_exp_sum<DT, false, false>(vec, sp, cc);
+}
+
+// General path of one item (NaN present, |q| > 1 somewhere, or a ragged last
+// item): element by element from global memory, the maximum first, then the
+// exponent sum.  Out of line and rare; it holds nothing across the streaming
+// loop.  Returns (item max, exponent origin, sum).
+template <int DT>
+__device__ __noinline__ float3 slow_item(const void *logits, int64_t row_stride, int vocab, int row, int sub,
+                                         const SParams sp, bool draw)
 {
     using T = DtypeTraits<DT>;
-    constexpr int VW = T::VW, NV = EPT / VW, SLAB = NTHREADS * VW, NSUB = NV * NWARPS;
-    constexpr int CPT = NCH_MAX / NTHREADS;  // chunks per thread in the scan
-    const int nch = a.nch, tid = threadIdx.x, lane = tid & 31;
-    ChunkStat *st = a.stats + (int64_t)row * nch;
+    constexpr int VW = Geo<DT>::VW;
+    const float NEG_INF = -__uint_as_float(0x7f800000u);
+    const int lane = threadIdx.x & 31;
+    const int n = item_len<DT>(vocab, sub);
+    const char *rowp = (const char *)logits + (int64_t)row * row_stride * T::ESIZE;
+    const int64_t base = (int64_t)sub * Geo<DT>::ITEM;
+    float m = NEG_INF;
+#pragma unroll 1
+    for (int j = 0; j < NVEC; j++)
+#pragma unroll
+        for (int k = 0; k < VW; k++) {
+            const int e = item_pos<DT>(j, k, lane);
+            if (e < n) m = fmaxf(m, s_of(load_elem<DT>(rowp, base + e), sp));
+        }
+    m = warp_max_nan(m);
+    float cc = 0.0f, S = 0.0f;
+    if (draw && m > NEG_INF) {
+        cc = __fmul_rn(m, G4_L2E);
+#pragma unroll 1
+        for (int j = 0; j < NVEC; j++)
+#pragma unroll
+            for (int k = 0; k < VW; k++) {
+                const int e = item_pos<DT>(j, k, lane);
+                if (e < n) S += ex2_approx(__fmaf_rn(s_of(load_elem<DT>(rowp, base + e), sp), G4_L2E, -cc));
+            }
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) S += __shfl_xor_sync(FULLMASK, S, d);
+    }
+    return make_float3(m, cc, S);
+}
+
+// One item of the streaming pass; vec(j) returns this lane's vector j.
+template <int DT, class Vec>
+__device__ __forceinline__ void stream_item(const SampleArgs &a, int64_t it, int row, int sub, Vec vec)
+{
+    const float NEG_INF = -__uint_as_float(0x7f800000u);
+    const g4s_params p = a.params.get(row);
+    if (!(p.top_k <= 0 || p.top_k >= a.vocab)) return;
+    const SParams sp = make_sparams(a, p, row);
+    const bool draw = p.temperature > 0.0f;
+    const int n = item_len<DT>(a.vocab, sub);
+    float xmax;
+    const bool fast = n == Geo<DT>::ITEM && item_fast<DT>(vec, sp, xmax);
+    float m, cc = 0.0f, S = 0.0f;
+    if (fast) {
+        m = s_of(xmax, sp);  // softcap and temperature are monotone
+        if (draw && m > NEG_INF) {
+            cc = __fmul_rn(m, G4_L2E);
+            S = fast_exp_sum_any<DT>(vec, sp, cc);
+#pragma unroll
+            for (int d = 16; d > 0; d >>= 1) S += __shfl_xor_sync(FULLMASK, S, d);
+        }
+    } else {
+        const float3 r = slow_item<DT>(a.logits, a.row_stride, a.vocab, row, sub, sp, draw);
+        m = r.x;
+        cc = r.y;
+        S = r.z;
+    }
+    if ((threadIdx.x & 31) == 0) a.istat[it] = make_float4(m, cc, S, 0.0f);
+}
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem)
+{
+    const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Persistent streaming pass.  Warp w handles items w, w + W, w + 2W, ... (W =
+// warps in the grid).  With aligned rows each lane copies its own 16-byte
+// vectors of the next item into a per-warp two-stage shared-memory ring with
+// cp.async (completion tracked by cp.async.wait_group, no polling).
+template <int DT, bool VEC>
+__global__ void __launch_bounds__(STREAM_THREADS) full_stream_kernel(SampleArgs a)
+{
+    using T = DtypeTraits<DT>;
+    constexpr int VW = Geo<DT>::VW, ITEM = Geo<DT>::ITEM;
+    constexpr int WPB = STREAM_THREADS / 32;
+    __shared__ uint4 ring[VEC ? WPB * 2 * NVEC * 32 : 1];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int ipr = (a.vocab + ITEM - 1) / ITEM;
+    const int64_t nitems = (int64_t)a.rows * ipr;
+    const int64_t nw = (int64_t)gridDim.x * WPB;
+    const int64_t it0 = (int64_t)blockIdx.x * WPB + wib;
+    // (row, item-in-row) cursors advance by nw items without dividing
+    const int step_row = (int)(nw / ipr), step_sub = (int)(nw % ipr);
+    struct Cursor {
+        int row, sub;
+    };
+    auto advance = [&](Cursor &c) {
+        c.sub += step_sub;
+        c.row += step_row;
+        if (c.sub >= ipr) {
+            c.sub -= ipr;
+            c.row++;
+        }
+    };
+    Cursor cur{(int)(it0 / ipr), (int)(it0 % ipr)};
+
+    if constexpr (!VEC) {
+        for (int64_t it = it0; it < nitems; it += nw, advance(cur)) {
+            const int n = item_len<DT>(a.vocab, cur.sub);
+            const char *src = (const char *)a.logits + ((int64_t)cur.row * a.row_stride + (int64_t)cur.sub * ITEM) * T::ESIZE;
+            uint4 regs[NVEC];
+#pragma unroll
+            for (int j = 0; j < NVEC; j++) {
+                uint32_t w[4];
+                const int e0 = item_pos<DT>(j, 0, lane);
+                if constexpr (DT == G4S_F32) {
+#pragma unroll
+                    for (int k = 0; k < 4; k++)
+                        w[k] = e0 + k < n ? __float_as_uint(__ldg((const float *)src + e0 + k)) : 0u;
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const uint32_t lo = e0 + 2 * k < n ? __ldg((const unsigned short *)src + e0 + 2 * k) : 0u;
+                        const uint32_t hi = e0 + 2 * k + 1 < n ? __ldg((const unsigned short *)src + e0 + 2 * k + 1) : 0u;
+                        w[k] = lo | (hi << 16);
+                    }
+                }
+                regs[j] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            stream_item<DT>(a, it, cur.row, cur.sub, [&](int j) { return regs[j]; });
+        }
+    } else {
+        uint4 *wring = ring + wib * 2 * NVEC * 32;
+        // copies of a partial last item stop at the last whole vector; such items
+        // take the general path, which rereads them
+        auto issue = [&](int64_t i, const Cursor &c, int stage) {
+            if (i >= nitems) return;
+            const int n = item_len<DT>(a.vocab, c.sub);
+            const char *src = (const char *)a.logits + ((int64_t)c.row * a.row_stride + (int64_t)c.sub * ITEM) * T::ESIZE;
+            uint4 *dst = wring + stage * NVEC * 32;
+#pragma unroll
+            for (int j = 0; j < NVEC; j++) {
+                const int e0 = item_pos<DT>(j, 0, lane);
+                if (e0 + VW <= n) cp_async16(dst + j * 32 + lane, src + (int64_t)e0 * T::ESIZE);
+            }
+        };
+        Cursor nxt = cur;
+        issue(it0, nxt, 0);
+        cp_async_commit();
+        advance(nxt);
+        int stage = 0;
+        for (int64_t it = it0; it < nitems; it += nw) {
+            issue(it + nw, nxt, stage ^ 1);  // the other stage was consumed last iteration
+            cp_async_commit();
+            advance(nxt);
+            cp_async_wait<1>();  // this lane's copies of item `it` have landed
+            const uint4 *src = wring + stage * NVEC * 32;
+            stream_item<DT>(a, it, cur.row, cur.sub, [&](int j) { return src[j * 32 + lane]; });
+            advance(cur);
+            stage ^= 1;
+        }
+        cp_async_wait<0>();
+    }
+}
+
+// 2^d for a double d <= ~0: 2^round(d) * ex2(d - round(d)) (|f| <= 1/2, so the
+// fp32 ex2 is accurate to a few units in 1e-7 relative); 0 below 2^-1000.
+__device__ __forceinline__ double pow2_split(double d)
+{
+    if (d < -1000.0) return 0.0;
+    const double r = rint(d);
+    const float f = (float)(d - r);
+    const double scale = __longlong_as_double((long long)((int)r + 1023) << 52);
+    return (double)ex2_approx(f) * scale;
+}
+
+// s of the element at item position e (for the rescans), -inf past n.
+template <int DT>
+__device__ __forceinline__ float elem_s(const char *rowp, int64_t base, int e, int n, const SParams &sp)
+{
+    return e < n ? s_of(load_elem<DT>(rowp, base + e), sp) : -__uint_as_float(0x7f800000u);
+}
+
+// First id of the row's item `sub` whose s equals M (warp-uniform result).
+template <int DT>
+__device__ int item_argmax(const SampleArgs &a, int row, int sub, const SParams &sp, float M)
+{
+    using T = DtypeTraits<DT>;
+    constexpr int VW = Geo<DT>::VW;
+    const int lane = threadIdx.x & 31;
+    const int n = item_len<DT>(a.vocab, sub);
+    const char *rowp = (const char *)a.logits + (int64_t)row * a.row_stride * T::ESIZE;
+    const int64_t base = (int64_t)sub * Geo<DT>::ITEM;
+    unsigned best = 0xffffffffu;
+    for (int j = 0; j < NVEC; j++)
+#pragma unroll
+        for (int k = 0; k < VW; k++) {
+            const int e = item_pos<DT>(j, k, lane);
+            if (elem_s<DT>(rowp, base, e, n, sp) == M && (unsigned)e < best) best = (unsigned)e;
+        }
+    best = __reduce_min_sync(FULLMASK, best);
+    return sub * Geo<DT>::ITEM + (best == 0xffffffffu ? 0 : (int)best);
+}
+
+template <int DT, bool VEC>
+__global__ void __launch_bounds__(128) full_combine_kernel(SampleArgs a)
+{
+    using T = DtypeTraits<DT>;
+    constexpr int VW = Geo<DT>::VW, ITEM = Geo<DT>::ITEM;
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= a.rows) return;
+    const g4s_params p = a.params.get(row);
+    if (!(p.top_k <= 0 || p.top_k >= a.vocab)) return;
+    const SParams sp = make_sparams(a, p, row);
+    const int ipr = (a.vocab + ITEM - 1) / ITEM;
+    const float4 *st = a.istat + (int64_t)row * ipr;
     const float NEG_INF = -__uint_as_float(0x7f800000u);
 
+    // row maximum and the first item holding it
     float M = NEG_INF;
-    int arg = 0x7fffffff;
-    for (int c = tid; c < nch; c += NTHREADS) {
-        const float m = __ldcg(&st[c].m);
-        const int ai = __ldcg(&st[c].arg);
-        if (m > M || (m == M && ai < arg)) { M = m; arg = ai; }
+    int mi = 0x7fffffff;
+    for (int i = lane; i < ipr; i += 32) {
+        const float m = st[i].x;
+        if (m > M) { M = m; mi = i; }
     }
-    block_argmax(M, arg, sm);
-    if (!(M > NEG_INF)) arg = 0;  // every value is -inf (softcap disabled): the reference lands on id 0
-
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) {
+        const float om = __shfl_xor_sync(FULLMASK, M, d);
+        const int oi = __shfl_xor_sync(FULLMASK, mi, d);
+        if (om > M || (om == M && oi < mi)) { M = om; mi = oi; }
+    }
     const bool draw = p.temperature > 0.0f;
-    int token = arg;
     int32_t flags = G4S_ROW_FULL_PATH | (draw ? 0 : G4S_ROW_GREEDY);
+    int token = -1;
     float tprob = 0.0f;
     double S = 0.0;
-    if (draw && M > NEG_INF) {
+    bool need_argmax = !draw;
+    if (!(M > NEG_INF)) {
+        token = 0;  // every value is -inf (softcap disabled): the reference's NaN arithmetic ends at id 0
+        need_argmax = false;
+    } else if (draw) {
         const double Ml = (double)M * (double)G4_L2E;
-        double loc[CPT];
-        double tsum = 0.0;
-#pragma unroll
-        for (int r = 0; r < CPT; r++) {
-            const int c = tid * CPT + r;
-            double w = 0.0, ps = 0.0;
-            if (c < nch) {
-                const float m = __ldcg(&st[c].m);
-                if (m > NEG_INF) {
-                    w = exp2((double)__ldcg(&st[c].cc) - Ml);
-                    ps = __ldcg(&st[c].S) * w;
-                }
-                sm.w[c] = w;
+        for (int r0 = 0; r0 < ipr; r0 += 32) {
+            const int i = r0 + lane;
+            double P = 0.0;
+            if (i < ipr) {
+                const float4 q = st[i];
+                if (q.x > NEG_INF) P = (double)q.z * pow2_split((double)q.y - Ml);
             }
-            tsum += ps;
-            loc[r] = tsum;
-        }
-        const double excl = block_excl_scan_d(tsum, &S, sm.dscan);
 #pragma unroll
-        for (int r = 0; r < CPT; r++) {
-            const int c = tid * CPT + r;
-            if (c < nch) sm.pref[c] = excl + loc[r];
+            for (int d = 16; d > 0; d >>= 1) P += __shfl_xor_sync(FULLMASK, P, d);
+            S += P;
         }
-        if (tid == 0) sm.misc[2] = -1;
-        __syncthreads();
         const float thr = __double2float_rn(a.u[row] * (double)p.top_p);
         const double target = (double)thr * S;
-        for (int c = tid; c < nch; c += NTHREADS)
-            if (sm.pref[c] >= target && (c == 0 || sm.pref[c - 1] < target)) sm.misc[2] = c;
-        __syncthreads();
-        const int cs = sm.misc[2];
-        if (cs < 0) {
-            flags |= G4S_ROW_FALLBACK;
-            if (tid == 0) {
-                const int ca = arg / a.chunk;
-                const float e = ex2_approx(__fmaf_rn(M, G4_L2E, -__ldcg(&st[ca].cc)));
-                tprob = (float)((double)e * sm.w[ca] / S);
-            }
-        } else if (tid < 32) {
-            const double base = cs > 0 ? sm.pref[cs - 1] : 0.0;
-            const double w = sm.w[cs];
-            const double tloc = (target - base) / w;
-            const float cc = __ldcg(&st[cs].cc);
-            // sub-range: first whose running sum reaches tloc (else the last non-empty one)
-            int ks = -1;
-            double subbase = 0.0;
-            if (lane == 0) {
-                double cum = 0.0, lastbase = 0.0;
-                int last = 0;
-                for (int k = 0; k < NSUB; k++) {
-                    const double sv = (double)__ldcg(&st[cs].sub[k]);
-                    if (sv > 0.0) { last = k; lastbase = cum; }
-                    if (cum + sv >= tloc) { ks = k; subbase = cum; break; }
-                    cum += sv;
+        // the item whose cumulative mass reaches the target
+        double base = 0.0, ibase = 0.0, iw = 0.0;
+        int hit_item = -1;
+        for (int r0 = 0; r0 < ipr && hit_item < 0; r0 += 32) {
+            const int i = r0 + lane;
+            double P = 0.0, w = 0.0;
+            if (i < ipr) {
+                const float4 q = st[i];
+                if (q.x > NEG_INF) {
+                    w = pow2_split((double)q.y - Ml);
+                    P = (double)q.z * w;
                 }
-                if (ks < 0) { ks = last; subbase = lastbase; }
             }
-            ks = __shfl_sync(FULLMASK, ks, 0);
-            subbase = __shfl_sync(FULLMASK, subbase, 0);
-            const int j = ks / NWARPS, wsub = ks % NWARPS;
-            const int64_t c0 = (int64_t)cs * a.chunk;
-            const int n = (int)min((int64_t)a.chunk, (int64_t)a.vocab - c0);
-            const int e0 = j * SLAB + wsub * 32 * VW + lane * VW;
-            const void *rowp = (const char *)a.logits + (int64_t)row * a.row_stride * T::ESIZE;
-            float ev[VW];
-            double lsum = 0.0;
+            double incl = P;
 #pragma unroll
-            for (int l = 0; l < VW; l++) {
-                float e = 0.0f;
-                if (e0 + l < n) {
-                    const float s = s_of(T::load1(rowp, c0 + e0 + l), sp);
-                    e = ex2_approx(__fmaf_rn(s, G4_L2E, -cc));
-                }
-                ev[l] = e;
-                lsum += (double)e;
+            for (int d = 1; d < 32; d <<= 1) {
+                const double o = __shfl_up_sync(FULLMASK, incl, d);
+                if (lane >= d) incl += o;
             }
-            const double lincl = warp_incl_scan_d(lsum);
-            double run = subbase + (lincl - lsum);
-            int found = -1;
-#pragma unroll
-            for (int l = 0; l < VW; l++) {
-                run += (double)ev[l];
-                if (found < 0 && run >= tloc) found = l;
-            }
-            unsigned hit = __ballot_sync(FULLMASK, found >= 0);
-            int tl, te;
+            const unsigned hit = __ballot_sync(FULLMASK, i < ipr && base + incl >= target);
             if (hit) {
-                tl = __ffs(hit) - 1;
-                te = __shfl_sync(FULLMASK, found, tl);
-            } else {
-                // rounding left the threshold past this range: last id with mass
-                int lastl = -1;
-#pragma unroll
-                for (int l = 0; l < VW; l++)
-                    if (ev[l] > 0.0f) lastl = l;
-                unsigned any = __ballot_sync(FULLMASK, lastl >= 0);
-                tl = any ? 31 - __clz(any) : 0;
-                te = __shfl_sync(FULLMASK, lastl < 0 ? 0 : lastl, tl);
+                const int L = __ffs(hit) - 1;
+                hit_item = r0 + L;
+                ibase = __shfl_sync(FULLMASK, base + incl - P, L);
+                iw = __shfl_sync(FULLMASK, w, L);
             }
-            float etok = 0.0f;
+            base += __shfl_sync(FULLMASK, incl, 31);
+        }
+        if (hit_item < 0) {
+            flags |= G4S_ROW_FALLBACK;
+            need_argmax = true;
+        } else {
+            // rescan the item: first id whose running sum reaches the target.
+            // Item ids run j-major, then lane, then k.
+            const float cc = st[hit_item].y;
+            const double tloc = (target - ibase) / iw;
+            const int n = item_len<DT>(a.vocab, hit_item);
+            const char *rowp = (const char *)a.logits + (int64_t)row * a.row_stride * T::ESIZE;
+            const int64_t ib = (int64_t)hit_item * ITEM;
+            double run = 0.0;
+            int pos = -1, last = -1;
+            float etok = 0.0f, elast = 0.0f;
+            for (int j = 0; j < NVEC && pos < 0; j++) {
+                float ev[VW];
+                double lsum = 0.0;
 #pragma unroll
-            for (int l = 0; l < VW; l++)
-                if (l == te) etok = ev[l];
-            etok = __shfl_sync(FULLMASK, etok, tl);
-            token = (int)(c0 + j * SLAB + wsub * 32 * VW + tl * VW + te);
-            tprob = (float)((double)etok * w / S);
+                for (int k = 0; k < VW; k++) {
+                    const int e = item_pos<DT>(j, k, lane);
+                    ev[k] = e < n ? ex2_approx(__fmaf_rn(elem_s<DT>(rowp, ib, e, n, sp), G4_L2E, -cc)) : 0.0f;
+                    lsum += (double)ev[k];
+                }
+                double lincl = lsum;
+#pragma unroll
+                for (int d = 1; d < 32; d <<= 1) {
+                    const double o = __shfl_up_sync(FULLMASK, lincl, d);
+                    if (lane >= d) lincl += o;
+                }
+                double c = run + lincl - lsum;
+                int found = -1;
+                float efound = 0.0f;
+#pragma unroll
+                for (int k = 0; k < VW; k++) {
+                    c += (double)ev[k];
+                    if (found < 0 && c >= tloc) { found = k; efound = ev[k]; }
+                    if (ev[k] > 0.0f) { last = item_pos<DT>(j, k, lane); elast = ev[k]; }
+                }
+                const unsigned hit = __ballot_sync(FULLMASK, found >= 0);
+                if (hit) {
+                    const int L = __ffs(hit) - 1;
+                    pos = item_pos<DT>(j, __shfl_sync(FULLMASK, found, L), L);
+                    etok = __shfl_sync(FULLMASK, efound, L);
+                }
+                run += __shfl_sync(FULLMASK, lincl, 31);
+            }
+            if (pos < 0) {
+                // rounding left the threshold past this item: its last id with mass
+                const int lmax = (int)__reduce_max_sync(FULLMASK, (unsigned)(last + 1)) - 1;
+                const unsigned owner = __ballot_sync(FULLMASK, last == lmax && lmax >= 0);
+                pos = lmax < 0 ? 0 : lmax;
+                etok = owner ? __shfl_sync(FULLMASK, elast, __ffs(owner) - 1) : 0.0f;
+            }
+            token = hit_item * ITEM + pos;
+            tprob = (float)((double)etok * iw / S);
         }
     }
-    if (tid == 0) {
+    if (need_argmax) {
+        token = item_argmax<DT>(a, row, mi, sp, M);
+        if (draw) {
+            const float4 q = st[mi];
+            const double w = pow2_split((double)q.y - (double)M * (double)G4_L2E);
+            tprob = (float)((double)ex2_approx(__fmaf_rn(M, G4_L2E, -q.y)) * w / S);
+        }
+    }
+    if (lane == 0) {
         a.out_tokens[row] = token;
         if (a.token_prob) a.token_prob[row] = tprob;
         if (a.row_flags) a.row_flags[row] = flags;
@@ -320,155 +583,94 @@ __device__ void full_combine(const SampleArgs &a, int row, const g4s_params &p,
         rs.M = M;
         rs.token = token;
         a.rowstat[row] = rs;
-        a.counters_full[row] = 0;  // ready for the next call
     }
-    if (draw && M > NEG_INF)
-        for (int c = tid; c < nch; c += NTHREADS) st[c].w = sm.w[c];
 }
 
-template <int DT, int EPT, bool VEC>
-__global__ void __launch_bounds__(NTHREADS) full_chunk_kernel(SampleArgs a)
-{
-    __shared__ FullSmem sm;
-    using T = DtypeTraits<DT>;
-    constexpr int VW = T::VW, NV = EPT / VW, SLAB = NTHREADS * VW;
-    const int row = blockIdx.y, chunk = blockIdx.x, tid = threadIdx.x;
-    const int lane = tid & 31, warp = tid >> 5;
-    const g4s_params p = a.params.get(row);
-    const int K = p.top_k;
-    if (!(K <= 0 || K >= a.vocab)) return;
-    const int64_t c0 = (int64_t)chunk * a.chunk;
-    const int n = (int)min((int64_t)a.chunk, (int64_t)a.vocab - c0);
-    const void *rowp = (const char *)a.logits + (int64_t)row * a.row_stride * T::ESIZE;
-    const SParams sp = make_sparams(a.softcap, p);
-    const float NEG_INF = -__uint_as_float(0x7f800000u);
-
-    float x[EPT];
-    load_chunk<DT, EPT, VEC>(rowp, c0, n, x);
-    s_of_vec<EPT>(x, sp);
-    if (n < a.chunk) {
-#pragma unroll
-        for (int i = 0; i < EPT; i++)
-            if ((i / VW) * SLAB + tid * VW + (i % VW) >= n) x[i] = NEG_INF;
-    }
-    float m = NEG_INF;
-    int arg = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < EPT; i++) {
-        if (x[i] > m) {
-            m = x[i];
-            arg = (int)(c0 + (i / VW) * SLAB + tid * VW + (i % VW));
-        }
-    }
-    block_argmax(m, arg, sm);
-
-    const bool draw = p.temperature > 0.0f;
-    float cc = 0.0f;
-    double S = 0.0;
-    if (draw && m > NEG_INF) {
-        cc = __fmul_rn(m, G4_L2E);
-        const float2 l2 = make_float2(G4_L2E, G4_L2E), nc = make_float2(-cc, -cc);
-#pragma unroll
-        for (int j = 0; j < NV; j++) {
-            float e[VW];
-#pragma unroll
-            for (int l = 0; l < VW; l += 2) {
-                float2 y = __ffma2_rn(make_float2(x[j * VW + l], x[j * VW + l + 1]), l2, nc);
-                e[l] = ex2_approx(y.x);
-                e[l + 1] = ex2_approx(y.y);
-            }
-            float ps;
-            if constexpr (VW == 8)
-                ps = ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
-            else
-                ps = (e[0] + e[1]) + (e[2] + e[3]);
-            ps = warp_sum_f(ps);
-            if (lane == 0) sm.sub[j * NWARPS + warp] = ps;
-        }
-        __syncthreads();
-        if (tid == 0) {
-            for (int k = 0; k < NV * NWARPS; k++) S += (double)sm.sub[k];
-        }
-    }
-    ChunkStat *st = a.stats + (int64_t)row * a.nch + chunk;
-    if (tid == 0) {
-        st->m = m;
-        st->arg = arg;
-        st->cc = cc;
-        st->nsub = NV * NWARPS;
-        st->S = S;
-    }
-    if (tid < NV * NWARPS) st->sub[tid] = (draw && m > NEG_INF) ? sm.sub[tid] : 0.0f;
-
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) sm.misc[1] = atomicAdd(&a.counters_full[row], 1u) == (unsigned)(a.nch - 1);
-    __syncthreads();
-    if (!sm.misc[1]) return;
-    __threadfence();
-    full_combine<DT, EPT>(a, row, p, sp, sm);
-}
-
-// Verification pass: every probability of full-path rows, from the statistics
-// the sampling kernel left (same per-element arithmetic).
-template <int DT, int EPT, bool VEC>
+// Verification pass: every probability of full-path rows from the statistics
+// the sampling kernels left (same per-element arithmetic).  One warp per item.
+template <int DT>
 __global__ void __launch_bounds__(NTHREADS) full_probs_kernel(SampleArgs a)
 {
     using T = DtypeTraits<DT>;
-    constexpr int VW = T::VW, SLAB = NTHREADS * VW;
-    const int row = blockIdx.y, chunk = blockIdx.x, tid = threadIdx.x;
+    constexpr int VW = Geo<DT>::VW, ITEM = Geo<DT>::ITEM;
+    const int lane = threadIdx.x & 31;
+    const int ipr = (a.vocab + ITEM - 1) / ITEM;
+    const int64_t it = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (it >= (int64_t)a.rows * ipr) return;
+    const int row = (int)(it / ipr), sub = (int)(it - (int64_t)row * ipr);
     const g4s_params p = a.params.get(row);
-    const int K = p.top_k;
-    if (!(K <= 0 || K >= a.vocab) || !(p.temperature > 0.0f)) return;
+    if (!(p.top_k <= 0 || p.top_k >= a.vocab) || !(p.temperature > 0.0f)) return;
     const RowStat rs = a.rowstat[row];
     if (!(rs.S > 0.0)) return;
-    const ChunkStat *st = a.stats + (int64_t)row * a.nch + chunk;
-    const int64_t c0 = (int64_t)chunk * a.chunk;
-    const int n = (int)min((int64_t)a.chunk, (int64_t)a.vocab - c0);
-    const void *rowp = (const char *)a.logits + (int64_t)row * a.row_stride * T::ESIZE;
-    const SParams sp = make_sparams(a.softcap, p);
-    const float cc = st->cc;
-    const double w = st->w;
-    const bool live = st->m > -__uint_as_float(0x7f800000u);
-    float x[EPT];
-    load_chunk<DT, EPT, VEC>(rowp, c0, n, x);
-    s_of_vec<EPT>(x, sp);
+    const float4 q = a.istat[it];
+    const SParams sp = make_sparams(a, p, row);
+    const int n = item_len<DT>(a.vocab, sub);
+    const char *rowp = (const char *)a.logits + (int64_t)row * a.row_stride * T::ESIZE;
+    const int64_t ib = (int64_t)sub * ITEM;
+    const bool live = q.x > -__uint_as_float(0x7f800000u);
+    const double w = live ? pow2_split((double)q.y - (double)rs.M * (double)G4_L2E) : 0.0;
+    for (int j = 0; j < NVEC; j++)
 #pragma unroll
-    for (int i = 0; i < EPT; i++) {
-        const int e = (i / VW) * SLAB + tid * VW + (i % VW);
-        if (e < n) {
-            const float ev = live ? ex2_approx(__fmaf_rn(x[i], G4_L2E, -cc)) : 0.0f;
-            a.full_probs[(int64_t)row * a.vocab + c0 + e] = (float)((double)ev * w / rs.S);
+        for (int k = 0; k < VW; k++) {
+            const int e = item_pos<DT>(j, k, lane);
+            if (e < n) {
+                const float ev = live ? ex2_approx(__fmaf_rn(elem_s<DT>(rowp, ib, e, n, sp), G4_L2E, -q.y)) : 0.0f;
+                a.full_probs[(int64_t)row * a.vocab + ib + e] = (float)((double)ev * w / rs.S);
+            }
         }
-    }
 }
 
-template <int DT, int EPT, bool VEC>
+template <int DT, bool VEC>
 static cudaError_t launch_full_t(const SampleArgs &a, cudaStream_t s, bool probs)
 {
-    dim3 grid(a.nch, a.rows);
-    if (probs) full_probs_kernel<DT, EPT, VEC><<<grid, NTHREADS, 0, s>>>(a);
-    else full_chunk_kernel<DT, EPT, VEC><<<grid, NTHREADS, 0, s>>>(a);
+    constexpr int ITEM = Geo<DT>::ITEM;
+    const int ipr = (a.vocab + ITEM - 1) / ITEM;
+    const int64_t nitems = (int64_t)a.rows * ipr;
+    if (!probs) {
+        constexpr int wpb = STREAM_THREADS / 32;
+        int64_t blocks = (nitems + wpb - 1) / wpb;
+        if (a.persist_blocks > 0 && blocks > a.persist_blocks) blocks = a.persist_blocks;
+        full_stream_kernel<DT, VEC><<<(unsigned)blocks, STREAM_THREADS, 0, s>>>(a);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        full_combine_kernel<DT, VEC><<<(a.rows + 3) / 4, 128, 0, s>>>(a);
+    } else {
+        full_probs_kernel<DT><<<(unsigned)((nitems + NWARPS - 1) / NWARPS), NTHREADS, 0, s>>>(a);
+    }
     return cudaGetLastError();
 }
 
 template <int DT>
-static cudaError_t launch_full_dt(const SampleArgs &a, int ept, bool vec, cudaStream_t s, bool probs)
+static cudaError_t launch_full_dt(const SampleArgs &a, bool vec, cudaStream_t s, bool probs)
 {
-    if (ept == 8) return vec ? launch_full_t<DT, 8, true>(a, s, probs) : launch_full_t<DT, 8, false>(a, s, probs);
-    return vec ? launch_full_t<DT, 32, true>(a, s, probs) : launch_full_t<DT, 32, false>(a, s, probs);
+    return vec ? launch_full_t<DT, true>(a, s, probs) : launch_full_t<DT, false>(a, s, probs);
 }
 
-cudaError_t launch_full(const SampleArgs &a, int ept, bool vec, cudaStream_t s)
+int full_stream_blocks_per_sm(int dtype, bool vec)
 {
-    return a.dtype == G4S_F32 ? launch_full_dt<G4S_F32>(a, ept, vec, s, false)
-                              : launch_full_dt<G4S_BF16>(a, ept, vec, s, false);
+    int n = 0;
+    cudaError_t e;
+    if (dtype == G4S_F32)
+        e = vec ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, full_stream_kernel<G4S_F32, true>, STREAM_THREADS, 0)
+                : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, full_stream_kernel<G4S_F32, false>, STREAM_THREADS, 0);
+    else
+        e = vec ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, full_stream_kernel<G4S_BF16, true>, STREAM_THREADS, 0)
+                : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, full_stream_kernel<G4S_BF16, false>, STREAM_THREADS, 0);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return 4;
+    }
+    return n > 0 ? n : 1;
 }
 
-cudaError_t launch_full_probs(const SampleArgs &a, int ept, bool vec, cudaStream_t s)
+cudaError_t launch_full(const SampleArgs &a, int, bool vec, cudaStream_t s)
 {
-    return a.dtype == G4S_F32 ? launch_full_dt<G4S_F32>(a, ept, vec, s, true)
-                              : launch_full_dt<G4S_BF16>(a, ept, vec, s, true);
+    return a.dtype == G4S_F32 ? launch_full_dt<G4S_F32>(a, vec, s, false) : launch_full_dt<G4S_BF16>(a, vec, s, false);
+}
+
+cudaError_t launch_full_probs(const SampleArgs &a, int, bool vec, cudaStream_t s)
+{
+    return a.dtype == G4S_F32 ? launch_full_dt<G4S_F32>(a, vec, s, true) : launch_full_dt<G4S_BF16>(a, vec, s, true);
 }
 
 }  // namespace g4s

@@ -8,27 +8,22 @@
 
 namespace g4s {
 
-// Per-row sampling parameters: one broadcast record, or a device array.
+// Per-row sampling parameters: one broadcast record, or a device array.  The
+// reciprocal temperature fl32(1/T) is computed on the host (IEEE division,
+// identical to the device's) so that no kernel divides per item.
 struct RowParams {
     const g4s_params *dev;  // [rows] on the device, or nullptr
+    const float *inv_t_dev; // [rows] fl32(1/temperature), when dev != nullptr
     g4s_params p0;          // used when dev == nullptr
+    float inv_t0;           // fl32(1/p0.temperature)
     __device__ __forceinline__ g4s_params get(int r) const { return dev ? dev[r] : p0; }
+    __device__ __forceinline__ float inv_t(int r) const { return dev ? inv_t_dev[r] : inv_t0; }
 };
 
-// Statistics of one chunk of a full-vocabulary row.
-struct __align__(16) ChunkStat {
-    float m;         // largest softcapped (and tempered) logit of the chunk
-    int32_t arg;     // lowest vocab id holding m
-    float cc;        // fl32(m * log2 e): the chunk's exponent origin
-    int32_t nsub;    // number of sub-sums below
-    double S;        // sum of 2^(s * log2 e - cc) over the chunk
-    double w;        // 2^(cc - M * log2 e): chunk weight, written by the row combine
-    float sub[64];   // sums over consecutive 32 * VW-id ranges, in id order
-};
-
+// Per-row result of the full-vocabulary combine (read by the verification pass).
 struct RowStat {
     double S;        // row denominator in the scale of the row maximum
-    float M;
+    float M;         // row maximum of the softcapped/tempered logits
     int32_t token;
 };
 
@@ -41,8 +36,10 @@ struct SampleArgs {
     int32_t chunk;        // elements per chunk (per kernel kind)
     int32_t nch;          // chunks per row
     int32_t lk_slots;     // concurrent rows of the large-K kernel
+    int32_t persist_blocks;  // CTAs of the persistent full-path streaming kernel
     RowParams params;
     float softcap;
+    float invcap;         // fl32(1/softcap) when softcap > 0
     const double *u;
     int32_t *out_tokens;
     // optional outputs (nullable)
@@ -56,8 +53,7 @@ struct SampleArgs {
     uint64_t *cand;            // [rows][nch][KMAX] per-chunk sorted candidates
     int32_t *cand_cnt;         // [rows][nch]
     uint32_t *counters_topk;   // [rows], zero between calls
-    uint32_t *counters_full;   // [rows], zero between calls
-    ChunkStat *stats;          // [rows][nch]
+    float4 *istat;             // [rows][items per row] full path: (m, cc, S, 0) per item
     RowStat *rowstat;          // [rows]
     int32_t *lk_idx;           // [lk_slots][vocab]
     float *lk_val;             // [lk_slots][vocab]
@@ -68,5 +64,7 @@ cudaError_t launch_topk(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
 cudaError_t launch_full(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
 cudaError_t launch_full_probs(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
 cudaError_t launch_largek(const SampleArgs &a, cudaStream_t s);
+// Resident CTAs per SM of the full-path streaming kernel (for its persistent grid).
+int full_stream_blocks_per_sm(int dtype, bool vec);
 
 }  // namespace g4s

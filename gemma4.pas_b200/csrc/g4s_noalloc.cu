@@ -133,7 +133,9 @@ extern "C" int32_t g4s_sample_topk_noalloc(const void *logits, int32_t dtype, in
     a.nch = (int32_t)nch;
     a.params.dev = nullptr;
     a.params.p0 = p;
+    a.params.inv_t0 = (p.temperature > 0.0f && p.temperature != 1.0f) ? 1.0f / p.temperature : 1.0f;
     a.softcap = softcap;
+    a.invcap = softcap > 0.0f ? 1.0f / softcap : 0.0f;
     a.u = u;
     a.out_tokens = out_tokens;
     a.cand = (uint64_t *)b;

@@ -28,13 +28,14 @@ namespace g4s {
 
 struct TopkSmem {
     uint64_t L[CAP2];
-    float tv[KMAX];
+    alignas(16) float tv[KMAX];
     int32_t ids[KMAX];
     uint32_t hist[256];
     uint32_t wthr[NWARPS];
     int scan[NWARPS + 1];
     int misc[4];
     float fmisc[2];
+    uint64_t t2;
 };
 
 // Radix selection of the K-th largest 64-bit composite among the candidates a
@@ -123,8 +124,17 @@ __device__ void topk_tail(const SampleArgs &a, int row, const g4s_params &p, int
         __syncwarp();
         // serial fp32 sum in ascending-id order (src/Gemma4.Model.pas:2794-2799)
         if (lane == 0) {
+            // four values per shared-memory load; only the fp32 adds are serial
             float s = 0.0f;
-            for (int i = 0; i < kw; i++) s = __fadd_rn(s, sm.tv[i]);
+            int i = 0;
+            for (; i + 4 <= kw; i += 4) {
+                const float4 q = *reinterpret_cast<const float4 *>(&sm.tv[i]);
+                s = __fadd_rn(s, q.x);
+                s = __fadd_rn(s, q.y);
+                s = __fadd_rn(s, q.z);
+                s = __fadd_rn(s, q.w);
+            }
+            for (; i < kw; i++) s = __fadd_rn(s, sm.tv[i]);
             sm.fmisc[0] = s;
         }
         __syncwarp();
@@ -151,9 +161,21 @@ __device__ void topk_tail(const SampleArgs &a, int row, const g4s_params &p, int
                 const float thr = __double2float_rn(a.u[row] * (double)p.top_p);
                 float cum = 0.0f;
                 int found = -1;
-                for (int i = 0; i < kw; i++) {
-                    cum = __fadd_rn(cum, sm.tv[i]);
+                int i = 0;
+                for (; i + 4 <= kw && found < 0; i += 4) {
+                    const float4 q = *reinterpret_cast<const float4 *>(&sm.tv[i]);
+                    cum = __fadd_rn(cum, q.x);
                     if (cum >= thr) { found = i; break; }
+                    cum = __fadd_rn(cum, q.y);
+                    if (cum >= thr) { found = i + 1; break; }
+                    cum = __fadd_rn(cum, q.z);
+                    if (cum >= thr) { found = i + 2; break; }
+                    cum = __fadd_rn(cum, q.w);
+                    if (cum >= thr) { found = i + 3; break; }
+                }
+                for (; i < kw && found < 0; i++) {
+                    cum = __fadd_rn(cum, sm.tv[i]);
+                    if (cum >= thr) found = i;
                 }
                 sm.misc[3] = found;
             }
@@ -178,13 +200,51 @@ __device__ void topk_tail(const SampleArgs &a, int row, const g4s_params &p, int
     }
 }
 
-// Sorts sm.L[0..n) descending (pads to a power of two with zeros).
+// Sorts sm.L[0..n) descending.  Up to NTHREADS distinct keys: one thread per
+// key counts the keys above it and scatters (no barrier-bound stages);
+// larger lists: bitonic sort padded to a power of two with zeros.
 __device__ __forceinline__ void sort_list_desc(TopkSmem &sm, int n)
 {
-    const int P = next_pow2(n > 1 ? n : 1);
+    if (n <= NTHREADS) {
+        uint64_t *out = sm.L + CAP2 / 2;
+        const int t = threadIdx.x;
+        if (t < n) {
+            const uint64_t v = sm.L[t];
+            int r = 0;
+            for (int q = 0; q < n; q++) r += sm.L[q] > v;
+            out[r] = v;
+        }
+        __syncthreads();
+        if (t < n) sm.L[t] = out[t];
+        __syncthreads();
+        return;
+    }
+    const int P = next_pow2(n);
     for (int i = n + threadIdx.x; i < P; i += NTHREADS) sm.L[i] = 0;
     __syncthreads();
     block_bitonic_desc(sm.L, P);
+}
+
+// Number of leading entries >= t of a descending list of cnt entries (global).
+// The first 8 entries come in with independent loads; only lists whose first 8
+// all qualify (rare) continue with a binary search.
+__device__ __forceinline__ int prefix_at_least(const uint64_t *list, int cnt, uint64_t t)
+{
+    if (cnt <= 0) return 0;
+    uint64_t h[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) h[i] = i < cnt ? __ldcg(&list[i]) : 0;
+    int c = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) c += (i < cnt && h[i] >= t);
+    if (c < 8 || cnt <= 8) return c;
+    int lo = 8, hi = cnt;  // answer in [lo, hi]
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (__ldcg(&list[mid]) >= t) lo = mid + 1;
+        else hi = mid;
+    }
+    return lo;
 }
 
 // Stage 2 of a row (last-arriving CTA): merge the per-chunk lists and sample.
@@ -196,35 +256,54 @@ __device__ void topk_merge(const SampleArgs &a, int row, const g4s_params &p, To
     const int j = (K + nch - 1) / nch;
     const int mm = (K + j - 1) / j;
     // lower bound t2: the mm-th largest of the chunks' j-th entries
-    {
-        const int P = next_pow2(nch);
-        for (int c = tid; c < P; c += NTHREADS) {
-            uint64_t h = 0;
-            if (c < nch && __ldcg(&CC[c]) >= j) h = __ldcg(&C[(int64_t)c * KMAX + j - 1]);
-            sm.L[c] = h;
+    for (int c = tid; c < nch; c += NTHREADS) {
+        uint64_t h = 0;
+        if (__ldcg(&CC[c]) >= j) h = __ldcg(&C[(int64_t)c * KMAX + j - 1]);
+        sm.L[c] = h;
+    }
+    __syncthreads();
+    uint64_t t2;
+    if (nch <= NTHREADS) {
+        // stable rank of each head; the one ranked mm-1 is t2
+        if (tid < nch) {
+            const uint64_t v = sm.L[tid];
+            int r = 0;
+            for (int q = 0; q < nch; q++) {
+                const uint64_t w = sm.L[q];
+                r += (w > v) || (w == v && q < tid);
+            }
+            if (r == mm - 1) sm.t2 = v;
         }
         __syncthreads();
+        t2 = sm.t2;
+    } else {
+        const int P = next_pow2(nch);
+        for (int c = nch + tid; c < P; c += NTHREADS) sm.L[c] = 0;
+        __syncthreads();
         block_bitonic_desc(sm.L, P);
+        t2 = sm.L[mm - 1];
     }
-    uint64_t t2 = sm.L[mm - 1];
     if (t2 == 0) t2 = 1;  // every list entry is a valid candidate
     __syncthreads();
-    const int slots = nch * K;
+    // candidates >= t2: a prefix of each chunk's descending list
+    constexpr int CPT = NCH_MAX / NTHREADS;
+    int pc[CPT];
     int cnt = 0;
-    for (int s = tid; s < slots; s += NTHREADS) {
-        const int c = s / K, i = s - c * K;
-        if (i < __ldcg(&CC[c]) && __ldcg(&C[(int64_t)c * KMAX + i]) >= t2) cnt++;
+#pragma unroll
+    for (int r = 0; r < CPT; r++) {
+        const int c = tid * CPT + r;
+        pc[r] = c < nch ? prefix_at_least(C + (int64_t)c * KMAX, __ldcg(&CC[c]), t2) : 0;
+        cnt += pc[r];
     }
+    const int slots = nch * K;
     int total;
     int off = block_excl_scan(cnt, &total, sm.scan);
     int kw;
-    if (total <= CAP2) {
-        for (int s = tid; s < slots; s += NTHREADS) {
-            const int c = s / K, i = s - c * K;
-            if (i < __ldcg(&CC[c])) {
-                const uint64_t v = __ldcg(&C[(int64_t)c * KMAX + i]);
-                if (v >= t2) sm.L[off++] = v;
-            }
+    if (total <= CAP2 / 2) {
+#pragma unroll
+        for (int r = 0; r < CPT; r++) {
+            const uint64_t *list = C + (int64_t)(tid * CPT + r) * KMAX;
+            for (int i = 0; i < pc[r]; i++) sm.L[off++] = __ldcg(&list[i]);
         }
         __syncthreads();
         sort_list_desc(sm, total);
