@@ -4,10 +4,10 @@
 // (src/Gemma4.Tensors.pas:638-674) as one streaming pass plus a per-row combine.
 //
 // full_stream_kernel: persistent, independent warps (no block barriers, no
-//   fences).  A warp item is 4 KiB of one row (2048 bf16 or 1024 fp32 logits);
-//   each lane copies its own eight 16-byte vectors of the next item into a
-//   per-warp two-stage shared-memory ring with cp.async while the current item
-//   is processed in two passes over the ring:
+//   fences).  A warp item is 2 KiB of one row (1024 bf16 or 512 fp32 logits);
+//   each lane copies its own four 16-byte vectors of the items two ahead into a
+//   per-warp three-stage shared-memory ring with cp.async, and processes the
+//   current item from registers in two passes:
 //     1. NaN-propagating min/max of the raw logits (packed bf16x2 or 3-input
 //        fp32 min/max), reduced over the warp.  With no NaN and every
 //        q = v * (1/cap) in [-1, 1] (decided from the two extremes: fl32(v * c)
@@ -16,8 +16,9 @@
 //     2. each pair of logits: softcap (packed fp32 polynomial) -> temperature ->
 //        e = 2^(s * log2e - cc), cc = fl32(m * log2e) -> packed accumulate.
 //   Items with a NaN, an |q| > 1 or a ragged end take an out-of-line general
-//   path (per element g4_tanhf, NaN -> -inf) that rereads the item.  Each item
-//   writes (m, cc, S): 16 bytes per 4 KiB read.
+//   path (per element g4_tanhf, NaN -> -inf) that reads the shared-memory copy
+//   (or global memory for a ragged end).  Each item writes (m, cc, S): 16 bytes
+//   per 2 KiB read.
 // full_combine_kernel: one warp per row.  M = max of the item maxima; item
 //   weights 2^(cc - M * log2e); the index-order prefix of the weighted item sums
 //   locates the item whose mass crosses fl32(u * top_p) * S, and that one item
@@ -34,13 +35,14 @@
 namespace g4s {
 
 constexpr int STREAM_THREADS = 128;  // CTA size of the persistent streaming kernel
-constexpr int NVEC = 8;              // 16-byte vectors per lane per item
+constexpr int NVEC = 4;              // 16-byte vectors per lane per item
+constexpr int STAGES = 3;            // items per warp in the shared-memory ring
 
-// Item geometry: 32 lanes x NVEC vectors x VW logits = 4 KiB.
+// Item geometry: 32 lanes x NVEC vectors x VW logits = 2 KiB.
 template <int DT>
 struct Geo {
     static constexpr int VW = DtypeTraits<DT>::VW;
-    static constexpr int ITEM = 32 * NVEC * VW;  // 2048 (bf16) or 1024 (fp32)
+    static constexpr int ITEM = 32 * NVEC * VW;  // 1024 (bf16) or 512 (fp32)
 };
 
 // Item position of lane-local element (j, k): vector j, component k.
@@ -261,9 +263,46 @@ __device__ __noinline__ float3 slow_item(const void *logits, int64_t row_stride,
     return make_float3(m, cc, S);
 }
 
-// One item of the streaming pass; vec(j) returns this lane's vector j.
+// General path of one item whose lane vectors are in shared memory (the
+// cp.async ring): same arithmetic as slow_item, without rereading global memory.
+template <int DT>
+__device__ __noinline__ float3 slow_item_smem(const uint4 *stage, int n, const SParams sp, bool draw)
+{
+    constexpr int VW = Geo<DT>::VW;
+    const float NEG_INF = -__uint_as_float(0x7f800000u);
+    const int lane = threadIdx.x & 31;
+    float m = NEG_INF;
+#pragma unroll 1
+    for (int j = 0; j < NVEC; j++) {
+        float x[VW];
+        DtypeTraits<DT>::unpack(stage[j * 32 + lane], x);
+#pragma unroll 1
+        for (int k = 0; k < VW; k++)
+            if (item_pos<DT>(j, k, lane) < n) m = fmaxf(m, s_of(x[k], sp));
+    }
+    m = warp_max_nan(m);
+    float cc = 0.0f, S = 0.0f;
+    if (draw && m > NEG_INF) {
+        cc = __fmul_rn(m, G4_L2E);
+#pragma unroll 1
+        for (int j = 0; j < NVEC; j++) {
+            float x[VW];
+            DtypeTraits<DT>::unpack(stage[j * 32 + lane], x);
+#pragma unroll 1
+            for (int k = 0; k < VW; k++)
+                if (item_pos<DT>(j, k, lane) < n) S += ex2_approx(__fmaf_rn(s_of(x[k], sp), G4_L2E, -cc));
+        }
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) S += __shfl_xor_sync(FULLMASK, S, d);
+    }
+    return make_float3(m, cc, S);
+}
+
+// One item of the streaming pass; vec(j) returns this lane's vector j.  stage:
+// the item's shared-memory copy when there is one (else nullptr).
 template <int DT, class Vec>
-__device__ __forceinline__ void stream_item(const SampleArgs &a, int64_t it, int row, int sub, Vec vec)
+__device__ __forceinline__ void stream_item(const SampleArgs &a, int64_t it, int row, int sub, Vec vec,
+                                            const uint4 *stage)
 {
     const float NEG_INF = -__uint_as_float(0x7f800000u);
     const g4s_params p = a.params.get(row);
@@ -283,7 +322,9 @@ __device__ __forceinline__ void stream_item(const SampleArgs &a, int64_t it, int
             for (int d = 16; d > 0; d >>= 1) S += __shfl_xor_sync(FULLMASK, S, d);
         }
     } else {
-        const float3 r = slow_item<DT>(a.logits, a.row_stride, a.vocab, row, sub, sp, draw);
+        // partial copies of a ragged last item are completed from global memory
+        const float3 r = (stage && n == Geo<DT>::ITEM) ? slow_item_smem<DT>(stage, n, sp, draw)
+                                                      : slow_item<DT>(a.logits, a.row_stride, a.vocab, row, sub, sp, draw);
         m = r.x;
         cc = r.y;
         S = r.z;
@@ -302,15 +343,15 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 // Persistent streaming pass.  Warp w handles items w, w + W, w + 2W, ... (W =
 // warps in the grid).  With aligned rows each lane copies its own 16-byte
-// vectors of the next item into a per-warp two-stage shared-memory ring with
-// cp.async (completion tracked by cp.async.wait_group, no polling).
+// vectors of the items two ahead into a per-warp three-stage shared-memory ring
+// with cp.async (completion tracked by cp.async.wait_group, no polling).
 template <int DT, bool VEC>
 __global__ void __launch_bounds__(STREAM_THREADS) full_stream_kernel(SampleArgs a)
 {
     using T = DtypeTraits<DT>;
     constexpr int VW = Geo<DT>::VW, ITEM = Geo<DT>::ITEM;
     constexpr int WPB = STREAM_THREADS / 32;
-    __shared__ uint4 ring[VEC ? WPB * 2 * NVEC * 32 : 1];
+    __shared__ uint4 ring[VEC ? WPB * STAGES * NVEC * 32 : 1];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int ipr = (a.vocab + ITEM - 1) / ITEM;
     const int64_t nitems = (int64_t)a.rows * ipr;
@@ -354,10 +395,10 @@ __global__ void __launch_bounds__(STREAM_THREADS) full_stream_kernel(SampleArgs 
                 }
                 regs[j] = make_uint4(w[0], w[1], w[2], w[3]);
             }
-            stream_item<DT>(a, it, cur.row, cur.sub, [&](int j) { return regs[j]; });
+            stream_item<DT>(a, it, cur.row, cur.sub, [&](int j) { return regs[j]; }, nullptr);
         }
     } else {
-        uint4 *wring = ring + wib * 2 * NVEC * 32;
+        uint4 *wring = ring + wib * STAGES * NVEC * 32;
         // copies of a partial last item stop at the last whole vector; such items
         // take the general path, which rereads them
         auto issue = [&](int64_t i, const Cursor &c, int stage) {
@@ -372,19 +413,26 @@ __global__ void __launch_bounds__(STREAM_THREADS) full_stream_kernel(SampleArgs 
             }
         };
         Cursor nxt = cur;
-        issue(it0, nxt, 0);
-        cp_async_commit();
-        advance(nxt);
-        int stage = 0;
-        for (int64_t it = it0; it < nitems; it += nw) {
-            issue(it + nw, nxt, stage ^ 1);  // the other stage was consumed last iteration
+#pragma unroll
+        for (int st = 0; st < STAGES - 1; st++) {
+            issue(it0 + st * nw, nxt, st);
             cp_async_commit();
             advance(nxt);
-            cp_async_wait<1>();  // this lane's copies of item `it` have landed
+        }
+        int stage = 0;
+        for (int64_t it = it0; it < nitems; it += nw) {
+            // refill the stage consumed last iteration with the item STAGES-1 ahead
+            issue(it + (STAGES - 1) * nw, nxt, stage == 0 ? STAGES - 1 : stage - 1);
+            cp_async_commit();
+            advance(nxt);
+            cp_async_wait<STAGES - 1>();  // this lane's copies of item `it` have landed
             const uint4 *src = wring + stage * NVEC * 32;
-            stream_item<DT>(a, it, cur.row, cur.sub, [&](int j) { return src[j * 32 + lane]; });
+            uint4 regs[NVEC];
+#pragma unroll
+            for (int j = 0; j < NVEC; j++) regs[j] = src[j * 32 + lane];
+            stream_item<DT>(a, it, cur.row, cur.sub, [&](int j) { return regs[j]; }, src);
             advance(cur);
-            stage ^= 1;
+            stage = stage + 1 == STAGES ? 0 : stage + 1;
         }
         cp_async_wait<0>();
     }
@@ -401,30 +449,59 @@ __device__ __forceinline__ double pow2_split(double d)
     return (double)ex2_approx(f) * scale;
 }
 
-// s of the element at item position e (for the rescans), -inf past n.
-template <int DT>
-__device__ __forceinline__ float elem_s(const char *rowp, int64_t base, int e, int n, const SParams &sp)
-{
-    return e < n ? s_of(load_elem<DT>(rowp, base + e), sp) : -__uint_as_float(0x7f800000u);
-}
-
-// First id of the row's item `sub` whose s equals M (warp-uniform result).
-template <int DT>
-__device__ int item_argmax(const SampleArgs &a, int row, int sub, const SParams &sp, float M)
+// This lane's NVEC vectors of item `sub`, all loads issued before any use
+// (positions past n are unspecified; callers check e < n).
+template <int DT, bool VEC>
+__device__ __forceinline__ void lane_vectors(const SampleArgs &a, int row, int sub, uint4 *r)
 {
     using T = DtypeTraits<DT>;
     constexpr int VW = Geo<DT>::VW;
     const int lane = threadIdx.x & 31;
     const int n = item_len<DT>(a.vocab, sub);
-    const char *rowp = (const char *)a.logits + (int64_t)row * a.row_stride * T::ESIZE;
-    const int64_t base = (int64_t)sub * Geo<DT>::ITEM;
+    const char *src = (const char *)a.logits + ((int64_t)row * a.row_stride + (int64_t)sub * Geo<DT>::ITEM) * T::ESIZE;
+#pragma unroll
+    for (int j = 0; j < NVEC; j++) {
+        const int e0 = item_pos<DT>(j, 0, lane);
+        if (VEC && e0 + VW <= n) {
+            r[j] = __ldcg((const uint4 *)(src + (int64_t)e0 * T::ESIZE));
+        } else {
+            uint32_t w[4];
+            if constexpr (DT == G4S_F32) {
+#pragma unroll
+                for (int k = 0; k < 4; k++) w[k] = e0 + k < n ? __float_as_uint(__ldg((const float *)src + e0 + k)) : 0u;
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const uint32_t lo = e0 + 2 * k < n ? __ldg((const unsigned short *)src + e0 + 2 * k) : 0u;
+                    const uint32_t hi = e0 + 2 * k + 1 < n ? __ldg((const unsigned short *)src + e0 + 2 * k + 1) : 0u;
+                    w[k] = lo | (hi << 16);
+                }
+            }
+            r[j] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+}
+
+// First id of the row's item `sub` whose s equals M (warp-uniform result).
+template <int DT, bool VEC>
+__device__ int item_argmax(const SampleArgs &a, int row, int sub, const SParams &sp, float M)
+{
+    constexpr int VW = Geo<DT>::VW;
+    const int lane = threadIdx.x & 31;
+    const int n = item_len<DT>(a.vocab, sub);
+    uint4 r[NVEC];
+    lane_vectors<DT, VEC>(a, row, sub, r);
     unsigned best = 0xffffffffu;
-    for (int j = 0; j < NVEC; j++)
+#pragma unroll
+    for (int j = 0; j < NVEC; j++) {
+        float x[VW];
+        DtypeTraits<DT>::unpack(r[j], x);
 #pragma unroll
         for (int k = 0; k < VW; k++) {
             const int e = item_pos<DT>(j, k, lane);
-            if (elem_s<DT>(rowp, base, e, n, sp) == M && (unsigned)e < best) best = (unsigned)e;
+            if (e < n && s_of(x[k], sp) == M && (unsigned)e < best) best = (unsigned)e;
         }
+    }
     best = __reduce_min_sync(FULLMASK, best);
     return sub * Geo<DT>::ITEM + (best == 0xffffffffu ? 0 : (int)best);
 }
@@ -518,18 +595,21 @@ __global__ void __launch_bounds__(128) full_combine_kernel(SampleArgs a)
             const float cc = st[hit_item].y;
             const double tloc = (target - ibase) / iw;
             const int n = item_len<DT>(a.vocab, hit_item);
-            const char *rowp = (const char *)a.logits + (int64_t)row * a.row_stride * T::ESIZE;
-            const int64_t ib = (int64_t)hit_item * ITEM;
+            uint4 rv[NVEC];
+            lane_vectors<DT, VEC>(a, row, hit_item, rv);
             double run = 0.0;
             int pos = -1, last = -1;
             float etok = 0.0f, elast = 0.0f;
-            for (int j = 0; j < NVEC && pos < 0; j++) {
+#pragma unroll
+            for (int j = 0; j < NVEC; j++) {
+                if (pos >= 0) break;
                 float ev[VW];
+                DtypeTraits<DT>::unpack(rv[j], ev);
                 double lsum = 0.0;
 #pragma unroll
                 for (int k = 0; k < VW; k++) {
                     const int e = item_pos<DT>(j, k, lane);
-                    ev[k] = e < n ? ex2_approx(__fmaf_rn(elem_s<DT>(rowp, ib, e, n, sp), G4_L2E, -cc)) : 0.0f;
+                    ev[k] = e < n ? ex2_approx(__fmaf_rn(s_of(ev[k], sp), G4_L2E, -cc)) : 0.0f;
                     lsum += (double)ev[k];
                 }
                 double lincl = lsum;
@@ -567,7 +647,7 @@ __global__ void __launch_bounds__(128) full_combine_kernel(SampleArgs a)
         }
     }
     if (need_argmax) {
-        token = item_argmax<DT>(a, row, mi, sp, M);
+        token = item_argmax<DT, VEC>(a, row, mi, sp, M);
         if (draw) {
             const float4 q = st[mi];
             const double w = pow2_split((double)q.y - (double)M * (double)G4_L2E);
@@ -605,19 +685,24 @@ __global__ void __launch_bounds__(NTHREADS) full_probs_kernel(SampleArgs a)
     const float4 q = a.istat[it];
     const SParams sp = make_sparams(a, p, row);
     const int n = item_len<DT>(a.vocab, sub);
-    const char *rowp = (const char *)a.logits + (int64_t)row * a.row_stride * T::ESIZE;
     const int64_t ib = (int64_t)sub * ITEM;
     const bool live = q.x > -__uint_as_float(0x7f800000u);
     const double w = live ? pow2_split((double)q.y - (double)rs.M * (double)G4_L2E) : 0.0;
-    for (int j = 0; j < NVEC; j++)
+    uint4 r[NVEC];
+    lane_vectors<DT, false>(a, row, sub, r);
+#pragma unroll
+    for (int j = 0; j < NVEC; j++) {
+        float x[VW];
+        DtypeTraits<DT>::unpack(r[j], x);
 #pragma unroll
         for (int k = 0; k < VW; k++) {
             const int e = item_pos<DT>(j, k, lane);
             if (e < n) {
-                const float ev = live ? ex2_approx(__fmaf_rn(elem_s<DT>(rowp, ib, e, n, sp), G4_L2E, -q.y)) : 0.0f;
+                const float ev = live ? ex2_approx(__fmaf_rn(s_of(x[k], sp), G4_L2E, -q.y)) : 0.0f;
                 a.full_probs[(int64_t)row * a.vocab + ib + e] = (float)((double)ev * w / rs.S);
             }
         }
+    }
 }
 
 template <int DT, bool VEC>
