@@ -544,47 +544,65 @@ __global__ void __launch_bounds__(128) full_combine_kernel(SampleArgs a)
         token = 0;  // every value is -inf (softcap disabled): the reference's NaN arithmetic ends at id 0
         need_argmax = false;
     } else if (draw) {
+        // weighted item sums P_i = S_i * 2^(cc_i - M * log2e); lane l holds the
+        // CI consecutive items [CI*l, CI*l + CI) of each block of 32*CI items
+        constexpr int CI = 8;
         const double Ml = (double)M * (double)G4_L2E;
-        for (int r0 = 0; r0 < ipr; r0 += 32) {
-            const int i = r0 + lane;
-            double P = 0.0;
-            if (i < ipr) {
-                const float4 q = st[i];
-                if (q.x > NEG_INF) P = (double)q.z * pow2_split((double)q.y - Ml);
-            }
+        auto item_P = [&](int i, double &w) -> double {
+            w = 0.0;
+            if (i >= ipr) return 0.0;
+            const float4 q = st[i];
+            if (!(q.x > NEG_INF)) return 0.0;
+            w = pow2_split((double)q.y - Ml);
+            return (double)q.z * w;
+        };
+        for (int b0 = 0; b0 < ipr; b0 += 32 * CI) {
+            double ls = 0.0, w;
 #pragma unroll
-            for (int d = 16; d > 0; d >>= 1) P += __shfl_xor_sync(FULLMASK, P, d);
-            S += P;
+            for (int c = 0; c < CI; c++) ls += item_P(b0 + lane * CI + c, w);
+#pragma unroll
+            for (int d = 16; d > 0; d >>= 1) ls += __shfl_xor_sync(FULLMASK, ls, d);
+            S += ls;
         }
         const float thr = __double2float_rn(a.u[row] * (double)p.top_p);
         const double target = (double)thr * S;
-        // the item whose cumulative mass reaches the target
+        // the first item whose inclusive prefix reaches the target
         double base = 0.0, ibase = 0.0, iw = 0.0;
         int hit_item = -1;
-        for (int r0 = 0; r0 < ipr && hit_item < 0; r0 += 32) {
-            const int i = r0 + lane;
-            double P = 0.0, w = 0.0;
-            if (i < ipr) {
-                const float4 q = st[i];
-                if (q.x > NEG_INF) {
-                    w = pow2_split((double)q.y - Ml);
-                    P = (double)q.z * w;
-                }
+        for (int b0 = 0; b0 < ipr && hit_item < 0; b0 += 32 * CI) {
+            double P[CI], W[CI], ls = 0.0;
+#pragma unroll
+            for (int c = 0; c < CI; c++) {
+                P[c] = item_P(b0 + lane * CI + c, W[c]);
+                ls += P[c];
             }
-            double incl = P;
+            double lincl = ls;
 #pragma unroll
             for (int d = 1; d < 32; d <<= 1) {
-                const double o = __shfl_up_sync(FULLMASK, incl, d);
-                if (lane >= d) incl += o;
+                const double o = __shfl_up_sync(FULLMASK, lincl, d);
+                if (lane >= d) lincl += o;
             }
-            const unsigned hit = __ballot_sync(FULLMASK, i < ipr && base + incl >= target);
+            double run = base + lincl - ls;
+            int found = -1;
+            double fbase = 0.0, fw = 0.0;
+#pragma unroll
+            for (int c = 0; c < CI; c++) {
+                const bool in = b0 + lane * CI + c < ipr;
+                if (found < 0 && in && run + P[c] >= target) {
+                    found = b0 + lane * CI + c;
+                    fbase = run;
+                    fw = W[c];
+                }
+                run += P[c];
+            }
+            const unsigned hit = __ballot_sync(FULLMASK, found >= 0);
             if (hit) {
                 const int L = __ffs(hit) - 1;
-                hit_item = r0 + L;
-                ibase = __shfl_sync(FULLMASK, base + incl - P, L);
-                iw = __shfl_sync(FULLMASK, w, L);
+                hit_item = __shfl_sync(FULLMASK, found, L);
+                ibase = __shfl_sync(FULLMASK, fbase, L);
+                iw = __shfl_sync(FULLMASK, fw, L);
             }
-            base += __shfl_sync(FULLMASK, incl, 31);
+            base += __shfl_sync(FULLMASK, lincl, 31);
         }
         if (hit_item < 0) {
             flags |= G4S_ROW_FALLBACK;
