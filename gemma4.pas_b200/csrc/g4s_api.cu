@@ -2,6 +2,8 @@
 // kernel launches.  See include/g4sampler.h for the contract.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -180,7 +182,8 @@ int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t
     const size_t o_cand = off; off = align(off + (size_t)lists * KMAX_ * sizeof(uint64_t));
     const size_t o_cnt = off; off = align(off + (size_t)lists * sizeof(int32_t));
     const size_t o_ct = off; off = align(off + (size_t)max_rows * sizeof(uint32_t));
-    const int64_t items = (int64_t)max_rows * ceil_div(max_vocab, 1024);  // items of >= 1024 logits
+    const int64_t item_min = std::min(full_item_logits(G4S_F32), full_item_logits(G4S_BF16));
+    const int64_t items = (int64_t)max_rows * ceil_div(max_vocab, item_min);
     const size_t o_st = off; off = align(off + (size_t)items * sizeof(float4));
     const size_t o_rs = off; off = align(off + (size_t)max_rows * sizeof(RowStat));
     const size_t o_li = off; off = align(off + (size_t)LK_SLOTS * max_vocab * sizeof(int32_t));

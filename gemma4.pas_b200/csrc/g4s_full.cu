@@ -5,26 +5,27 @@
 //
 // full_stream_kernel: persistent, independent warps (no block barriers, no
 //   fences).  A warp item is 2 KiB of one row (1024 bf16 or 512 fp32 logits);
-//   each lane copies its own four 16-byte vectors of the items two ahead into a
-//   per-warp three-stage shared-memory ring with cp.async, and processes the
+//   each lane copies its own four 16-byte vectors of the items two ahead into
+//   a per-warp three-stage shared-memory ring with cp.async, and processes the
 //   current item from registers in two passes:
-//     1. NaN-propagating min/max of the raw logits (packed bf16x2 or 3-input
-//        fp32 min/max), reduced over the warp.  With no NaN and every
-//        q = v * (1/cap) in [-1, 1] (decided from the two extremes: fl32(v * c)
-//        is monotone in v) the item maximum is s(max v), softcap and
-//        temperature being monotone;
+//     1. NaN-propagating min/max of the lane's raw logits (packed bf16x2 or
+//        3-input fp32 min/max).  Each lane tests its own extremes (no NaN, every
+//        q = v * (1/cap) in [-1, 1]: fl32(v * c) is monotone in v) and one vote
+//        decides the item; the item maximum is then s(max v) (softcap and
+//        temperature are monotone), max v from one redux.sync;
 //     2. each pair of logits: softcap (packed fp32 polynomial) -> temperature ->
 //        e = 2^(s * log2e - cc), cc = fl32(m * log2e) -> packed accumulate.
 //   Items with a NaN, an |q| > 1 or a ragged end take an out-of-line general
 //   path (per element g4_tanhf, NaN -> -inf) that reads the shared-memory copy
 //   (or global memory for a ragged end).  Each item writes (m, cc, S): 16 bytes
 //   per 2 KiB read.
-// full_combine_kernel: one warp per row.  M = max of the item maxima; item
-//   weights 2^(cc - M * log2e); the index-order prefix of the weighted item sums
-//   locates the item whose mass crosses fl32(u * top_p) * S, and that one item
-//   is rescanned element by element with the identical per-element arithmetic
-//   to pick the first id whose cumulative sum reaches the threshold.  Greedy
-//   rows and the argmax fallback rescan the first item holding M.
+// full_combine_kernel: one 256-thread CTA per row.  M = max of the item maxima;
+//   item weights 2^(cc - M * log2e); a block scan of the weighted item sums in
+//   index order locates the item whose mass crosses fl32(u * top_p) * S, and
+//   that one item is rescanned element by element (one 16-byte vector per
+//   thread, a second block scan) with the identical per-element arithmetic to
+//   pick the first id whose cumulative sum reaches the threshold.  Greedy rows
+//   and the argmax fallback rescan the first item holding M.
 //
 // The reference's serial fp32 sums drift by ~3e-4 over 262144 terms; this path
 // matches the fp64 restatement of the reference (same fp32 per-element values,
@@ -35,14 +36,20 @@
 namespace g4s {
 
 constexpr int STREAM_THREADS = 128;  // CTA size of the persistent streaming kernel
-constexpr int NVEC = 4;              // 16-byte vectors per lane per item
-constexpr int STAGES = 3;            // items per warp in the shared-memory ring
+#ifndef G4S_FULL_NVEC
+#define G4S_FULL_NVEC 4
+#endif
+#ifndef G4S_FULL_STAGES
+#define G4S_FULL_STAGES 3
+#endif
+constexpr int NVEC = G4S_FULL_NVEC;      // 16-byte vectors per lane per item
+constexpr int STAGES = G4S_FULL_STAGES;  // items per warp in the shared-memory ring
 
-// Item geometry: 32 lanes x NVEC vectors x VW logits = 2 KiB.
+// Item geometry: 32 lanes x NVEC vectors x VW logits (2 KiB at NVEC 4).
 template <int DT>
 struct Geo {
     static constexpr int VW = DtypeTraits<DT>::VW;
-    static constexpr int ITEM = 32 * NVEC * VW;  // 1024 (bf16) or 512 (fp32)
+    static constexpr int ITEM = 32 * NVEC * VW;  // 1024 (bf16) or 512 (fp32) at NVEC 4
 };
 
 // Item position of lane-local element (j, k): vector j, component k.
@@ -123,11 +130,12 @@ __device__ __forceinline__ float warp_max_nan(float v)
     for (int d = 16; d > 0; d >>= 1) v = fmax_nan(v, __shfl_xor_sync(FULLMASK, v, d));
     return v;
 }
-__device__ __forceinline__ float warp_min_nan(float v)
+// Warp maximum of non-NaN floats in one instruction (sm_100a).
+__device__ __forceinline__ float warp_max_redux(float v)
 {
-#pragma unroll
-    for (int d = 16; d > 0; d >>= 1) v = fmin_nan(v, __shfl_xor_sync(FULLMASK, v, d));
-    return v;
+    float r;
+    asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+    return r;
 }
 
 // Item `sub` of a row holds n = min(ITEM, vocab - sub * ITEM) logits.
@@ -144,7 +152,8 @@ __device__ __forceinline__ float load_elem(const void *rowp, int64_t i)
 }
 
 // Pass 1: warp-uniform fast-path decision and the raw item maximum.  vec(j)
-// returns this lane's vector j.
+// returns this lane's vector j.  Each lane tests its own extremes; one vote
+// decides the item.
 template <int DT, class Vec>
 __device__ __forceinline__ bool item_fast(Vec vec, const SParams &sp, float &xmax)
 {
@@ -178,17 +187,18 @@ __device__ __forceinline__ bool item_fast(Vec vec, const SParams &sp, float &xma
         mx = a;
         mn = b;
     }
-    mx = warp_max_nan(mx);
-    mn = warp_min_nan(mn);
-    xmax = mx;
-    if (mx != mx || mn != mn) return false;  // NaN present
-    if (!sp.use_cap) return true;
-    return fabsf(__fmul_rn(mx, sp.invcap)) <= 1.0f && fabsf(__fmul_rn(mn, sp.invcap)) <= 1.0f;
+    // NaN fails every comparison below
+    const bool ok = sp.use_cap ? (fabsf(__fmul_rn(mx, sp.invcap)) <= 1.0f && fabsf(__fmul_rn(mn, sp.invcap)) <= 1.0f)
+                               : (mx == mx && mn == mn);
+    const bool fast = __all_sync(FULLMASK, ok);
+    xmax = warp_max_redux(mx);  // used only when fast (no NaN in the item)
+    return fast;
 }
 
 // Pass 2 of the fast path: each pair of logits goes softcap -> temperature ->
-// exponent -> accumulate.  Returns the lane's sum of e.
-template <int DT, bool CAP, bool TEMP, class Vec>
+// exponent -> accumulate.  Returns the lane's sum of e.  ROLLED: vec(j) is a
+// cheap shared-memory read, so the vector loop stays rolled (small code).
+template <int DT, bool CAP, bool TEMP, bool ROLLED, class Vec>
 __device__ __forceinline__ float fast_exp_sum(Vec vec, const SParams &sp, float cc)
 {
     constexpr int VW = Geo<DT>::VW;
@@ -196,10 +206,9 @@ __device__ __forceinline__ float fast_exp_sum(Vec vec, const SParams &sp, float 
     const float2 t2 = make_float2(sp.invT, sp.invT);
     const float2 l2 = make_float2(G4_L2E, G4_L2E), nc = make_float2(-cc, -cc);
     float2 acc0 = make_float2(0.0f, 0.0f), acc1 = acc0;
-#pragma unroll
-    for (int j = 0; j < NVEC; j++) {
+    auto body = [&](uint4 w) {
         float x[VW];
-        DtypeTraits<DT>::unpack(vec(j), x);
+        DtypeTraits<DT>::unpack(w, x);
 #pragma unroll
         for (int k = 0; k < VW; k += 2) {
             float2 v = make_float2(x[k], x[k + 1]);
@@ -210,17 +219,24 @@ __device__ __forceinline__ float fast_exp_sum(Vec vec, const SParams &sp, float 
             if ((k >> 1) & 1) acc1 = __fadd2_rn(acc1, e);
             else acc0 = __fadd2_rn(acc0, e);
         }
+    };
+    if constexpr (ROLLED) {
+#pragma unroll 1
+        for (int j = 0; j < NVEC; j++) body(vec(j));
+    } else {
+#pragma unroll
+        for (int j = 0; j < NVEC; j++) body(vec(j));
     }
     acc0 = __fadd2_rn(acc0, acc1);
     return acc0.x + acc0.y;
 }
 
-template <int DT, class Vec>
+template <int DT, bool ROLLED, class Vec>
 __device__ __forceinline__ float fast_exp_sum_any(Vec vec, const SParams &sp, float cc)
 {
     if (sp.use_cap)
-        return sp.use_t ? fast_exp_sum<DT, true, true>(vec, sp, cc) : fast_exp_sum<DT, true, false>(vec, sp, cc);
-    return sp.use_t ? fast_exp_sum<DT, false, true>(vec, sp, cc) : fast_exp_sum<DT, false, false>(vec, sp, cc);
+        return sp.use_t ? fast_exp_sum<DT, true, true, ROLLED>(vec, sp, cc) : fast_exp_sum<DT, true, false, ROLLED>(vec, sp, cc);
+    return sp.use_t ? fast_exp_sum<DT, false, true, ROLLED>(vec, sp, cc) : fast_exp_sum<DT, false, false, ROLLED>(vec, sp, cc);
 }
 
 // General path of one item (NaN present, |q| > 1 somewhere, or a ragged last
@@ -300,7 +316,7 @@ __device__ __noinline__ float3 slow_item_smem(const uint4 *stage, int n, const S
 
 // One item of the streaming pass; vec(j) returns this lane's vector j.  stage:
 // the item's shared-memory copy when there is one (else nullptr).
-template <int DT, class Vec>
+template <int DT, bool ROLLED, class Vec>
 __device__ __forceinline__ void stream_item(const SampleArgs &a, int64_t it, int row, int sub, Vec vec,
                                             const uint4 *stage)
 {
@@ -317,7 +333,7 @@ __device__ __forceinline__ void stream_item(const SampleArgs &a, int64_t it, int
         m = s_of(xmax, sp);  // softcap and temperature are monotone
         if (draw && m > NEG_INF) {
             cc = __fmul_rn(m, G4_L2E);
-            S = fast_exp_sum_any<DT>(vec, sp, cc);
+            S = fast_exp_sum_any<DT, ROLLED>(vec, sp, cc);
 #pragma unroll
             for (int d = 16; d > 0; d >>= 1) S += __shfl_xor_sync(FULLMASK, S, d);
         }
@@ -346,7 +362,7 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // vectors of the items two ahead into a per-warp three-stage shared-memory ring
 // with cp.async (completion tracked by cp.async.wait_group, no polling).
 template <int DT, bool VEC>
-__global__ void __launch_bounds__(STREAM_THREADS) full_stream_kernel(SampleArgs a)
+__global__ void __launch_bounds__(STREAM_THREADS, 4) full_stream_kernel(SampleArgs a)
 {
     using T = DtypeTraits<DT>;
     constexpr int VW = Geo<DT>::VW, ITEM = Geo<DT>::ITEM;
@@ -395,7 +411,7 @@ __global__ void __launch_bounds__(STREAM_THREADS) full_stream_kernel(SampleArgs 
                 }
                 regs[j] = make_uint4(w[0], w[1], w[2], w[3]);
             }
-            stream_item<DT>(a, it, cur.row, cur.sub, [&](int j) { return regs[j]; }, nullptr);
+            stream_item<DT, false>(a, it, cur.row, cur.sub, [&](int j) { return regs[j]; }, nullptr);
         }
     } else {
         uint4 *wring = ring + wib * STAGES * NVEC * 32;
@@ -427,10 +443,7 @@ __global__ void __launch_bounds__(STREAM_THREADS) full_stream_kernel(SampleArgs 
             advance(nxt);
             cp_async_wait<STAGES - 1>();  // this lane's copies of item `it` have landed
             const uint4 *src = wring + stage * NVEC * 32;
-            uint4 regs[NVEC];
-#pragma unroll
-            for (int j = 0; j < NVEC; j++) regs[j] = src[j * 32 + lane];
-            stream_item<DT>(a, it, cur.row, cur.sub, [&](int j) { return regs[j]; }, src);
+            stream_item<DT, true>(a, it, cur.row, cur.sub, [&](int j) { return src[j * 32 + lane]; }, src);
             advance(cur);
             stage = stage + 1 == STAGES ? 0 : stage + 1;
         }
@@ -482,58 +495,153 @@ __device__ __forceinline__ void lane_vectors(const SampleArgs &a, int row, int s
     }
 }
 
-// First id of the row's item `sub` whose s equals M (warp-uniform result).
-template <int DT, bool VEC>
-__device__ int item_argmax(const SampleArgs &a, int row, int sub, const SParams &sp, float M)
+// ---------------------------------------------------------------------------
+// block primitives of the combine (one row per CTA of COMBINE_THREADS)
+// ---------------------------------------------------------------------------
+constexpr int COMBINE_THREADS = 256;
+constexpr int CWARPS = COMBINE_THREADS / 32;
+
+struct CombineSmem {
+    double d[CWARPS];
+    float f[CWARPS];
+    int i[CWARPS];
+    double hit_base, hit_w;
+    float etok;
+};
+
+// Block maximum of (m, idx), lower idx on ties; every thread gets the result.
+__device__ __forceinline__ void block_argmax_first(float &m, int &idx, CombineSmem &sm)
 {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) {
+        const float om = __shfl_xor_sync(FULLMASK, m, d);
+        const int oi = __shfl_xor_sync(FULLMASK, idx, d);
+        if (om > m || (om == m && oi < idx)) { m = om; idx = oi; }
+    }
+    if (lane == 0) { sm.f[w] = m; sm.i[w] = idx; }
+    __syncthreads();
+    m = sm.f[0];
+    idx = sm.i[0];
+#pragma unroll
+    for (int k = 1; k < CWARPS; k++)
+        if (sm.f[k] > m || (sm.f[k] == m && sm.i[k] < idx)) { m = sm.f[k]; idx = sm.i[k]; }
+    __syncthreads();
+}
+
+__device__ __forceinline__ int block_min_int(int v, CombineSmem &sm)
+{
+    const int w = threadIdx.x >> 5;
+    v = __reduce_min_sync(FULLMASK, v);
+    if ((threadIdx.x & 31) == 0) sm.i[w] = v;
+    __syncthreads();
+    v = sm.i[0];
+#pragma unroll
+    for (int k = 1; k < CWARPS; k++) v = min(v, sm.i[k]);
+    __syncthreads();
+    return v;
+}
+
+__device__ __forceinline__ int block_max_int(int v, CombineSmem &sm)
+{
+    const int w = threadIdx.x >> 5;
+    v = __reduce_max_sync(FULLMASK, v);
+    if ((threadIdx.x & 31) == 0) sm.i[w] = v;
+    __syncthreads();
+    v = sm.i[0];
+#pragma unroll
+    for (int k = 1; k < CWARPS; k++) v = max(v, sm.i[k]);
+    __syncthreads();
+    return v;
+}
+
+// Inclusive block scan of doubles in thread order.  Returns the inclusive
+// prefix; *prev gets the previous thread's inclusive prefix (0 for thread 0)
+// and *total the last thread's, bit for bit, so the prefixes are monotone and
+// the last one equals the total.
+__device__ __forceinline__ double block_incl_scan_d(double v, double *prev, double *total, CombineSmem &sm)
+{
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    double incl = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const double o = __shfl_up_sync(FULLMASK, incl, d);
+        if (lane >= d) incl += o;
+    }
+    double up = __shfl_up_sync(FULLMASK, incl, 1);
+    if (lane == 31) sm.d[w] = incl;
+    __syncthreads();
+    double acc = 0.0, base = 0.0;
+#pragma unroll
+    for (int k = 0; k < CWARPS; k++) {
+        if (k == w) base = acc;
+        acc += sm.d[k];
+    }
+    __syncthreads();
+    // warp w's first inclusive prefix is base + incl; base + up reproduces the
+    // previous lane's (warp-local prefixes are exact partial sums of the same
+    // additions), and lane 0 follows the last lane of warp w - 1, whose
+    // inclusive prefix is base itself.
+    incl = w == 0 ? incl : base + incl;
+    up = w == 0 ? up : base + up;
+    *prev = lane == 0 ? base : up;
+    *total = acc;
+    return incl;
+}
+
+// This thread's 16-byte vector t of item `sub` (positions t*VW .. t*VW+VW-1 of
+// the item; positions past n are unspecified, callers check them).
+template <int DT, bool VEC>
+__device__ __forceinline__ uint4 item_vector(const SampleArgs &a, int row, int sub, int t)
+{
+    using T = DtypeTraits<DT>;
     constexpr int VW = Geo<DT>::VW;
-    const int lane = threadIdx.x & 31;
     const int n = item_len<DT>(a.vocab, sub);
-    uint4 r[NVEC];
-    lane_vectors<DT, VEC>(a, row, sub, r);
-    unsigned best = 0xffffffffu;
+    const char *src = (const char *)a.logits + ((int64_t)row * a.row_stride + (int64_t)sub * Geo<DT>::ITEM) * T::ESIZE;
+    const int e0 = t * VW;
+    if (VEC && e0 + VW <= n) return __ldcg((const uint4 *)(src + (int64_t)e0 * T::ESIZE));
+    uint32_t w[4];
+    if constexpr (DT == G4S_F32) {
 #pragma unroll
-    for (int j = 0; j < NVEC; j++) {
-        float x[VW];
-        DtypeTraits<DT>::unpack(r[j], x);
+        for (int k = 0; k < 4; k++) w[k] = e0 + k < n ? __float_as_uint(__ldg((const float *)src + e0 + k)) : 0u;
+    } else {
 #pragma unroll
-        for (int k = 0; k < VW; k++) {
-            const int e = item_pos<DT>(j, k, lane);
-            if (e < n && s_of(x[k], sp) == M && (unsigned)e < best) best = (unsigned)e;
+        for (int k = 0; k < 4; k++) {
+            const uint32_t lo = e0 + 2 * k < n ? __ldg((const unsigned short *)src + e0 + 2 * k) : 0u;
+            const uint32_t hi = e0 + 2 * k + 1 < n ? __ldg((const unsigned short *)src + e0 + 2 * k + 1) : 0u;
+            w[k] = lo | (hi << 16);
         }
     }
-    best = __reduce_min_sync(FULLMASK, best);
-    return sub * Geo<DT>::ITEM + (best == 0xffffffffu ? 0 : (int)best);
+    return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 template <int DT, bool VEC>
-__global__ void __launch_bounds__(128) full_combine_kernel(SampleArgs a)
+__global__ void __launch_bounds__(COMBINE_THREADS) full_combine_kernel(SampleArgs a)
 {
-    using T = DtypeTraits<DT>;
-    constexpr int VW = Geo<DT>::VW, ITEM = Geo<DT>::ITEM;
-    const int lane = threadIdx.x & 31;
-    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (row >= a.rows) return;
+    constexpr int VW = Geo<DT>::VW, ITEM = Geo<DT>::ITEM, CT = COMBINE_THREADS;
+    constexpr int IV = NVEC * 32;  // vectors per item: one per thread in the rescans
+    static_assert(IV <= CT, "an item rescan takes one vector per thread");
+    __shared__ CombineSmem sm;
+    const int t = threadIdx.x;
+    const int row = blockIdx.x;
     const g4s_params p = a.params.get(row);
-    if (!(p.top_k <= 0 || p.top_k >= a.vocab)) return;
+    if (!(p.top_k <= 0 || p.top_k >= a.vocab)) return;  // uniform over the CTA
     const SParams sp = make_sparams(a, p, row);
     const int ipr = (a.vocab + ITEM - 1) / ITEM;
     const float4 *st = a.istat + (int64_t)row * ipr;
     const float NEG_INF = -__uint_as_float(0x7f800000u);
+    const float4 none = make_float4(NEG_INF, 0.0f, 0.0f, 0.0f);
 
     // row maximum and the first item holding it
-    float M = NEG_INF;
-    int mi = 0x7fffffff;
-    for (int i = lane; i < ipr; i += 32) {
+    const float4 q0 = t < ipr ? st[t] : none;
+    float M = q0.x;
+    int mi = t < ipr ? t : 0x7fffffff;
+    for (int i = t + CT; i < ipr; i += CT) {
         const float m = st[i].x;
         if (m > M) { M = m; mi = i; }
     }
-#pragma unroll
-    for (int d = 16; d > 0; d >>= 1) {
-        const float om = __shfl_xor_sync(FULLMASK, M, d);
-        const int oi = __shfl_xor_sync(FULLMASK, mi, d);
-        if (om > M || (om == M && oi < mi)) { M = om; mi = oi; }
-    }
+    block_argmax_first(M, mi, sm);
+
     const bool draw = p.temperature > 0.0f;
     int32_t flags = G4S_ROW_FULL_PATH | (draw ? 0 : G4S_ROW_GREEDY);
     int token = -1;
@@ -544,135 +652,113 @@ __global__ void __launch_bounds__(128) full_combine_kernel(SampleArgs a)
         token = 0;  // every value is -inf (softcap disabled): the reference's NaN arithmetic ends at id 0
         need_argmax = false;
     } else if (draw) {
-        // weighted item sums P_i = S_i * 2^(cc_i - M * log2e); lane l holds the
-        // CI consecutive items [CI*l, CI*l + CI) of each block of 32*CI items
-        constexpr int CI = 8;
+        // weighted item sums P_i = S_i * 2^(cc_i - M * log2e), scanned in item order
         const double Ml = (double)M * (double)G4_L2E;
-        auto item_P = [&](int i, double &w) -> double {
+        auto item_P = [&](const float4 &q, double &w) -> double {
             w = 0.0;
-            if (i >= ipr) return 0.0;
-            const float4 q = st[i];
             if (!(q.x > NEG_INF)) return 0.0;
             w = pow2_split((double)q.y - Ml);
             return (double)q.z * w;
         };
-        for (int b0 = 0; b0 < ipr; b0 += 32 * CI) {
-            double ls = 0.0, w;
-#pragma unroll
-            for (int c = 0; c < CI; c++) ls += item_P(b0 + lane * CI + c, w);
-#pragma unroll
-            for (int d = 16; d > 0; d >>= 1) ls += __shfl_xor_sync(FULLMASK, ls, d);
-            S += ls;
-        }
         const float thr = __double2float_rn(a.u[row] * (double)p.top_p);
-        const double target = (double)thr * S;
-        // the first item whose inclusive prefix reaches the target
-        double base = 0.0, ibase = 0.0, iw = 0.0;
-        int hit_item = -1;
-        for (int b0 = 0; b0 < ipr && hit_item < 0; b0 += 32 * CI) {
-            double P[CI], W[CI], ls = 0.0;
-#pragma unroll
-            for (int c = 0; c < CI; c++) {
-                P[c] = item_P(b0 + lane * CI + c, W[c]);
-                ls += P[c];
+        int hit = 0x7fffffff;
+        double target;
+        if (ipr <= CT) {
+            double w, prev;
+            const double P = item_P(q0, w);
+            const double incl = block_incl_scan_d(P, &prev, &S, sm);
+            target = (double)thr * S;
+            hit = block_min_int(t < ipr && incl >= target ? t : 0x7fffffff, sm);
+            if (t == hit) { sm.hit_base = prev; sm.hit_w = w; }
+        } else {
+            for (int b0 = 0; b0 < ipr; b0 += CT) {
+                double w, prev, tot;
+                const int i = b0 + t;
+                block_incl_scan_d(item_P(i < ipr ? st[i] : none, w), &prev, &tot, sm);
+                S += tot;
             }
-            double lincl = ls;
-#pragma unroll
-            for (int d = 1; d < 32; d <<= 1) {
-                const double o = __shfl_up_sync(FULLMASK, lincl, d);
-                if (lane >= d) lincl += o;
+            target = (double)thr * S;
+            double base = 0.0;
+            for (int b0 = 0; b0 < ipr && hit == 0x7fffffff; b0 += CT) {
+                double w, prev, tot;
+                const int i = b0 + t;
+                const double incl = base + block_incl_scan_d(item_P(i < ipr ? st[i] : none, w), &prev, &tot, sm);
+                hit = block_min_int(i < ipr && incl >= target ? i : 0x7fffffff, sm);
+                if (i == hit) { sm.hit_base = base + prev; sm.hit_w = w; }
+                base += tot;
             }
-            double run = base + lincl - ls;
-            int found = -1;
-            double fbase = 0.0, fw = 0.0;
-#pragma unroll
-            for (int c = 0; c < CI; c++) {
-                const bool in = b0 + lane * CI + c < ipr;
-                if (found < 0 && in && run + P[c] >= target) {
-                    found = b0 + lane * CI + c;
-                    fbase = run;
-                    fw = W[c];
-                }
-                run += P[c];
-            }
-            const unsigned hit = __ballot_sync(FULLMASK, found >= 0);
-            if (hit) {
-                const int L = __ffs(hit) - 1;
-                hit_item = __shfl_sync(FULLMASK, found, L);
-                ibase = __shfl_sync(FULLMASK, fbase, L);
-                iw = __shfl_sync(FULLMASK, fw, L);
-            }
-            base += __shfl_sync(FULLMASK, lincl, 31);
         }
-        if (hit_item < 0) {
+        __syncthreads();
+        if (hit == 0x7fffffff) {
             flags |= G4S_ROW_FALLBACK;
             need_argmax = true;
         } else {
-            // rescan the item: first id whose running sum reaches the target.
-            // Item ids run j-major, then lane, then k.
-            const float cc = st[hit_item].y;
+            // rescan the item: first id whose running sum reaches the target
+            const double ibase = sm.hit_base, iw = sm.hit_w;
+            const float cc = st[hit].y;
             const double tloc = (target - ibase) / iw;
-            const int n = item_len<DT>(a.vocab, hit_item);
-            uint4 rv[NVEC];
-            lane_vectors<DT, VEC>(a, row, hit_item, rv);
-            double run = 0.0;
-            int pos = -1, last = -1;
-            float etok = 0.0f, elast = 0.0f;
-#pragma unroll
-            for (int j = 0; j < NVEC; j++) {
-                if (pos >= 0) break;
-                float ev[VW];
-                DtypeTraits<DT>::unpack(rv[j], ev);
-                double lsum = 0.0;
+            const int n = item_len<DT>(a.vocab, hit);
+            float ev[VW];
+            double lsum = 0.0;
+            if (t < IV) {
+                float x[VW];
+                DtypeTraits<DT>::unpack(item_vector<DT, VEC>(a, row, hit, t), x);
 #pragma unroll
                 for (int k = 0; k < VW; k++) {
-                    const int e = item_pos<DT>(j, k, lane);
-                    ev[k] = e < n ? ex2_approx(__fmaf_rn(s_of(ev[k], sp), G4_L2E, -cc)) : 0.0f;
+                    ev[k] = t * VW + k < n ? ex2_approx(__fmaf_rn(s_of(x[k], sp), G4_L2E, -cc)) : 0.0f;
                     lsum += (double)ev[k];
                 }
-                double lincl = lsum;
+            } else {
 #pragma unroll
-                for (int d = 1; d < 32; d <<= 1) {
-                    const double o = __shfl_up_sync(FULLMASK, lincl, d);
-                    if (lane >= d) lincl += o;
-                }
-                double c = run + lincl - lsum;
-                int found = -1;
-                float efound = 0.0f;
-#pragma unroll
-                for (int k = 0; k < VW; k++) {
-                    c += (double)ev[k];
-                    if (found < 0 && c >= tloc) { found = k; efound = ev[k]; }
-                    if (ev[k] > 0.0f) { last = item_pos<DT>(j, k, lane); elast = ev[k]; }
-                }
-                const unsigned hit = __ballot_sync(FULLMASK, found >= 0);
-                if (hit) {
-                    const int L = __ffs(hit) - 1;
-                    pos = item_pos<DT>(j, __shfl_sync(FULLMASK, found, L), L);
-                    etok = __shfl_sync(FULLMASK, efound, L);
-                }
-                run += __shfl_sync(FULLMASK, lincl, 31);
+                for (int k = 0; k < VW; k++) ev[k] = 0.0f;
             }
-            if (pos < 0) {
+            double c, tot;
+            block_incl_scan_d(lsum, &c, &tot, sm);
+            int found = 0x7fffffff, last = -1;
+#pragma unroll
+            for (int k = 0; k < VW; k++) {
+                c += (double)ev[k];
+                if (found == 0x7fffffff && c >= tloc) found = t * VW + k;
+                if (ev[k] > 0.0f) last = t * VW + k;
+            }
+            int pos = block_min_int(found, sm);
+            if (pos == 0x7fffffff) {
                 // rounding left the threshold past this item: its last id with mass
-                const int lmax = (int)__reduce_max_sync(FULLMASK, (unsigned)(last + 1)) - 1;
-                const unsigned owner = __ballot_sync(FULLMASK, last == lmax && lmax >= 0);
-                pos = lmax < 0 ? 0 : lmax;
-                etok = owner ? __shfl_sync(FULLMASK, elast, __ffs(owner) - 1) : 0.0f;
+                pos = block_max_int(last, sm);
+                if (pos < 0) pos = 0;
             }
-            token = hit_item * ITEM + pos;
-            tprob = (float)((double)etok * iw / S);
+            if (t == pos / VW) {
+                float e = 0.0f;
+#pragma unroll
+                for (int k = 0; k < VW; k++)
+                    if (k == pos % VW) e = ev[k];
+                sm.etok = e;
+            }
+            __syncthreads();
+            token = hit * ITEM + pos;
+            tprob = (float)((double)sm.etok * iw / S);
         }
     }
     if (need_argmax) {
-        token = item_argmax<DT, VEC>(a, row, mi, sp, M);
+        // first id of item mi whose s equals M
+        const int n = item_len<DT>(a.vocab, mi);
+        int best = 0x7fffffff;
+        if (t < IV) {
+            float x[VW];
+            DtypeTraits<DT>::unpack(item_vector<DT, VEC>(a, row, mi, t), x);
+#pragma unroll
+            for (int k = VW - 1; k >= 0; k--)
+                if (t * VW + k < n && s_of(x[k], sp) == M) best = t * VW + k;
+        }
+        best = block_min_int(best, sm);
+        token = mi * ITEM + (best == 0x7fffffff ? 0 : best);
         if (draw) {
             const float4 q = st[mi];
             const double w = pow2_split((double)q.y - (double)M * (double)G4_L2E);
             tprob = (float)((double)ex2_approx(__fmaf_rn(M, G4_L2E, -q.y)) * w / S);
         }
     }
-    if (lane == 0) {
+    if (t == 0) {
         a.out_tokens[row] = token;
         if (a.token_prob) a.token_prob[row] = tprob;
         if (a.row_flags) a.row_flags[row] = flags;
@@ -736,7 +822,7 @@ static cudaError_t launch_full_t(const SampleArgs &a, cudaStream_t s, bool probs
         full_stream_kernel<DT, VEC><<<(unsigned)blocks, STREAM_THREADS, 0, s>>>(a);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
-        full_combine_kernel<DT, VEC><<<(a.rows + 3) / 4, 128, 0, s>>>(a);
+        full_combine_kernel<DT, VEC><<<a.rows, COMBINE_THREADS, 0, s>>>(a);
     } else {
         full_probs_kernel<DT><<<(unsigned)((nitems + NWARPS - 1) / NWARPS), NTHREADS, 0, s>>>(a);
     }
@@ -748,6 +834,8 @@ static cudaError_t launch_full_dt(const SampleArgs &a, bool vec, cudaStream_t s,
 {
     return vec ? launch_full_t<DT, true>(a, s, probs) : launch_full_t<DT, false>(a, s, probs);
 }
+
+int full_item_logits(int dtype) { return dtype == G4S_F32 ? Geo<G4S_F32>::ITEM : Geo<G4S_BF16>::ITEM; }
 
 int full_stream_blocks_per_sm(int dtype, bool vec)
 {

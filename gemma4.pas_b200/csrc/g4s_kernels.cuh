@@ -64,6 +64,8 @@ cudaError_t launch_topk(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
 cudaError_t launch_full(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
 cudaError_t launch_full_probs(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
 cudaError_t launch_largek(const SampleArgs &a, cudaStream_t s);
+// Logits per item of the full-path streaming kernel (one float4 of statistics each).
+int full_item_logits(int dtype);
 // Resident CTAs per SM of the full-path streaming kernel (for its persistent grid).
 int full_stream_blocks_per_sm(int dtype, bool vec);
 
