@@ -9,15 +9,16 @@
 //   a per-warp three-stage shared-memory ring with cp.async, and processes the
 //   current item from registers in two passes:
 //     1. NaN-propagating min/max of the lane's raw logits (packed bf16x2 or
-//        3-input fp32 min/max).  Each lane tests its own extremes (no NaN, every
-//        q = v * (1/cap) in [-1, 1]: fl32(v * c) is monotone in v) and one vote
-//        decides the item; the item maximum is then s(max v) (softcap and
+//        3-input fp32 min/max); the item maximum s(max v) (softcap and
 //        temperature are monotone), max v from one redux.sync;
 //     2. each pair of logits: softcap (packed fp32 polynomial) -> temperature ->
 //        e = 2^(s * log2e - cc), cc = fl32(m * log2e) -> packed accumulate.
-//   Items with a NaN, an |q| > 1 or a ragged end take an out-of-line general
-//   path (per element g4_tanhf, NaN -> -inf) that reads the shared-memory copy
-//   (or global memory for a ragged end).  Each item writes (m, cc, S): 16 bytes
+//   Only then does one vote check that every lane's extremes kept the
+//   polynomial exact (no NaN, every q = v * (1/cap) in [-1, 1]: fl32(v * c) is
+//   monotone in v).  Deciding before the sum put the vote's latency in front
+//   of every item; the rare item it rejects is redone on an out-of-line general
+//   path (per element g4_tanhf, NaN -> -inf) that reads the shared-memory copy,
+//   as is a ragged last item (from global memory).  Each item writes (m, cc, S): 16 bytes
 //   per 2 KiB read.
 // full_combine_kernel: one 256-thread CTA per row.  M = max of the item maxima;
 //   item weights 2^(cc - M * log2e); a block scan of the weighted item sums in
@@ -151,13 +152,13 @@ __device__ __forceinline__ float load_elem(const void *rowp, int64_t i)
     return DtypeTraits<DT>::load1(rowp, i);
 }
 
-// Pass 1: warp-uniform fast-path decision and the raw item maximum.  vec(j)
-// returns this lane's vector j.  Each lane tests its own extremes; one vote
-// decides the item.
+// Pass 1: this lane's raw extremes (NaN-propagating) and whether they keep the
+// polynomial softcap exact: no NaN and every q = v * (1/cap) in [-1, 1]
+// (fl32(v * c) is monotone in v).  vec(j) returns this lane's vector j.
 template <int DT, class Vec>
-__device__ __forceinline__ bool item_fast(Vec vec, const SParams &sp, float &xmax)
+__device__ __forceinline__ bool lane_fast(Vec vec, const SParams &sp, float &mx)
 {
-    float mn, mx;
+    float mn;
     if constexpr (DT == G4S_BF16) {
         uint4 v = vec(0);
         uint32_t a = bmax2_nan(bmax2_nan(v.x, v.y), bmax2_nan(v.z, v.w));
@@ -187,12 +188,9 @@ __device__ __forceinline__ bool item_fast(Vec vec, const SParams &sp, float &xma
         mx = a;
         mn = b;
     }
-    // NaN fails every comparison below
-    const bool ok = sp.use_cap ? (fabsf(__fmul_rn(mx, sp.invcap)) <= 1.0f && fabsf(__fmul_rn(mn, sp.invcap)) <= 1.0f)
-                               : (mx == mx && mn == mn);
-    const bool fast = __all_sync(FULLMASK, ok);
-    xmax = warp_max_redux(mx);  // used only when fast (no NaN in the item)
-    return fast;
+    // NaN fails every comparison
+    if (sp.use_cap) return (fabsf(__fmul_rn(mx, sp.invcap)) <= 1.0f) & (fabsf(__fmul_rn(mn, sp.invcap)) <= 1.0f);
+    return (mx == mx) & (mn == mn);
 }
 
 // Pass 2 of the fast path: each pair of logits goes softcap -> temperature ->
@@ -239,86 +237,15 @@ __device__ __forceinline__ float fast_exp_sum_any(Vec vec, const SParams &sp, fl
     return sp.use_t ? fast_exp_sum<DT, false, true, ROLLED>(vec, sp, cc) : fast_exp_sum<DT, false, false, ROLLED>(vec, sp, cc);
 }
 
-// General path of one item (NaN present, |q| > 1 somewhere, or a ragged last
-// item): element by element from global memory, the maximum first, then the
-// exponent sum.  Out of line and rare; it holds nothing across the streaming
-// loop.  Returns (item max, exponent origin, sum).
-template <int DT>
-__device__ __noinline__ float3 slow_item(const void *logits, int64_t row_stride, int vocab, int row, int sub,
-                                         const SParams sp, bool draw)
-{
-    using T = DtypeTraits<DT>;
-    constexpr int VW = Geo<DT>::VW;
-    const float NEG_INF = -__uint_as_float(0x7f800000u);
-    const int lane = threadIdx.x & 31;
-    const int n = item_len<DT>(vocab, sub);
-    const char *rowp = (const char *)logits + (int64_t)row * row_stride * T::ESIZE;
-    const int64_t base = (int64_t)sub * Geo<DT>::ITEM;
-    float m = NEG_INF;
-#pragma unroll 1
-    for (int j = 0; j < NVEC; j++)
-#pragma unroll
-        for (int k = 0; k < VW; k++) {
-            const int e = item_pos<DT>(j, k, lane);
-            if (e < n) m = fmaxf(m, s_of(load_elem<DT>(rowp, base + e), sp));
-        }
-    m = warp_max_nan(m);
-    float cc = 0.0f, S = 0.0f;
-    if (draw && m > NEG_INF) {
-        cc = __fmul_rn(m, G4_L2E);
-#pragma unroll 1
-        for (int j = 0; j < NVEC; j++)
-#pragma unroll
-            for (int k = 0; k < VW; k++) {
-                const int e = item_pos<DT>(j, k, lane);
-                if (e < n) S += ex2_approx(__fmaf_rn(s_of(load_elem<DT>(rowp, base + e), sp), G4_L2E, -cc));
-            }
-#pragma unroll
-        for (int d = 16; d > 0; d >>= 1) S += __shfl_xor_sync(FULLMASK, S, d);
-    }
-    return make_float3(m, cc, S);
-}
-
-// General path of one item whose lane vectors are in shared memory (the
-// cp.async ring): same arithmetic as slow_item, without rereading global memory.
-template <int DT>
-__device__ __noinline__ float3 slow_item_smem(const uint4 *stage, int n, const SParams sp, bool draw)
-{
-    constexpr int VW = Geo<DT>::VW;
-    const float NEG_INF = -__uint_as_float(0x7f800000u);
-    const int lane = threadIdx.x & 31;
-    float m = NEG_INF;
-#pragma unroll 1
-    for (int j = 0; j < NVEC; j++) {
-        float x[VW];
-        DtypeTraits<DT>::unpack(stage[j * 32 + lane], x);
-#pragma unroll 1
-        for (int k = 0; k < VW; k++)
-            if (item_pos<DT>(j, k, lane) < n) m = fmaxf(m, s_of(x[k], sp));
-    }
-    m = warp_max_nan(m);
-    float cc = 0.0f, S = 0.0f;
-    if (draw && m > NEG_INF) {
-        cc = __fmul_rn(m, G4_L2E);
-#pragma unroll 1
-        for (int j = 0; j < NVEC; j++) {
-            float x[VW];
-            DtypeTraits<DT>::unpack(stage[j * 32 + lane], x);
-#pragma unroll 1
-            for (int k = 0; k < VW; k++)
-                if (item_pos<DT>(j, k, lane) < n) S += ex2_approx(__fmaf_rn(s_of(x[k], sp), G4_L2E, -cc));
-        }
-#pragma unroll
-        for (int d = 16; d > 0; d >>= 1) S += __shfl_xor_sync(FULLMASK, S, d);
-    }
-    return make_float3(m, cc, S);
-}
-
-// One item of the streaming pass; vec(j) returns this lane's vector j.  stage:
-// the item's shared-memory copy when there is one (else nullptr).
+// One item of the streaming pass; vec(j) returns this lane's vector j.  The
+// fast path runs without waiting for the warp's verdict on it; the vote comes
+// after the exponent sum.  Items that must be redone on the general path (a
+// NaN, an |q| > 1, a ragged last item) are only flagged in their statistics
+// (w = 1): the per-row combine redoes them.  Any general-path code in the
+// streaming kernel, even after its loop and never executed, cost it a quarter
+// of its speed (more registers, fewer resident warps).
 template <int DT, bool ROLLED, class Vec>
-__device__ __forceinline__ void stream_item(const SampleArgs &a, int64_t it, int row, int sub, Vec vec,
-                                            const uint4 *stage)
+__device__ __forceinline__ void stream_item(const SampleArgs &a, int64_t it, int row, int sub, Vec vec)
 {
     const float NEG_INF = -__uint_as_float(0x7f800000u);
     const g4s_params p = a.params.get(row);
@@ -326,26 +253,23 @@ __device__ __forceinline__ void stream_item(const SampleArgs &a, int64_t it, int
     const SParams sp = make_sparams(a, p, row);
     const bool draw = p.temperature > 0.0f;
     const int n = item_len<DT>(a.vocab, sub);
-    float xmax;
-    const bool fast = n == Geo<DT>::ITEM && item_fast<DT>(vec, sp, xmax);
-    float m, cc = 0.0f, S = 0.0f;
-    if (fast) {
-        m = s_of(xmax, sp);  // softcap and temperature are monotone
+    float m = NEG_INF, cc = 0.0f, S = 0.0f;
+    bool redo = n != Geo<DT>::ITEM;
+    if (!redo) {
+        float mx;
+        const bool ok = lane_fast<DT>(vec, sp, mx);
+        // with ok on every lane the item maximum is s(max v): softcap and
+        // temperature are monotone
+        m = s_of(warp_max_redux(mx), sp);
         if (draw && m > NEG_INF) {
             cc = __fmul_rn(m, G4_L2E);
             S = fast_exp_sum_any<DT, ROLLED>(vec, sp, cc);
 #pragma unroll
             for (int d = 16; d > 0; d >>= 1) S += __shfl_xor_sync(FULLMASK, S, d);
         }
-    } else {
-        // partial copies of a ragged last item are completed from global memory
-        const float3 r = (stage && n == Geo<DT>::ITEM) ? slow_item_smem<DT>(stage, n, sp, draw)
-                                                      : slow_item<DT>(a.logits, a.row_stride, a.vocab, row, sub, sp, draw);
-        m = r.x;
-        cc = r.y;
-        S = r.z;
+        redo = !__all_sync(FULLMASK, ok);
     }
-    if ((threadIdx.x & 31) == 0) a.istat[it] = make_float4(m, cc, S, 0.0f);
+    if ((threadIdx.x & 31) == 0) a.istat[it] = make_float4(m, cc, S, redo ? 1.0f : 0.0f);
 }
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem)
@@ -411,7 +335,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 4) full_stream_kernel(SampleAr
                 }
                 regs[j] = make_uint4(w[0], w[1], w[2], w[3]);
             }
-            stream_item<DT, false>(a, it, cur.row, cur.sub, [&](int j) { return regs[j]; }, nullptr);
+            stream_item<DT, false>(a, it, cur.row, cur.sub, [&](int j) { return regs[j]; });
         }
     } else {
         uint4 *wring = ring + wib * STAGES * NVEC * 32;
@@ -443,7 +367,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 4) full_stream_kernel(SampleAr
             advance(nxt);
             cp_async_wait<STAGES - 1>();  // this lane's copies of item `it` have landed
             const uint4 *src = wring + stage * NVEC * 32;
-            stream_item<DT, true>(a, it, cur.row, cur.sub, [&](int j) { return src[j * 32 + lane]; }, src);
+            stream_item<DT, true>(a, it, cur.row, cur.sub, [&](int j) { return src[j * 32 + lane]; });
             advance(cur);
             stage = stage + 1 == STAGES ? 0 : stage + 1;
         }
@@ -495,6 +419,43 @@ __device__ __forceinline__ void lane_vectors(const SampleArgs &a, int row, int s
     }
 }
 
+// General path of one item (a NaN, an |q| > 1 somewhere, or a ragged last
+// item), by one warp: the lane's vectors are loaded once, then the maximum and
+// the exponent sum use per-element s_of (g4_tanhf, NaN -> -inf).  Returns
+// (item max, exponent origin, sum).
+template <int DT, bool VEC>
+__device__ __forceinline__ float3 general_item(const SampleArgs &a, int row, int sub, const SParams &sp, bool draw)
+{
+    constexpr int VW = Geo<DT>::VW;
+    const float NEG_INF = -__uint_as_float(0x7f800000u);
+    const int lane = threadIdx.x & 31;
+    const int n = item_len<DT>(a.vocab, sub);
+    uint4 r[NVEC];
+    lane_vectors<DT, VEC>(a, row, sub, r);
+    float s[NVEC * VW];
+#pragma unroll
+    for (int j = 0; j < NVEC; j++) DtypeTraits<DT>::unpack(r[j], s + j * VW);
+    float m = NEG_INF;
+#pragma unroll
+    for (int j = 0; j < NVEC; j++)
+#pragma unroll
+        for (int k = 0; k < VW; k++) {
+            s[j * VW + k] = item_pos<DT>(j, k, lane) < n ? s_of(s[j * VW + k], sp) : NEG_INF;
+            m = fmaxf(m, s[j * VW + k]);
+        }
+    m = warp_max_nan(m);
+    float cc = 0.0f, S = 0.0f;
+    if (draw && m > NEG_INF) {
+        cc = __fmul_rn(m, G4_L2E);
+#pragma unroll
+        for (int i = 0; i < NVEC * VW; i++)
+            if (s[i] > NEG_INF) S += ex2_approx(__fmaf_rn(s[i], G4_L2E, -cc));
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) S += __shfl_xor_sync(FULLMASK, S, d);
+    }
+    return make_float3(m, cc, S);
+}
+
 // ---------------------------------------------------------------------------
 // block primitives of the combine (one row per CTA of COMBINE_THREADS)
 // ---------------------------------------------------------------------------
@@ -507,6 +468,8 @@ struct CombineSmem {
     int i[CWARPS];
     double hit_base, hit_w;
     float etok;
+    int nredo;
+    int redo[COMBINE_THREADS];
 };
 
 // Block maximum of (m, idx), lower idx on ties; every thread gets the result.
@@ -631,6 +594,24 @@ __global__ void __launch_bounds__(COMBINE_THREADS) full_combine_kernel(SampleArg
     const float4 *st = a.istat + (int64_t)row * ipr;
     const float NEG_INF = -__uint_as_float(0x7f800000u);
     const float4 none = make_float4(NEG_INF, 0.0f, 0.0f, 0.0f);
+
+    // items the streaming pass flagged (w = 1) are redone here on the general
+    // path, one warp per item, before anything reads their statistics
+    for (int b0 = 0; b0 < ipr; b0 += CT) {
+        const bool flagged = b0 + t < ipr && st[b0 + t].w != 0.0f;
+        if (!__syncthreads_or(flagged)) continue;
+        if (t == 0) sm.nredo = 0;
+        __syncthreads();
+        if (flagged) sm.redo[atomicAdd(&sm.nredo, 1)] = b0 + t;
+        __syncthreads();
+        const bool draw = p.temperature > 0.0f;
+        for (int k = t >> 5; k < sm.nredo; k += CWARPS) {
+            const int sub = sm.redo[k];
+            const float3 r = general_item<DT, VEC>(a, row, sub, sp, draw);
+            if ((t & 31) == 0) a.istat[(int64_t)row * ipr + sub] = make_float4(r.x, r.y, r.z, 0.0f);
+        }
+        __syncthreads();  // the block's global writes are visible to it after the barrier
+    }
 
     // row maximum and the first item holding it
     const float4 q0 = t < ipr ? st[t] : none;

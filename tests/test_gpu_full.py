@@ -74,3 +74,26 @@ def test_c3_full_size_batch(sampler, torch_cuda, oracle, g4):
     st = check_full_rows(oracle, xb[pick], BF16, p, CAP, u[pick], sub, check_probs=False)
     print("C3 full batch sample:", st)
     assert ((res["tokens"] >= 0) & (res["tokens"] < 262144)).all()
+
+
+def test_full_path_general_items_bf16(sampler, torch_cuda, oracle, g4):
+    # bf16 rows on the aligned (shared-memory ring) path with items the fast
+    # polynomial cannot take: a NaN, a logit beyond +cap, many below -cap.
+    # The streaming pass flags them and redoes them on the general path.
+    V = 262144
+    xb = synth.c3_logits(5, step=11)
+    rng = np.random.default_rng(12)
+    xb[0, rng.choice(V, 7, replace=False)] = 0x7FC0                       # NaN
+    xb[1, rng.choice(V, 3, replace=False)] = synth.f32_to_bf16_rne(np.float32([45.0]))[0]
+    xb[2, ::97] = synth.f32_to_bf16_rne(np.float32([-60.0]))[0]           # every item
+    xb[3, :5] = synth.f32_to_bf16_rne(np.float32([-31.0]))[0]
+    u = synth.uniforms(5, 1234)
+    for T in (1.0, 0.8):
+        p = g4.make_params(T, 0, 0.95)
+        res = run_gpu(sampler, torch_cuda, xb, BF16, p, CAP, u, full_probs=True)
+        st = check_full_rows(oracle, xb, BF16, p, CAP, u, res)
+        assert st["rows"] == 5
+    # greedy rows take the same items
+    p = g4.make_params(0.0, 0, 0.95)
+    res = run_gpu(sampler, torch_cuda, xb, BF16, p, CAP, u)
+    check_full_rows(oracle, xb, BF16, p, CAP, u, res, check_probs=False)
