@@ -188,14 +188,15 @@ struct DtypeTraits<G4S_BF16> {
     }
     __device__ static __forceinline__ void unpack(uint4 v, float *o)
     {
-        // TBFloat16.ToSingle: bits << 16 (exact)
-        o[0] = __uint_as_float(v.x << 16);
+        // TBFloat16.ToSingle: bits << 16 (exact).  The low half moves up with a
+        // byte permute (integer pipe), keeping shifts off the fp32 FMA pipe.
+        o[0] = __uint_as_float(__byte_perm(v.x, 0u, 0x1044));
         o[1] = __uint_as_float(v.x & 0xffff0000u);
-        o[2] = __uint_as_float(v.y << 16);
+        o[2] = __uint_as_float(__byte_perm(v.y, 0u, 0x1044));
         o[3] = __uint_as_float(v.y & 0xffff0000u);
-        o[4] = __uint_as_float(v.z << 16);
+        o[4] = __uint_as_float(__byte_perm(v.z, 0u, 0x1044));
         o[5] = __uint_as_float(v.z & 0xffff0000u);
-        o[6] = __uint_as_float(v.w << 16);
+        o[6] = __uint_as_float(__byte_perm(v.w, 0u, 0x1044));
         o[7] = __uint_as_float(v.w & 0xffff0000u);
     }
 };

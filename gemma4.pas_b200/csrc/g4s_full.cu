@@ -36,7 +36,10 @@
 
 namespace g4s {
 
-constexpr int STREAM_THREADS = 128;  // CTA size of the persistent streaming kernel
+#ifndef G4S_FULL_STREAM_THREADS
+#define G4S_FULL_STREAM_THREADS 128
+#endif
+constexpr int STREAM_THREADS = G4S_FULL_STREAM_THREADS;  // CTA size of the persistent streaming kernel
 #ifndef G4S_FULL_NVEC
 #define G4S_FULL_NVEC 4
 #endif
@@ -286,12 +289,15 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // vectors of the items two ahead into a per-warp three-stage shared-memory ring
 // with cp.async (completion tracked by cp.async.wait_group, no polling).
 template <int DT, bool VEC>
-__global__ void __launch_bounds__(STREAM_THREADS, 4) full_stream_kernel(SampleArgs a)
+__global__ void __launch_bounds__(STREAM_THREADS) full_stream_kernel(SampleArgs a)
 {
     using T = DtypeTraits<DT>;
     constexpr int VW = Geo<DT>::VW, ITEM = Geo<DT>::ITEM;
     constexpr int WPB = STREAM_THREADS / 32;
     __shared__ uint4 ring[VEC ? WPB * STAGES * NVEC * 32 : 1];
+    // the per-row combine may be scheduled as soon as this grid's CTAs retire;
+    // it waits for this grid's results itself (griddepcontrol.wait)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int ipr = (a.vocab + ITEM - 1) / ITEM;
     const int64_t nitems = (int64_t)a.rows * ipr;
@@ -594,6 +600,11 @@ __global__ void __launch_bounds__(COMBINE_THREADS) full_combine_kernel(SampleArg
     const float4 *st = a.istat + (int64_t)row * ipr;
     const float NEG_INF = -__uint_as_float(0x7f800000u);
     const float4 none = make_float4(NEG_INF, 0.0f, 0.0f, 0.0f);
+    const double u_row = p.temperature > 0.0f ? a.u[row] : 0.0;  // u may be null for greedy calls
+    // launched as a programmatic dependent of the streaming kernel: everything
+    // above reads only the call's inputs; the item statistics are read after
+    // the streaming grid has completed and flushed
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     // items the streaming pass flagged (w = 1) are redone here on the general
     // path, one warp per item, before anything reads their statistics
@@ -641,7 +652,7 @@ __global__ void __launch_bounds__(COMBINE_THREADS) full_combine_kernel(SampleArg
             w = pow2_split((double)q.y - Ml);
             return (double)q.z * w;
         };
-        const float thr = __double2float_rn(a.u[row] * (double)p.top_p);
+        const float thr = __double2float_rn(u_row * (double)p.top_p);
         int hit = 0x7fffffff;
         double target;
         if (ipr <= CT) {
@@ -803,7 +814,17 @@ static cudaError_t launch_full_t(const SampleArgs &a, cudaStream_t s, bool probs
         full_stream_kernel<DT, VEC><<<(unsigned)blocks, STREAM_THREADS, 0, s>>>(a);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
-        full_combine_kernel<DT, VEC><<<a.rows, COMBINE_THREADS, 0, s>>>(a);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)a.rows);
+        cfg.blockDim = dim3(COMBINE_THREADS);
+        cfg.stream = s;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, full_combine_kernel<DT, VEC>, a);
+        if (e != cudaSuccess) return e;
     } else {
         full_probs_kernel<DT><<<(unsigned)((nitems + NWARPS - 1) / NWARPS), NTHREADS, 0, s>>>(a);
     }
