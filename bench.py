@@ -42,7 +42,7 @@ FALLBACK_HBM_GBS = 6650.0
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -77,51 +77,98 @@ def profiled_traffic():
 
 
 class Clocks:
-    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    """SM clock and throttle reasons sampled every ~2 ms through NVML (read-only
+    queries) in a background thread while the timed region runs; nvidia-smi at
+    100 ms when NVML is unavailable."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
     def __init__(self, gpu_index):
         self.idx = gpu_index
+        self.samples = []
+        self.run = False
+        self.thread = None
         self.proc = None
-        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.nvml = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            uuid = None
+            try:
+                import torch
+
+                uuid = "GPU-" + str(torch.cuda.get_device_properties(gpu_index).uuid)
+            except Exception:
+                pass
+            self.h = (pynvml.nvmlDeviceGetHandleByUUID(uuid) if uuid else
+                      pynvml.nvmlDeviceGetHandleByIndex(gpu_index))
+            self.smax = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.reasons_fn = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        except Exception:
+            self.nvml = None
+
+    def _poll(self):
+        nv = self.nvml
+        while self.run:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                rs = self.reasons_fn(self.h)
+                pw = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+                self.samples.append((sm, rs, pw))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def start(self):
+        if self.nvml is not None:
+            import threading
+
+            self.run = True
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
-            time.sleep(0.3)
+            self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
 
     def stop(self):
+        if self.thread is not None:
+            self.run = False
+            self.thread.join()
+            if not self.samples:
+                return None
+            reasons = sorted({n for _, rs, _ in self.samples for n, bit in self.REASONS.items() if rs & bit})
+            return {"sm_mhz": statistics.median(s[0] for s in self.samples), "sm_max_mhz": self.smax,
+                    "reasons": reasons, "samples": len(self.samples),
+                    "power_w_max": max(s[2] for s in self.samples), "source": "NVML, 2 ms"}
         if self.proc is None:
             return None
-        time.sleep(0.25)
         self.proc.terminate()
         try:
             self.proc.wait(5)
         except Exception:
             self.proc.kill()
         self.f.flush()
-        rows = []
-        for line in open(self.f.name):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
+        rows = [[p.strip() for p in line.split(",")] for line in open(self.f.name)]
         os.unlink(self.f.name)
+        rows = [r for r in rows if len(r) >= 7 and r[0].replace(".", "").isdigit()]
         if not rows:
             return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        pw = [float(r[3]) for r in rows if re.match(r"^[0-9.]+$", r[3])]
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None}
+        return {"sm_mhz": statistics.median(float(r[0]) for r in rows), "sm_max_mhz": max(float(r[1]) for r in rows),
+                "reasons": sorted({names[i] for r in rows for i in range(4) if r[3 + i].lower() == "active"}),
+                "samples": len(rows), "source": "nvidia-smi, 100 ms"}
 
 
 def dist_setup(n):
@@ -248,36 +295,57 @@ def main():
     for i in range(W):
         step(i)
     torch.cuda.synchronize()
-    # The K timed steps are captured in one CUDA graph and replayed: a Python
-    # loop of ctypes calls cannot enqueue a ~25 us step as fast as the GPU runs
-    # it, and per-call events would time the host.  The graph is replayed once
-    # untimed (upload), then once timed.
+
+    # The timed steps run from CUDA graphs of G consecutive g4s_sample calls: a
+    # Python loop of ctypes calls cannot enqueue a ~50 us step as fast as the
+    # GPU runs it, and per-call events would time the host.  Exactly K steps are
+    # timed: the G-step graph is replayed K // G times, then a graph of the
+    # remaining K % G steps.  Each graph is replayed once untimed first.
     cap = torch.cuda.Stream(device=dev)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=cap):
-        for i in range(K):
-            step(W + i, stream=cap.cuda_stream)
-    graph.replay()
-    torch.cuda.synchronize()
-    barrier(world)
-    clocks = Clocks(local)
-    clocks.start()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    barrier(world)
-    t0.record()
-    graph.replay()
-    t1.record()
-    torch.cuda.synchronize()
-    barrier(world)
-    clk = clocks.stop()
-    total_ms = t0.elapsed_time(t1)
+    G = min(K, 250)
+
+    def capture(nsteps, phase_mask=0):
+        o = g4.Outputs()
+        o.phase_mask = phase_mask
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=cap):
+            for i in range(nsteps):
+                j = W + i
+                s.sample(sets[j % 4].data_ptr(), g4.BF16, ROWS, VOCAB, VOCAB, p, SOFTCAP, u_all[j % (K + W)].data_ptr(),
+                         out.data_ptr(), stream=cap.cuda_stream, outputs=o)
+        gr.replay()
+        return gr
+
+    def timed(graphs, clocks=None):
+        torch.cuda.synchronize()
+        barrier(world)
+        if clocks:
+            clocks.start()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for gr in graphs:
+            gr.replay()
+        t1.record()
+        torch.cuda.synchronize()
+        clk = clocks.stop() if clocks else None
+        barrier(world)
+        return t0.elapsed_time(t1), clk
+
+    g_main = capture(G)
+    g_rest = capture(K % G) if K % G else None
+    plan = [g_main] * (K // G) + ([g_rest] if g_rest else [])
+    total_ms, clk = timed(plan, Clocks(local))
     total_ms_max = allreduce_max(total_ms, world)
     value = world * ROWS * K / (total_ms_max / 1e3)
-    mean_launch_s = total_ms / K / 1e3
-    achieved = ROWS * BYTES_PER_ROW / mean_launch_s / 1e9
     tokens_ok = bool(((out >= 0) & (out < VOCAB)).all().item())
-    del graph
+    # the dominant kernel alone: the same steps with only the streaming pass
+    # (G4S_PHASE_FULL_STREAM_ONLY), for the roofline's achieved bandwidth
+    gs_main = capture(G, 1)
+    gs_rest = capture(K % G, 1) if K % G else None
+    stream_ms, _ = timed([gs_main] * (K // G) + ([gs_rest] if gs_rest else []))
+    stream_us = stream_ms / K * 1e3
+    achieved = ROWS * BYTES_PER_ROW / (stream_us * 1e-6) / 1e9
+    del plan, g_main, g_rest, gs_main, gs_rest
 
     # ---- latency at B=1 (config C1: fp32, top_k 64, top_p 0.95) ----
     # one call per CUDA graph (8 graphs over 8 rows, as a decode loop would
@@ -353,15 +421,18 @@ def main():
                        "global_batch": ROWS * world, "seq_len": VOCAB,
                        "parallelism": f"row-sharded x{world} (independent rows, no collective)",
                        "l2": "4 rotating input sets of 128 MiB (512 MiB > 126 MB L2)",
-                       "timing": "K steps captured in one CUDA graph; one untimed replay, then one "
-                                 "replay timed with CUDA events"},
-            "hbm_frac_of_peak": achieved / peak,
+                       "timing": f"K steps from CUDA graphs of {G} calls, each graph replayed once "
+                                 "untimed; K steps timed with CUDA events"},
+            "hbm_frac_of_peak": ROWS * BYTES_PER_ROW / (total_ms_max / K * 1e-3) / 1e9 / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": profiled_traffic(),
-                         "kernel": "full_stream_kernel<bf16> (+ full_combine_kernel in the timed call)",
-                         "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
+                         "kernel": "full_stream_kernel<bf16>, timed alone (phase_mask = stream only), "
+                                   "CUDA events over K launches",
+                         "kernel_mean_us": stream_us,
+                         "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json), burst copy",
                          "algorithmic_bytes_per_launch": ROWS * BYTES_PER_ROW,
-                         "mean_step_us": mean_launch_s * 1e6},
+                         "step_us": total_ms_max / K * 1e3,
+                         "step_hbm_frac": ROWS * BYTES_PER_ROW / (total_ms_max / K * 1e-3) / 1e9 / peak},
             "latency_b1": lat,
             "e2e": e2e,
             "cpu_baseline": cpu,

@@ -312,6 +312,7 @@ int32_t g4s_sample_ex(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t r
     a.cand_probs = ex.cand_probs;
     a.cand_stride = ex.cand_stride;
     a.full_probs = ex.full_probs;
+    a.stream_only = (ex.phase_mask & G4S_PHASE_FULL_STREAM_ONLY) ? 1 : 0;
     a.cand = ctx->cand;
     a.cand_cnt = ctx->cand_cnt;
     a.counters_topk = ctx->counters_topk;

@@ -813,7 +813,7 @@ static cudaError_t launch_full_t(const SampleArgs &a, cudaStream_t s, bool probs
         if (a.persist_blocks > 0 && blocks > a.persist_blocks) blocks = a.persist_blocks;
         full_stream_kernel<DT, VEC><<<(unsigned)blocks, STREAM_THREADS, 0, s>>>(a);
         cudaError_t e = cudaGetLastError();
-        if (e != cudaSuccess) return e;
+        if (e != cudaSuccess || a.stream_only) return e;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)a.rows);
         cfg.blockDim = dim3(COMBINE_THREADS);

@@ -37,6 +37,7 @@ struct SampleArgs {
     int32_t nch;          // chunks per row
     int32_t lk_slots;     // concurrent rows of the large-K kernel
     int32_t persist_blocks;  // CTAs of the persistent full-path streaming kernel
+    int32_t stream_only;     // G4S_PHASE_FULL_STREAM_ONLY: skip the full-path combine
     RowParams params;
     float softcap;
     float invcap;         // fl32(1/softcap) when softcap > 0

@@ -35,7 +35,7 @@ class Params(ctypes.Structure):
 
 class Outputs(ctypes.Structure):
     _fields_ = [("token_prob", c_void_p), ("row_flags", c_void_p), ("cand_ids", c_void_p),
-                ("cand_probs", c_void_p), ("cand_stride", c_int32), ("reserved", c_int32),
+                ("cand_probs", c_void_p), ("cand_stride", c_int32), ("phase_mask", c_int32),
                 ("full_probs", c_void_p)]
 
 

@@ -58,7 +58,7 @@ type
     CandIds: PInt32;
     CandProbs: PSingle;
     CandStride: Int32;
-    Reserved: Int32;
+    PhaseMask: Int32;   { 0; G4S_PHASE_FULL_STREAM_ONLY = 1 times the streaming pass alone }
     FullProbs: PSingle;
   end;
   PG4SOutputs = ^TG4SOutputs;

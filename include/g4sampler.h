@@ -79,6 +79,9 @@ enum g4s_row_flag {
     G4S_ROW_GREEDY     = 8   /* T <= 0                                              */
 };
 
+/* g4s_outputs.phase_mask bits */
+enum g4s_phase { G4S_PHASE_FULL_STREAM_ONLY = 1 };
+
 /* Optional per-row outputs (all device pointers; any may be NULL). */
 typedef struct g4s_outputs {
     float   *token_prob;   /* [rows] probability of the sampled token             */
@@ -87,7 +90,9 @@ typedef struct g4s_outputs {
                               padded with -1                                       */
     float   *cand_probs;   /* [rows * cand_stride] their probabilities, 0-padded   */
     int32_t  cand_stride;  /* >= largest top_k of the top-K rows when cand_* used  */
-    int32_t  reserved;
+    int32_t  phase_mask;   /* 0 (normal).  G4S_PHASE_FULL_STREAM_ONLY: measurement
+                              hook, runs only the streaming pass of full-path rows
+                              (no tokens written) so its bandwidth can be timed alone */
     float   *full_probs;   /* [rows * vocab] full-path rows: every probability (a
                               second pass; meant for verification)                 */
 } g4s_outputs;
