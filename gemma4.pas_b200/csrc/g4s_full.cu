@@ -92,6 +92,32 @@ __device__ __forceinline__ float s_of(float x, const SParams &sp)
     return s;
 }
 
+// s_of for N elements: the polynomial tanh for all of them first (independent,
+// branch-free), then the rare elements outside it (|q| > 1, NaN, +-inf) again
+// through s_of.  Same values as s_of element by element.
+template <int N>
+__device__ __forceinline__ void s_of_many(const float *x, const SParams &sp, float *s)
+{
+    bool wide = false;
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+        float v = x[i];
+        if (sp.use_cap) {
+            const float q = __fmul_rn(v, sp.invcap);
+            wide |= !(fabsf(q) <= 1.0f);
+            v = __fmul_rn(tanh_poly(q), sp.cap);
+        } else {
+            wide |= v != v;
+        }
+        s[i] = sp.use_t ? __fmul_rn(v, sp.invT) : v;
+    }
+    if (wide) {
+#pragma unroll
+        for (int i = 0; i < N; i++)
+            if (!(fabsf(__fmul_rn(x[i], sp.invcap)) <= 1.0f) || x[i] != x[i]) s[i] = s_of(x[i], sp);
+    }
+}
+
 __device__ __forceinline__ float fmax_nan(float a, float b)
 {
     float r;
@@ -432,30 +458,33 @@ __device__ __forceinline__ void lane_vectors(const SampleArgs &a, int row, int s
 template <int DT, bool VEC>
 __device__ __forceinline__ float3 general_item(const SampleArgs &a, int row, int sub, const SParams &sp, bool draw)
 {
-    constexpr int VW = Geo<DT>::VW;
+    constexpr int VW = Geo<DT>::VW, NE = NVEC * VW;
     const float NEG_INF = -__uint_as_float(0x7f800000u);
     const int lane = threadIdx.x & 31;
     const int n = item_len<DT>(a.vocab, sub);
     uint4 r[NVEC];
     lane_vectors<DT, VEC>(a, row, sub, r);
-    float s[NVEC * VW];
+    float x[NE], s[NE];
 #pragma unroll
-    for (int j = 0; j < NVEC; j++) DtypeTraits<DT>::unpack(r[j], s + j * VW);
+    for (int j = 0; j < NVEC; j++) DtypeTraits<DT>::unpack(r[j], x + j * VW);
+    s_of_many<NE>(x, sp, s);
     float m = NEG_INF;
 #pragma unroll
     for (int j = 0; j < NVEC; j++)
 #pragma unroll
         for (int k = 0; k < VW; k++) {
-            s[j * VW + k] = item_pos<DT>(j, k, lane) < n ? s_of(s[j * VW + k], sp) : NEG_INF;
+            if (!(item_pos<DT>(j, k, lane) < n)) s[j * VW + k] = NEG_INF;
             m = fmaxf(m, s[j * VW + k]);
         }
     m = warp_max_nan(m);
     float cc = 0.0f, S = 0.0f;
     if (draw && m > NEG_INF) {
         cc = __fmul_rn(m, G4_L2E);
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int i = 0; i < NVEC * VW; i++)
-            if (s[i] > NEG_INF) S += ex2_approx(__fmaf_rn(s[i], G4_L2E, -cc));
+        for (int i = 0; i < NE; i++)
+            acc[i & 3] += s[i] > NEG_INF ? ex2_approx(__fmaf_rn(s[i], G4_L2E, -cc)) : 0.0f;
+        S = (acc[0] + acc[1]) + (acc[2] + acc[3]);
 #pragma unroll
         for (int d = 16; d > 0; d >>= 1) S += __shfl_xor_sync(FULLMASK, S, d);
     }
@@ -693,11 +722,12 @@ __global__ void __launch_bounds__(COMBINE_THREADS) full_combine_kernel(SampleArg
             float ev[VW];
             double lsum = 0.0;
             if (t < IV) {
-                float x[VW];
+                float x[VW], sv[VW];
                 DtypeTraits<DT>::unpack(item_vector<DT, VEC>(a, row, hit, t), x);
+                s_of_many<VW>(x, sp, sv);
 #pragma unroll
                 for (int k = 0; k < VW; k++) {
-                    ev[k] = t * VW + k < n ? ex2_approx(__fmaf_rn(s_of(x[k], sp), G4_L2E, -cc)) : 0.0f;
+                    ev[k] = t * VW + k < n ? ex2_approx(__fmaf_rn(sv[k], G4_L2E, -cc)) : 0.0f;
                     lsum += (double)ev[k];
                 }
             } else {
@@ -736,11 +766,12 @@ __global__ void __launch_bounds__(COMBINE_THREADS) full_combine_kernel(SampleArg
         const int n = item_len<DT>(a.vocab, mi);
         int best = 0x7fffffff;
         if (t < IV) {
-            float x[VW];
+            float x[VW], sv[VW];
             DtypeTraits<DT>::unpack(item_vector<DT, VEC>(a, row, mi, t), x);
+            s_of_many<VW>(x, sp, sv);
 #pragma unroll
             for (int k = VW - 1; k >= 0; k--)
-                if (t * VW + k < n && s_of(x[k], sp) == M) best = t * VW + k;
+                if (t * VW + k < n && sv[k] == M) best = t * VW + k;
         }
         best = block_min_int(best, sm);
         token = mi * ITEM + (best == 0x7fffffff ? 0 : best);
