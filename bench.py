@@ -348,38 +348,75 @@ def main():
     del plan, g_main, g_rest, gs_main, gs_rest
 
     # ---- latency at B=1 (config C1: fp32, top_k 64, top_p 0.95) ----
-    # one call per CUDA graph (8 graphs over 8 rows, as a decode loop would
-    # replay it), device time of each replay
+    # (i) in a decode loop the sampler is one node of a captured step: device
+    #     time per call inside a CUDA graph of 20 consecutive calls (each on a
+    #     fresh row), p50/p90 over 200 replays; (ii) one call as a graph of its
+    #     own (adds the graph launch, ~8 us on this box for a one-kernel graph).
     lat = None
+    c2 = None
     if rank == 0:
-        c1 = torch.from_numpy(np.stack([synth.c1_logits(i) for i in range(8)])).to(dev)
-        u1 = torch.from_numpy(synth.uniforms(8, synth.SEEDS["c1"])).to(dev)
+        n1 = 20
+        c1 = torch.from_numpy(np.stack([synth.c1_logits(i) for i in range(n1)])).to(dev)
+        u1 = torch.from_numpy(synth.uniforms(n1, synth.SEEDS["c1"])).to(dev)
         p1 = g4.make_params(1.0, 64, 0.95)
-        o1 = torch.empty(1, dtype=torch.int32, device=dev)
-        for i in range(5):
-            s.sample(c1[i % 8].data_ptr(), g4.F32, 1, VOCAB, VOCAB, p1, SOFTCAP, u1[i % 8].data_ptr(), o1.data_ptr())
+        o1 = torch.empty(n1, dtype=torch.int32, device=dev)
+
+        def call1(i, st=None):
+            s.sample(c1[i].data_ptr(), g4.F32, 1, VOCAB, VOCAB, p1, SOFTCAP, u1[i:].data_ptr(), o1[i:].data_ptr(),
+                     stream=st)
+
+        for i in range(n1):
+            call1(i)
         torch.cuda.synchronize()
-        graphs = []
-        for i in range(8):
-            gi = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(gi, stream=cap):
-                s.sample(c1[i].data_ptr(), g4.F32, 1, VOCAB, VOCAB, p1, SOFTCAP, u1[i].data_ptr(), o1.data_ptr(),
-                         stream=cap.cuda_stream)
-            graphs.append(gi)
-        for gi in graphs:
-            gi.replay()
+
+        def replay_times(gr, reps):
+            gr.replay()
+            torch.cuda.synchronize()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+            for e0, e1 in ev:
+                e0.record()
+                gr.replay()
+                e1.record()
+                e1.synchronize()
+            return sorted(e0.elapsed_time(e1) * 1e3 for e0, e1 in ev)
+
+        gl = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gl, stream=cap):
+            for i in range(n1):
+                call1(i, cap.cuda_stream)
+        lt = [t / n1 for t in replay_times(gl, 200)]
+        g1 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g1, stream=cap):
+            call1(0, cap.cuda_stream)
+        ls = replay_times(g1, 200)
+        lat = {"p50_us": lt[len(lt) // 2], "p90_us": lt[int(len(lt) * 0.9)],
+               "single_graph_p50_us": ls[len(ls) // 2], "single_graph_p90_us": ls[int(len(ls) * 0.9)],
+               "steps": 200 * n1,
+               "config": "C1: B=1 x V=262144 fp32 (fresh row per call), top_k 64, T=1, top_p 0.95; p50_us: device "
+                         "time per call inside a CUDA graph of 20 consecutive calls; single_graph: one call per "
+                         "graph replay"}
+        del gl, g1
+
+        # ---- config C2: B=32 fp32 rows, T=0.7, top_k 40, top_p 0.9 (HBM-bound top-K) ----
+        nset, k2 = 8, 200
+        c2sets = [torch.from_numpy(synth.c2_logits(32, step=i)).to(dev) for i in range(nset)]
+        u2 = torch.from_numpy(synth.uniforms(32, synth.SEEDS["c2"])).to(dev)
+        o2 = torch.empty(32, dtype=torch.int32, device=dev)
+        p2 = g4.make_params(0.7, 40, 0.9)
+        for i in range(nset):
+            s.sample(c2sets[i].data_ptr(), g4.F32, 32, VOCAB, VOCAB, p2, SOFTCAP, u2.data_ptr(), o2.data_ptr())
         torch.cuda.synchronize()
-        evl = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(200)]
-        for i in range(200):
-            evl[i][0].record()
-            graphs[i % 8].replay()
-            evl[i][1].record()
-            evl[i][1].synchronize()
-        lt = sorted(a.elapsed_time(b) * 1e3 for a, b in evl)
-        lat = {"p50_us": lt[len(lt) // 2], "p90_us": lt[int(len(lt) * 0.9)], "steps": 200,
-               "config": "C1: B=1 x V=262144 fp32, top_k 64, T=1, top_p 0.95; device time of one "
-                         "CUDA-graph replay of one g4s_sample call"}
-        del graphs
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2, stream=cap):
+            for i in range(k2):
+                s.sample(c2sets[i % nset].data_ptr(), g4.F32, 32, VOCAB, VOCAB, p2, SOFTCAP, u2.data_ptr(),
+                         o2.data_ptr(), stream=cap.cuda_stream)
+        t2 = statistics.median(replay_times(g2, 5)) / k2
+        c2 = {"rows_per_s": 32 / (t2 * 1e-6), "us_per_step": t2,
+              "hbm_frac_of_peak": 32 * VOCAB * 4 / (t2 * 1e-6) / 1e9 / peak,
+              "config": "C2: B=32 x V=262144 fp32, T=0.7, top_k 40, top_p 0.9; 8 rotating input sets "
+                        "(256 MiB > L2); 200 calls per CUDA graph, median of 5 replays"}
+        del g2, c2sets
 
     # ---- end to end through g4s_sample_host (pinned host memory, PCIe inside) ----
     e2e = None
@@ -434,6 +471,7 @@ def main():
                          "step_us": total_ms_max / K * 1e3,
                          "step_hbm_frac": ROWS * BYTES_PER_ROW / (total_ms_max / K * 1e-3) / 1e9 / peak},
             "latency_b1": lat,
+            "c2": c2,
             "e2e": e2e,
             "cpu_baseline": cpu,
             "gpu_launches": 2 * K,

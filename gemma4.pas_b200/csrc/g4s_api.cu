@@ -26,6 +26,7 @@ struct g4s_ctx {
     int max_vocab = 0;
     uint32_t flags = 0;
     int sm_count = 0;
+    bool cluster_ok = false;  // the single-row cluster kernel can be scheduled
     cudaStream_t stream = nullptr;
     // workspace (one allocation)
     void *ws = nullptr;
@@ -167,6 +168,7 @@ int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t
     ctx->max_vocab = max_vocab;
     ctx->flags = flags;
     cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
+    ctx->cluster_ok = topk_cluster_available();
 
     // per-chunk lists: big chunks for every row, or small chunks for the few rows
     // that choose them
@@ -352,7 +354,10 @@ int32_t g4s_sample_ex(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t r
     }
 
     cudaError_t e = cudaSuccess;
-    if (any_topk && e == cudaSuccess) e = launch_topk(a, ept, vec, s);
+    // a few rows: one thread-block cluster per row (latency); else the chunked grid
+    const bool use_cluster = ctx->cluster_ok && rows <= TOPK_CLUSTER_MAX_ROWS && vocab <= TOPK_CLUSTER_MAX_VOCAB &&
+                             max_k_small <= TOPK_CLUSTER_KMAX;
+    if (any_topk && e == cudaSuccess) e = use_cluster ? launch_topk_cluster(a, vec, s) : launch_topk(a, ept, vec, s);
     if (any_full && e == cudaSuccess) e = launch_full(a, ept, vec, s);
     if (any_full && ex.full_probs && e == cudaSuccess) e = launch_full_probs(a, ept, vec, s);
     if (any_large && e == cudaSuccess) e = launch_largek(a, s);

@@ -60,11 +60,21 @@ struct SampleArgs {
     float *lk_val;             // [lk_slots][vocab]
 };
 
+// Single-row latency path of the top-K selection: one cluster of TOPK_CLUSTER
+// CTAs (16384 ids each) per row; used for a few rows with vocab <= 262144.
+constexpr int TOPK_CLUSTER = 16;
+constexpr int TOPK_CLUSTER_MAX_VOCAB = TOPK_CLUSTER * 16384;
+constexpr int TOPK_CLUSTER_MAX_ROWS = 8;
+constexpr int TOPK_CLUSTER_KMAX = 128;  // largest top_k of the cluster kernel
+
 // Launchers (return the launch status; nothing is launched for rows of other kinds).
 cudaError_t launch_topk(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
 cudaError_t launch_full(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
 cudaError_t launch_full_probs(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
 cudaError_t launch_largek(const SampleArgs &a, cudaStream_t s);
+cudaError_t launch_topk_cluster(const SampleArgs &a, bool vec, cudaStream_t s);
+// Whether a TOPK_CLUSTER-CTA cluster of the latency kernel can be scheduled.
+bool topk_cluster_available();
 // Logits per item of the full-path streaming kernel (one float4 of statistics each).
 int full_item_logits(int dtype);
 // Resident CTAs per SM of the full-path streaming kernel (for its persistent grid).

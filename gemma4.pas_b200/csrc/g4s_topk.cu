@@ -21,6 +21,8 @@
 //            cumulative draw -- the same fp32 operation sequence as the
 //            reference, so probabilities and tokens are bit-identical to the
 //            oracle's transcription.
+#include <cooperative_groups.h>
+
 #include "g4s_device.cuh"
 #include "g4s_kernels.cuh"
 
@@ -247,6 +249,27 @@ __device__ __forceinline__ int prefix_at_least(const uint64_t *list, int cnt, ui
     return lo;
 }
 
+// The kw winners in sm.L[0..kw) (descending composites) re-sorted by ascending
+// vocab id into sm.ids / sm.tv, then the tail on warp 0.
+__device__ __forceinline__ void finish_row(const SampleArgs &a, int row, const g4s_params &p, int kw, TopkSmem &sm)
+{
+    static_assert(KMAX <= NTHREADS, "one winner per thread");
+    const int tid = threadIdx.x;
+    __syncthreads();
+    const uint64_t mine = tid < kw ? sm.L[tid] : 0;
+    __syncthreads();
+    if (tid < kw) sm.L[tid] = ((uint64_t)comp_id(mine) ^ 0xffffffffull) << 32 | comp_key(mine);
+    __syncthreads();
+    sort_list_desc(sm, kw);
+    for (int i = tid; i < kw; i += NTHREADS) {
+        const uint64_t v = sm.L[i];
+        sm.ids[i] = (int32_t)(~(uint32_t)(v >> 32));
+        sm.tv[i] = key2f((uint32_t)v);
+    }
+    __syncthreads();
+    if (tid < 32) topk_tail(a, row, p, kw, sm);
+}
+
 // Stage 2 of a row (last-arriving CTA): merge the per-chunk lists and sample.
 __device__ void topk_merge(const SampleArgs &a, int row, const g4s_params &p, TopkSmem &sm)
 {
@@ -336,36 +359,62 @@ __device__ void topk_merge(const SampleArgs &a, int row, const g4s_params &p, To
         sort_list_desc(sm, tot2);
         kw = K;
     }
-    // the kw winners, re-sorted by ascending vocab id: key (~id << 32 | key) descending
-    static_assert(KMAX <= NTHREADS, "one winner per thread");
-    __syncthreads();
-    const uint64_t mine = tid < kw ? sm.L[tid] : 0;
-    __syncthreads();
-    if (tid < kw) sm.L[tid] = ((uint64_t)comp_id(mine) ^ 0xffffffffull) << 32 | comp_key(mine);
-    __syncthreads();
-    sort_list_desc(sm, kw);
-    for (int i = tid; i < kw; i += NTHREADS) {
-        const uint64_t v = sm.L[i];
-        sm.ids[i] = (int32_t)(~(uint32_t)(v >> 32));
-        sm.tv[i] = key2f((uint32_t)v);
-    }
-    __syncthreads();
-    if (tid < 32) topk_tail(a, row, p, kw, sm);
+    finish_row(a, row, p, kw, sm);
     if (tid == 0) a.counters_topk[row] = 0;  // ready for the next call
 }
 
-template <int DT, int EPT, bool VEC>
-__global__ void __launch_bounds__(NTHREADS) topk_chunk_kernel(SampleArgs a)
+// Heavy ties in a chunk (more than CAP1 keys at or above the bound): exact
+// radix selection of the K-th largest composite, then the K largest sorted.
+// Out of line and rare: it rereads the chunk from global memory in rolled
+// loops, so the register-resident fast path does not carry its code.
+template <int DT, int EPT>
+__device__ __noinline__ int chunk_select_radix(const void *rowp, int64_t c0, int n, int K, TopkSmem &sm)
 {
-    __shared__ TopkSmem sm;
     using T = DtypeTraits<DT>;
     constexpr int VW = T::VW;
-    const int row = blockIdx.y, chunk = blockIdx.x, tid = threadIdx.x;
-    const g4s_params p = a.params.get(row);
-    const int K = p.top_k;
-    if (!(K > 0 && K < a.vocab && K <= KMAX)) return;
-    const int64_t c0 = (int64_t)chunk * a.chunk;
-    const int n = (int)min((int64_t)a.chunk, (int64_t)a.vocab - c0);
+    const int tid = threadIdx.x;
+    auto comp_at = [&](int i, uint64_t &c) -> bool {
+        const int e = (i / VW) * (NTHREADS * VW) + tid * VW + (i % VW);
+        if (e >= n) return false;
+        const uint32_t k = cand_key(T::load1(rowp, c0 + e));
+        c = composite(k, (uint32_t)(c0 + e));
+        return k >= 1;
+    };
+    const uint64_t kth = radix_kth(
+        [&](auto fn) {
+#pragma unroll 1
+            for (int i = 0; i < EPT; i++) {
+                uint64_t c;
+                if (comp_at(i, c)) fn(c);
+            }
+        },
+        K, sm);
+    int c2 = 0;
+#pragma unroll 1
+    for (int i = 0; i < EPT; i++) {
+        uint64_t c;
+        c2 += comp_at(i, c) && c >= kth;
+    }
+    int tot2;
+    int o2 = block_excl_scan(c2, &tot2, sm.scan);
+#pragma unroll 1
+    for (int i = 0; i < EPT; i++) {
+        uint64_t c;
+        if (comp_at(i, c) && c >= kth) sm.L[o2++] = c;
+    }
+    __syncthreads();
+    sort_list_desc(sm, tot2);
+    return K;
+}
+
+// Stage 1 on one chunk [c0, c0 + n) of a row: the chunk's top min(K, valid)
+// candidates as composites, sorted descending, in sm.L[0..m).  Returns m.
+template <int DT, int EPT, bool VEC>
+__device__ __forceinline__ int chunk_select(const SampleArgs &a, int row, int64_t c0, int n, int K, TopkSmem &sm)
+{
+    using T = DtypeTraits<DT>;
+    constexpr int VW = T::VW;
+    const int tid = threadIdx.x;
     const void *rowp = (const char *)a.logits + (int64_t)row * a.row_stride * T::ESIZE;
 
     float x[EPT];
@@ -407,29 +456,22 @@ __global__ void __launch_bounds__(NTHREADS) topk_chunk_kernel(SampleArgs a)
         sort_list_desc(sm, total);
         m = total < K ? total : K;
     } else {
-        const uint64_t kth = radix_kth(
-            [&](auto fn) {
-#pragma unroll
-                for (int i = 0; i < EPT; i++)
-                    if (key[i] >= 1) fn(composite(key[i], idof(i)));
-            },
-            K, sm);
-        int c2 = 0;
-#pragma unroll
-        for (int i = 0; i < EPT; i++) c2 += key[i] >= 1 && composite(key[i], idof(i)) >= kth;
-        int tot2;
-        int o2 = block_excl_scan(c2, &tot2, sm.scan);
-#pragma unroll
-        for (int i = 0; i < EPT; i++) {
-            if (key[i] >= 1) {
-                const uint64_t v = composite(key[i], idof(i));
-                if (v >= kth) sm.L[o2++] = v;
-            }
-        }
-        __syncthreads();
-        sort_list_desc(sm, tot2);
-        m = K;
+        m = chunk_select_radix<DT, EPT>(rowp, c0, n, K, sm);
     }
+    return m;
+}
+
+template <int DT, int EPT, bool VEC>
+__global__ void __launch_bounds__(NTHREADS) topk_chunk_kernel(SampleArgs a)
+{
+    __shared__ TopkSmem sm;
+    const int row = blockIdx.y, chunk = blockIdx.x, tid = threadIdx.x;
+    const g4s_params p = a.params.get(row);
+    const int K = p.top_k;
+    if (!(K > 0 && K < a.vocab && K <= KMAX)) return;
+    const int64_t c0 = (int64_t)chunk * a.chunk;
+    const int n = (int)min((int64_t)a.chunk, (int64_t)a.vocab - c0);
+    const int m = chunk_select<DT, EPT, VEC>(a, row, c0, n, K, sm);
     uint64_t *out = a.cand + ((int64_t)row * a.nch + chunk) * KMAX;
     for (int i = tid; i < m; i += NTHREADS) out[i] = sm.L[i];
     if (tid == 0) a.cand_cnt[(int64_t)row * a.nch + chunk] = m;
@@ -445,6 +487,101 @@ __global__ void __launch_bounds__(NTHREADS) topk_chunk_kernel(SampleArgs a)
 }
 
 // ---------------------------------------------------------------------------
+// Latency path for a few rows: one cluster of CLUSTER CTAs per row, each CTA a
+// CSLICE-id slice (64 logits per thread).  The per-CTA candidate lists stay in
+// shared memory; after one cluster barrier CTA 0 reads them through
+// distributed shared memory (no global round trip, no fence, no arrival
+// counter): with T = the smallest of the lists' ceil(K/16)-th entries (a lower
+// bound on the row's K-th largest), it keeps the entries >= T (120-190 for
+// K = 64 on Gaussian logits), sorts them, and runs the same tail as the
+// chunked path.  A second
+// cluster barrier keeps the other CTAs' shared memory alive until CTA 0 has
+// read it.
+// ---------------------------------------------------------------------------
+constexpr int CEPT = 64;
+constexpr int CSLICE = CEPT * NTHREADS;  // 16384 ids per CTA
+
+template <int DT, bool VEC>
+__global__ void __launch_bounds__(NTHREADS, 1) topk_cluster_kernel(SampleArgs a)
+{
+    namespace cg = cooperative_groups;
+    static_assert(TOPK_CLUSTER * TOPK_CLUSTER_KMAX <= CAP2 / 2, "the gathered lists fit half of sm.L");
+    static_assert(TOPK_CLUSTER * TOPK_CLUSTER_KMAX % NTHREADS == 0, "whole gather slots per thread");
+    cg::cluster_group cluster = cg::this_cluster();
+    __shared__ TopkSmem sm;
+    __shared__ int s_cnt;
+    __shared__ int rc[TOPK_CLUSTER];
+    __shared__ uint64_t rk[1];
+    const int rank = (int)cluster.block_rank();
+    const int row = blockIdx.x / TOPK_CLUSTER, tid = threadIdx.x;
+    const g4s_params p = a.params.get(row);
+    const int K = p.top_k;
+    // the host sends rows with top_k <= TOPK_CLUSTER_KMAX here; others return
+    // (the whole cluster: one row)
+    if (!(K > 0 && K < a.vocab && K <= TOPK_CLUSTER_KMAX)) return;
+    const int64_t c0 = (int64_t)rank * CSLICE;
+    const int n = (int)max((int64_t)0, min((int64_t)CSLICE, (int64_t)a.vocab - c0));
+    const int m = chunk_select<DT, CEPT, VEC>(a, row, c0, n, K, sm);
+    if (tid == 0) s_cnt = m;
+    cluster.sync();  // every CTA's list is in its shared memory
+
+    // CTA 0: the gathered lists in sm.L[c * KS + i] (KS = TOPK_CLUSTER_KMAX; its
+    // own list is list 0 and is rewritten in place with its own values), the
+    // entries kept for the final sort in W
+    constexpr int KS = TOPK_CLUSTER_KMAX, SPT = TOPK_CLUSTER * KS / NTHREADS;
+    uint64_t *G = sm.L;
+    uint64_t *W = sm.L + CAP2 / 2;
+    int n2 = 0;
+    if (rank == 0) {
+        if (tid < TOPK_CLUSTER) rc[tid] = *cluster.map_shared_rank(&s_cnt, tid);
+        __syncthreads();
+        {
+            uint64_t v[SPT];
+#pragma unroll
+            for (int q = 0; q < SPT; q++) {
+                const int f = tid + q * NTHREADS, c = f / KS, i = f % KS;
+                v[q] = i < rc[c] ? cluster.map_shared_rank(sm.L, c)[i] : 0;
+            }
+            __syncthreads();
+#pragma unroll
+            for (int q = 0; q < SPT; q++) G[tid + q * NTHREADS] = v[q];
+        }
+        // lower bound on the row's K-th largest: with j0 = ceil(K / lists), each
+        // list holds j0 entries at or above its j0-th, so the smallest j0-th
+        // entry has at least K entries at or above it (no bound, T = 1, when a
+        // list is shorter than j0)
+        const int j0 = (K + TOPK_CLUSTER - 1) / TOPK_CLUSTER;
+        if (tid < 32) {
+            uint64_t h = ~0ull;
+            if (tid < TOPK_CLUSTER) h = rc[tid] >= j0 ? cluster.map_shared_rank(sm.L, tid)[j0 - 1] : 0;
+#pragma unroll
+            for (int d = 16; d > 0; d >>= 1) {
+                const uint64_t o = __shfl_xor_sync(FULLMASK, h, d);
+                h = o < h ? o : h;
+            }
+            if (tid == 0) rk[0] = h ? h : 1;
+        }
+        __syncthreads();
+        const uint64_t T = rk[0];
+        int cnt = 0;
+#pragma unroll
+        for (int q = 0; q < SPT; q++) cnt += G[tid + q * NTHREADS] >= T;
+        int off = block_excl_scan(cnt, &n2, sm.scan);
+#pragma unroll
+        for (int q = 0; q < SPT; q++) {
+            const uint64_t e = G[tid + q * NTHREADS];
+            if (e >= T) W[off++] = e;
+        }
+    }
+    cluster.sync();  // CTA 0 is done reading the other CTAs' shared memory
+    if (rank != 0) return;
+    for (int i = tid; i < n2; i += NTHREADS) sm.L[i] = W[i];
+    __syncthreads();
+    sort_list_desc(sm, n2);
+    finish_row(a, row, p, n2 < K ? n2 : K, sm);
+}
+
+// ---------------------------------------------------------------------------
 // launcher
 // ---------------------------------------------------------------------------
 template <int DT, int EPT, bool VEC>
@@ -453,6 +590,57 @@ static cudaError_t launch_topk_t(const SampleArgs &a, cudaStream_t s)
     dim3 grid(a.nch, a.rows);
     topk_chunk_kernel<DT, EPT, VEC><<<grid, NTHREADS, 0, s>>>(a);
     return cudaGetLastError();
+}
+
+template <int DT, bool VEC>
+static cudaError_t launch_cluster_t(const SampleArgs &a, cudaStream_t s)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(a.rows * TOPK_CLUSTER));
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = TOPK_CLUSTER;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, topk_cluster_kernel<DT, VEC>, a);
+}
+
+cudaError_t launch_topk_cluster(const SampleArgs &a, bool vec, cudaStream_t s)
+{
+    if (a.dtype == G4S_F32) return vec ? launch_cluster_t<G4S_F32, true>(a, s) : launch_cluster_t<G4S_F32, false>(a, s);
+    return vec ? launch_cluster_t<G4S_BF16, true>(a, s) : launch_cluster_t<G4S_BF16, false>(a, s);
+}
+
+template <int DT, bool VEC>
+static bool cluster_ok_t()
+{
+    if (cudaFuncSetAttribute(topk_cluster_kernel<DT, VEC>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
+        cudaSuccess)
+        return false;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(TOPK_CLUSTER);
+    cfg.blockDim = dim3(NTHREADS);
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = TOPK_CLUSTER;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int nc = 0;
+    return cudaOccupancyMaxActiveClusters(&nc, topk_cluster_kernel<DT, VEC>, &cfg) == cudaSuccess && nc > 0;
+}
+
+bool topk_cluster_available()
+{
+    const bool ok = cluster_ok_t<G4S_F32, true>() && cluster_ok_t<G4S_F32, false>() &&
+                    cluster_ok_t<G4S_BF16, true>() && cluster_ok_t<G4S_BF16, false>();
+    cudaGetLastError();
+    return ok;
 }
 
 cudaError_t launch_topk(const SampleArgs &a, int ept, bool vec, cudaStream_t s)

@@ -162,3 +162,20 @@ def test_argument_errors(sampler, torch_cuda, g4):
     pg = g4.make_params(0.0, 5, 0.9)
     assert sampler.sample(x.data_ptr(), F32, 2, 100, 100, pg, CAP, 0, out.data_ptr(), check=False) == g4.OK
     torch.cuda.synchronize()
+
+
+def test_single_row_cluster_merge_paths(sampler, torch_cuda, oracle, g4):
+    # Rows of a small batch take the one-cluster-per-row kernel (16 slices of
+    # 16384 ids).  Row 0 interleaves the slices' top entries so that more than
+    # half of all list entries lie at or above the merge bound (the heavy-tie
+    # merge through the workspace); row 1 keeps them apart (the direct merge).
+    V, K = 262144, 200
+    x = np.full((2, V), -1e30, dtype=np.float32)
+    for c in range(16):
+        i = np.arange(K)
+        pos = c * 16384 + (i * 37) % 16384
+        x[0, pos] = 1.0 + (i * 16 + c) * 1e-3
+        x[1, pos] = 1.0 + c + i * 1e-3
+    u = np.array([0.37, 0.81])
+    for T in (1.0, 0.0):
+        _both(sampler, torch_cuda, oracle, x, F32, g4.make_params(T, K, 0.9), CAP, u)
