@@ -4,6 +4,9 @@
 
 #include <algorithm>
 
+#include <dlfcn.h>
+#include <nccl.h>
+
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -44,6 +47,11 @@ struct g4s_ctx {
     g4s_params *params_pinned = nullptr;
     cudaEvent_t params_ev = nullptr;
     bool params_ev_pending = false;
+    // vocabulary-sharded mode (g4s_shard_init)
+    void *nccl_comm = nullptr;
+    int shard_world = 0, shard_rank = 0, shard_vocab = 0, shard_slice = 0;
+    uint64_t *sh_send = nullptr;  // [max_rows][KMAX] this rank's lists, then [max_rows] counts
+    uint64_t *sh_recv = nullptr;  // [world][max_rows][KMAX], then [world][max_rows] counts
     // g4s_sample_host staging
     void *h_logits = nullptr;
     double *h_u = nullptr;
@@ -90,6 +98,116 @@ static int choose_ept(const g4s_ctx *ctx, int rows, int vocab)
     const int64_t big = ceil_div(vocab, 8192);
     if ((int64_t)rows * big < 2LL * ctx->sm_count && ceil_div(vocab, 2048) <= NCH_MAX_) return 8;
     return 32;
+}
+
+// NCCL, loaded on first use of the sharded API (the rest of the library does
+// not depend on it).  A process that already holds libnccl.so.2 (PyTorch's,
+// for instance) shares that copy.
+struct NcclApi {
+    bool tried = false, ok = false;
+    std::string why;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*GroupStart)() = nullptr;
+    ncclResult_t (*GroupEnd)() = nullptr;
+    const char *(*GetErrorString)(ncclResult_t) = nullptr;
+};
+static NcclApi g_nccl;
+
+static bool nccl_load()
+{
+    if (g_nccl.tried) return g_nccl.ok;
+    g_nccl.tried = true;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_LOCAL);
+    if (!h) {
+        g_nccl.why = std::string("cannot load libnccl.so.2: ") + dlerror();
+        return false;
+    }
+    bool ok = true;
+    auto sym = [&](auto &fn, const char *name) {
+        fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(h, name));
+        if (!fn) ok = false;
+    };
+    sym(g_nccl.GetUniqueId, "ncclGetUniqueId");
+    sym(g_nccl.CommInitRank, "ncclCommInitRank");
+    sym(g_nccl.CommDestroy, "ncclCommDestroy");
+    sym(g_nccl.CommAbort, "ncclCommAbort");
+    sym(g_nccl.AllGather, "ncclAllGather");
+    sym(g_nccl.GroupStart, "ncclGroupStart");
+    sym(g_nccl.GroupEnd, "ncclGroupEnd");
+    sym(g_nccl.GetErrorString, "ncclGetErrorString");
+    if (!ok) g_nccl.why = "libnccl.so.2 lacks an expected symbol";
+    g_nccl.ok = ok;
+    return ok;
+}
+
+static void shard_release(g4s_ctx *ctx)
+{
+    if (ctx->nccl_comm && g_nccl.ok) g_nccl.CommDestroy((ncclComm_t)ctx->nccl_comm);
+    ctx->nccl_comm = nullptr;
+    if (ctx->sh_send) cudaFree(ctx->sh_send);
+    if (ctx->sh_recv) cudaFree(ctx->sh_recv);
+    ctx->sh_send = ctx->sh_recv = nullptr;
+    ctx->shard_world = 0;
+}
+
+// Per-row parameters into the launch arguments: a broadcast record travels in
+// the kernel arguments; per-row records go through the pinned staging buffer
+// (with fl32(1/T) computed here, the same IEEE division as on the device).
+static int32_t stage_params(g4s_ctx *ctx, const char *who, const g4s_params *params, int32_t params_stride,
+                            int rows, cudaStream_t s, RowParams &out)
+{
+    if (params_stride) {
+        // the pinned staging may still feed the previous call's copy
+        if (ctx->params_ev_pending && cudaEventSynchronize(ctx->params_ev) != cudaSuccess)
+            return fail(ctx, G4S_ERR_CUDA, "%s: waiting on the previous params copy failed", who);
+        memcpy(ctx->params_pinned, params, (size_t)rows * sizeof(g4s_params));
+        float *inv_t = (float *)(ctx->params_pinned + rows);
+        for (int r = 0; r < rows; r++) {
+            const float T = params[r].temperature;
+            inv_t[r] = (T > 0.0f && T != 1.0f) ? 1.0f / T : 1.0f;
+        }
+        if (cudaMemcpyAsync(ctx->params_dev, ctx->params_pinned, (size_t)rows * (sizeof(g4s_params) + sizeof(float)),
+                            cudaMemcpyHostToDevice, s) != cudaSuccess ||
+            cudaEventRecord(ctx->params_ev, s) != cudaSuccess) {
+            cudaError_t e = cudaGetLastError();
+            return fail(ctx, G4S_ERR_CUDA, "%s: params upload failed: %s", who, cudaGetErrorString(e));
+        }
+        ctx->params_ev_pending = true;
+        out.dev = ctx->params_dev;
+        out.inv_t_dev = (const float *)(ctx->params_dev + rows);
+    } else {
+        out.dev = nullptr;
+        out.p0 = params[0];
+        const float T = params[0].temperature;
+        out.inv_t0 = (T > 0.0f && T != 1.0f) ? 1.0f / T : 1.0f;
+    }
+    return G4S_OK;
+}
+
+// Checks that every row is a top-K row of the sharded path: 0 < top_k <= 256,
+// top_k below both the slice and the full vocabulary.
+static int32_t check_shard_rows(g4s_ctx *ctx, const char *who, const g4s_params *params, int32_t params_stride,
+                                int rows, int slice_vocab, int vocab_total, bool *any_draw)
+{
+    const int nparam = params_stride ? rows : 1;
+    *any_draw = false;
+    for (int r = 0; r < nparam; r++) {
+        const g4s_params &p = params[r];
+        if (p.temperature != p.temperature || p.top_p != p.top_p)
+            return fail(ctx, G4S_ERR_ARG, "%s: NaN temperature/top_p in params[%d]", who, r);
+        if (p.top_k <= 0 || p.top_k > KMAX_ || p.top_k >= vocab_total || (slice_vocab > 0 && p.top_k >= slice_vocab))
+            return fail(ctx, G4S_ERR_ARG,
+                        "%s: params[%d].top_k = %d; the sharded path takes 0 < top_k <= %d below the slice (%d) "
+                        "and the vocabulary (%d); sample full-vocabulary rows with a row split",
+                        who, r, p.top_k, KMAX_, slice_vocab, vocab_total);
+        if (p.temperature > 0.0f) *any_draw = true;
+    }
+    return G4S_OK;
 }
 
 extern "C" {
@@ -239,6 +357,7 @@ int32_t g4s_destroy(g4s_ctx *ctx)
     if (ctx->h_logits) cudaFree(ctx->h_logits);
     if (ctx->h_u) cudaFree(ctx->h_u);
     if (ctx->h_tok) cudaFree(ctx->h_tok);
+    shard_release(ctx);
     delete ctx;
     return G4S_OK;
 }
@@ -327,30 +446,9 @@ int32_t g4s_sample_ex(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t r
     a.rowstat = ctx->rowstat;
     a.lk_idx = ctx->lk_idx;
     a.lk_val = ctx->lk_val;
-    if (params_stride) {
-        // the pinned staging may still feed the previous call's copy
-        if (ctx->params_ev_pending && cudaEventSynchronize(ctx->params_ev) != cudaSuccess)
-            return fail(ctx, G4S_ERR_CUDA, "g4s_sample: waiting on the previous params copy failed");
-        memcpy(ctx->params_pinned, params, (size_t)rows * sizeof(g4s_params));
-        float *inv_t = (float *)(ctx->params_pinned + rows);
-        for (int r = 0; r < rows; r++) {
-            const float T = params[r].temperature;
-            inv_t[r] = (T > 0.0f && T != 1.0f) ? 1.0f / T : 1.0f;  // IEEE division, as on the device
-        }
-        if (cudaMemcpyAsync(ctx->params_dev, ctx->params_pinned, (size_t)rows * (sizeof(g4s_params) + sizeof(float)),
-                            cudaMemcpyHostToDevice, s) != cudaSuccess ||
-            cudaEventRecord(ctx->params_ev, s) != cudaSuccess) {
-            cudaError_t e = cudaGetLastError();
-            return fail(ctx, G4S_ERR_CUDA, "g4s_sample: params upload failed: %s", cudaGetErrorString(e));
-        }
-        ctx->params_ev_pending = true;
-        a.params.dev = ctx->params_dev;
-        a.params.inv_t_dev = (const float *)(ctx->params_dev + rows);
-    } else {
-        a.params.dev = nullptr;
-        a.params.p0 = params[0];
-        const float T = params[0].temperature;
-        a.params.inv_t0 = (T > 0.0f && T != 1.0f) ? 1.0f / T : 1.0f;
+    {
+        const int32_t rc = stage_params(ctx, "g4s_sample", params, params_stride, rows, s, a.params);
+        if (rc != G4S_OK) return rc;
     }
 
     cudaError_t e = cudaSuccess;
@@ -403,6 +501,190 @@ int32_t g4s_sample_host(g4s_ctx *ctx, const void *host_logits, int32_t dtype, in
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "g4s_sample_host: %s", cudaGetErrorString(e));
     return G4S_OK;
+}
+
+// ---------------------------------------------------------------------------
+// vocabulary-sharded mode
+// ---------------------------------------------------------------------------
+int32_t g4s_shard_lists(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t rows, int32_t slice_vocab,
+                        int64_t row_stride, int32_t id_offset, int32_t vocab_total, const g4s_params *params,
+                        int32_t params_stride, uint64_t *out_lists, int32_t *out_counts, void *stream)
+{
+    static const char *who = "g4s_shard_lists";
+    if (!ctx) return fail(nullptr, G4S_ERR_ARG, "%s: ctx is NULL", who);
+    if (!logits || !params || !out_lists || !out_counts)
+        return fail(ctx, G4S_ERR_ARG, "%s: logits, params, out_lists and out_counts must be non-NULL", who);
+    if (dtype != G4S_F32 && dtype != G4S_BF16) return fail(ctx, G4S_ERR_ARG, "%s: bad dtype %d", who, dtype);
+    if (rows < 1 || slice_vocab < 1 || rows > ctx->max_rows || slice_vocab > ctx->max_vocab)
+        return fail(ctx, G4S_ERR_CAPACITY, "%s: rows %d / slice %d outside the context (%d / %d)", who, rows,
+                    slice_vocab, ctx->max_rows, ctx->max_vocab);
+    if (row_stride < slice_vocab) return fail(ctx, G4S_ERR_ARG, "%s: row_stride < slice_vocab", who);
+    if (id_offset < 0 || vocab_total < 1 || (int64_t)id_offset + slice_vocab > vocab_total)
+        return fail(ctx, G4S_ERR_ARG, "%s: slice [%d, %lld) outside the vocabulary %d", who, id_offset,
+                    (long long)id_offset + slice_vocab, vocab_total);
+    if (params_stride != 0 && params_stride != 1)
+        return fail(ctx, G4S_ERR_ARG, "%s: params_stride must be 0 or 1", who);
+    bool any_draw;
+    int32_t rc = check_shard_rows(ctx, who, params, params_stride, rows, slice_vocab, vocab_total, &any_draw);
+    if (rc != G4S_OK) return rc;
+    const int esize = dtype == G4S_F32 ? 4 : 2;
+    const bool vec = ((uintptr_t)logits % 16u == 0) && (((int64_t)row_stride * esize) % 16 == 0);
+    const int ept = choose_ept(ctx, rows, slice_vocab);
+    const int nch = (int)ceil_div(slice_vocab, ept * 256);
+    if (nch > NCH_MAX_ || (int64_t)rows * nch > ctx->lists_cap)
+        return fail(ctx, G4S_ERR_CAPACITY, "%s: %d rows x %d chunks exceed the workspace", who, rows, nch);
+    DeviceGuard guard(ctx->device);
+    if (!guard.ok) return fail(ctx, G4S_ERR_CUDA, "%s: cannot select device %d", who, ctx->device);
+    cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
+    SampleArgs a;
+    memset(&a, 0, sizeof(a));
+    a.logits = logits;
+    a.row_stride = row_stride;
+    a.rows = rows;
+    a.vocab = slice_vocab;
+    a.dtype = dtype;
+    a.chunk = ept * 256;
+    a.nch = nch;
+    a.cand = ctx->cand;
+    a.cand_cnt = ctx->cand_cnt;
+    a.counters_topk = ctx->counters_topk;
+    a.id_offset = id_offset;
+    a.list_out = out_lists;
+    a.list_cnt = out_counts;
+    rc = stage_params(ctx, who, params, params_stride, rows, s, a.params);
+    if (rc != G4S_OK) return rc;
+    cudaError_t e = launch_topk(a, ept, vec, s);
+    if (e != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "%s: launch failed: %s", who, cudaGetErrorString(e));
+    return G4S_OK;
+}
+
+int32_t g4s_shard_merge(g4s_ctx *ctx, const uint64_t *lists, const int32_t *counts, int32_t world, int32_t rows,
+                        int32_t vocab_total, const g4s_params *params, int32_t params_stride, float softcap,
+                        const double *u, int32_t *out_tokens, const g4s_outputs *extra, void *stream)
+{
+    static const char *who = "g4s_shard_merge";
+    if (!ctx) return fail(nullptr, G4S_ERR_ARG, "%s: ctx is NULL", who);
+    if (!lists || !counts || !params || !out_tokens)
+        return fail(ctx, G4S_ERR_ARG, "%s: lists, counts, params and out_tokens must be non-NULL", who);
+    if (world < 1 || world > NCH_MAX_) return fail(ctx, G4S_ERR_ARG, "%s: world %d outside [1, %d]", who, world, NCH_MAX_);
+    if (rows < 1 || rows > ctx->max_rows) return fail(ctx, G4S_ERR_CAPACITY, "%s: rows %d outside [1, %d]", who, rows, ctx->max_rows);
+    if (params_stride != 0 && params_stride != 1)
+        return fail(ctx, G4S_ERR_ARG, "%s: params_stride must be 0 or 1", who);
+    bool any_draw;
+    int32_t rc = check_shard_rows(ctx, who, params, params_stride, rows, 0, vocab_total, &any_draw);
+    if (rc != G4S_OK) return rc;
+    if (any_draw && !u) return fail(ctx, G4S_ERR_ARG, "%s: u is NULL but a row has temperature > 0", who);
+    g4s_outputs ex;
+    memset(&ex, 0, sizeof(ex));
+    if (extra) ex = *extra;
+    int max_k = 0;
+    for (int r = 0; r < (params_stride ? rows : 1); r++) max_k = params[r].top_k > max_k ? params[r].top_k : max_k;
+    if ((ex.cand_ids || ex.cand_probs) && ex.cand_stride < max_k)
+        return fail(ctx, G4S_ERR_ARG, "%s: cand_stride %d < largest top_k %d", who, ex.cand_stride, max_k);
+    DeviceGuard guard(ctx->device);
+    if (!guard.ok) return fail(ctx, G4S_ERR_CUDA, "%s: cannot select device %d", who, ctx->device);
+    cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
+    SampleArgs a;
+    memset(&a, 0, sizeof(a));
+    a.rows = rows;
+    a.vocab = vocab_total;
+    a.softcap = softcap;
+    a.invcap = softcap > 0.0f ? 1.0f / softcap : 0.0f;
+    a.u = u;
+    a.out_tokens = out_tokens;
+    a.token_prob = ex.token_prob;
+    a.row_flags = ex.row_flags;
+    a.cand_ids = ex.cand_ids;
+    a.cand_probs = ex.cand_probs;
+    a.cand_stride = ex.cand_stride;
+    a.glists = lists;
+    a.gcnts = counts;
+    a.gworld = world;
+    rc = stage_params(ctx, who, params, params_stride, rows, s, a.params);
+    if (rc != G4S_OK) return rc;
+    cudaError_t e = launch_shard_merge(a, s);
+    if (e != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "%s: launch failed: %s", who, cudaGetErrorString(e));
+    return G4S_OK;
+}
+
+int32_t g4s_shard_unique_id(uint8_t *uid)
+{
+    if (!uid) return fail(nullptr, G4S_ERR_ARG, "g4s_shard_unique_id: uid is NULL");
+    if (!nccl_load()) return fail(nullptr, G4S_ERR_UNAVAILABLE, "g4s_shard_unique_id: %s", g_nccl.why.c_str());
+    static_assert(sizeof(ncclUniqueId) == G4S_SHARD_UID_BYTES, "NCCL unique id size");
+    ncclUniqueId id;
+    const ncclResult_t r = g_nccl.GetUniqueId(&id);
+    if (r != ncclSuccess) return fail(nullptr, G4S_ERR_NCCL, "ncclGetUniqueId: %s", g_nccl.GetErrorString(r));
+    memcpy(uid, &id, sizeof(id));
+    return G4S_OK;
+}
+
+int32_t g4s_shard_init(g4s_ctx *ctx, int32_t world, int32_t rank, int32_t vocab_total, const uint8_t *uid)
+{
+    static const char *who = "g4s_shard_init";
+    if (!ctx) return fail(nullptr, G4S_ERR_ARG, "%s: ctx is NULL", who);
+    if (!uid || world < 1 || world > 64 || rank < 0 || rank >= world || vocab_total < world)
+        return fail(ctx, G4S_ERR_ARG, "%s: bad world %d / rank %d / vocab %d", who, world, rank, vocab_total);
+    const int slice = (int)ceil_div(vocab_total, world);
+    if (slice > ctx->max_vocab)
+        return fail(ctx, G4S_ERR_CAPACITY, "%s: slice %d exceeds the context's max_vocab %d", who, slice, ctx->max_vocab);
+    if (ctx->nccl_comm) return fail(ctx, G4S_ERR_STATE, "%s: the context is already sharded", who);
+    if (!nccl_load()) return fail(ctx, G4S_ERR_UNAVAILABLE, "%s: %s", who, g_nccl.why.c_str());
+    DeviceGuard guard(ctx->device);
+    if (!guard.ok) return fail(ctx, G4S_ERR_CUDA, "%s: cannot select device %d", who, ctx->device);
+    const size_t per_rank = (size_t)ctx->max_rows * (KMAX_ + 1) * sizeof(uint64_t);
+    if (cudaMalloc(&ctx->sh_send, per_rank) != cudaSuccess ||
+        cudaMalloc(&ctx->sh_recv, per_rank * (size_t)world) != cudaSuccess) {
+        cudaGetLastError();
+        shard_release(ctx);
+        return fail(ctx, G4S_ERR_NOMEM, "%s: cannot allocate the exchange buffers", who);
+    }
+    ncclUniqueId id;
+    memcpy(&id, uid, sizeof(id));
+    ncclComm_t comm = nullptr;
+    const ncclResult_t r = g_nccl.CommInitRank(&comm, world, id, rank);
+    if (r != ncclSuccess) {
+        shard_release(ctx);
+        return fail(ctx, G4S_ERR_NCCL, "%s: ncclCommInitRank: %s", who, g_nccl.GetErrorString(r));
+    }
+    ctx->nccl_comm = comm;
+    ctx->shard_world = world;
+    ctx->shard_rank = rank;
+    ctx->shard_vocab = vocab_total;
+    ctx->shard_slice = slice;
+    return G4S_OK;
+}
+
+int32_t g4s_shard_sample(g4s_ctx *ctx, const void *logits_slice, int32_t dtype, int32_t rows, int64_t row_stride,
+                         const g4s_params *params, int32_t params_stride, float softcap, const double *u,
+                         int32_t *out_tokens, const g4s_outputs *extra, void *stream)
+{
+    static const char *who = "g4s_shard_sample";
+    if (!ctx) return fail(nullptr, G4S_ERR_ARG, "%s: ctx is NULL", who);
+    if (!ctx->nccl_comm) return fail(ctx, G4S_ERR_STATE, "%s: call g4s_shard_init first", who);
+    const int W = ctx->shard_world, Vs = ctx->shard_slice;
+    const int off = ctx->shard_rank * Vs;
+    const int n = std::min(Vs, ctx->shard_vocab - off);
+    if (rows < 1 || rows > ctx->max_rows) return fail(ctx, G4S_ERR_CAPACITY, "%s: rows %d outside [1, %d]", who, rows, ctx->max_rows);
+    cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
+    uint64_t *send = ctx->sh_send;
+    int32_t *send_cnt = (int32_t *)(ctx->sh_send + (size_t)ctx->max_rows * KMAX_);
+    uint64_t *recv = ctx->sh_recv;
+    int32_t *recv_cnt = (int32_t *)(ctx->sh_recv + (size_t)W * ctx->max_rows * KMAX_);
+    int32_t rc = g4s_shard_lists(ctx, logits_slice, dtype, rows, n, row_stride, off, ctx->shard_vocab, params,
+                                 params_stride, send, send_cnt, s);
+    if (rc != G4S_OK) return rc;
+    DeviceGuard guard(ctx->device);
+    ncclComm_t comm = (ncclComm_t)ctx->nccl_comm;
+    ncclResult_t r = g_nccl.GroupStart();
+    if (r == ncclSuccess) r = g_nccl.AllGather(send, recv, (size_t)rows * KMAX_, ncclUint64, comm, s);
+    if (r == ncclSuccess) r = g_nccl.AllGather(send_cnt, recv_cnt, (size_t)rows, ncclInt32, comm, s);
+    const ncclResult_t r2 = g_nccl.GroupEnd();
+    if (r == ncclSuccess) r = r2;
+    if (r != ncclSuccess) return fail(ctx, G4S_ERR_NCCL, "%s: all-gather: %s", who, g_nccl.GetErrorString(r));
+    // the merge reads list w of row i at recv + w * rows * KMAX + i * KMAX
+    return g4s_shard_merge(ctx, recv, recv_cnt, W, rows, ctx->shard_vocab, params, params_stride, softcap, u,
+                           out_tokens, extra, s);
 }
 
 }  // extern "C"

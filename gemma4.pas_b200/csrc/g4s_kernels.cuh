@@ -58,6 +58,13 @@ struct SampleArgs {
     RowStat *rowstat;          // [rows]
     int32_t *lk_idx;           // [lk_slots][vocab]
     float *lk_val;             // [lk_slots][vocab]
+    // vocabulary-sharded mode
+    int32_t id_offset;         // global vocab id of this slice's first logit
+    uint64_t *list_out;        // non-null: the chunked top-K path writes each row's sorted
+    int32_t *list_cnt;         //   top-K composites ([rows][KMAX], global ids) instead of sampling
+    const uint64_t *glists;    // shard merge: gathered lists [gworld][rows][KMAX]
+    const int32_t *gcnts;      //   and their lengths [gworld][rows]
+    int32_t gworld;
 };
 
 // Single-row latency path of the top-K selection: one cluster of TOPK_CLUSTER
@@ -73,6 +80,9 @@ cudaError_t launch_full(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
 cudaError_t launch_full_probs(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
 cudaError_t launch_largek(const SampleArgs &a, cudaStream_t s);
 cudaError_t launch_topk_cluster(const SampleArgs &a, bool vec, cudaStream_t s);
+// Vocabulary-sharded mode: the gathered per-shard lists merged into each row's
+// top-K, then the sampling tail (one CTA per row).
+cudaError_t launch_shard_merge(const SampleArgs &a, cudaStream_t s);
 // Whether a TOPK_CLUSTER-CTA cluster of the latency kernel can be scheduled.
 bool topk_cluster_available();
 // Logits per item of the full-path streaming kernel (one float4 of statistics each).

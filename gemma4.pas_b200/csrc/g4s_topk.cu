@@ -270,18 +270,21 @@ __device__ __forceinline__ void finish_row(const SampleArgs &a, int row, const g
     if (tid < 32) topk_tail(a, row, p, kw, sm);
 }
 
-// Stage 2 of a row (last-arriving CTA): merge the per-chunk lists and sample.
-__device__ void topk_merge(const SampleArgs &a, int row, const g4s_params &p, TopkSmem &sm)
+// Merge of nch descending candidate lists (list c: C + c * lstride, length
+// CC[c * cstride]) into the top min(K, entries) composites, sorted descending in
+// sm.L[0..kw).  With j = ceil(K / nch), the ceil(K/j)-th largest of the lists'
+// j-th entries is a lower bound on the K-th largest; the entries above it are
+// gathered (a prefix of each list), sorted and cut to K.  Returns kw.
+__device__ int merge_lists(int K, TopkSmem &sm, const uint64_t *C, int64_t lstride, const int32_t *CC,
+                           int64_t cstride, int nch)
 {
-    const int K = p.top_k, nch = a.nch, tid = threadIdx.x;
-    const uint64_t *C = a.cand + (int64_t)row * nch * KMAX;
-    const int32_t *CC = a.cand_cnt + (int64_t)row * nch;
+    const int tid = threadIdx.x;
     const int j = (K + nch - 1) / nch;
     const int mm = (K + j - 1) / j;
-    // lower bound t2: the mm-th largest of the chunks' j-th entries
+    // lower bound t2: the mm-th largest of the lists' j-th entries
     for (int c = tid; c < nch; c += NTHREADS) {
         uint64_t h = 0;
-        if (__ldcg(&CC[c]) >= j) h = __ldcg(&C[(int64_t)c * KMAX + j - 1]);
+        if (__ldcg(&CC[c * cstride]) >= j) h = __ldcg(&C[c * lstride + j - 1]);
         sm.L[c] = h;
     }
     __syncthreads();
@@ -308,59 +311,87 @@ __device__ void topk_merge(const SampleArgs &a, int row, const g4s_params &p, To
     }
     if (t2 == 0) t2 = 1;  // every list entry is a valid candidate
     __syncthreads();
-    // candidates >= t2: a prefix of each chunk's descending list
+    // candidates >= t2: a prefix of each descending list
     constexpr int CPT = NCH_MAX / NTHREADS;
     int pc[CPT];
     int cnt = 0;
 #pragma unroll
     for (int r = 0; r < CPT; r++) {
         const int c = tid * CPT + r;
-        pc[r] = c < nch ? prefix_at_least(C + (int64_t)c * KMAX, __ldcg(&CC[c]), t2) : 0;
+        pc[r] = c < nch ? prefix_at_least(C + c * lstride, __ldcg(&CC[c * cstride]), t2) : 0;
         cnt += pc[r];
     }
     const int slots = nch * K;
     int total;
     int off = block_excl_scan(cnt, &total, sm.scan);
-    int kw;
     if (total <= CAP2 / 2) {
 #pragma unroll
         for (int r = 0; r < CPT; r++) {
-            const uint64_t *list = C + (int64_t)(tid * CPT + r) * KMAX;
+            const uint64_t *list = C + (tid * CPT + r) * lstride;
             for (int i = 0; i < pc[r]; i++) sm.L[off++] = __ldcg(&list[i]);
         }
         __syncthreads();
         sort_list_desc(sm, total);
-        kw = total < K ? total : K;
-    } else {
-        // heavy ties: exact radix selection over all list entries
-        const uint64_t kth = radix_kth(
-            [&](auto fn) {
-                for (int s = tid; s < slots; s += NTHREADS) {
-                    const int c = s / K, i = s - c * K;
-                    if (i < __ldcg(&CC[c])) fn(__ldcg(&C[(int64_t)c * KMAX + i]));
-                }
-            },
-            K, sm);
-        int c2 = 0;
-        for (int s = tid; s < slots; s += NTHREADS) {
-            const int c = s / K, i = s - c * K;
-            if (i < __ldcg(&CC[c]) && __ldcg(&C[(int64_t)c * KMAX + i]) >= kth) c2++;
-        }
-        int tot2;
-        int o2 = block_excl_scan(c2, &tot2, sm.scan);
-        for (int s = tid; s < slots; s += NTHREADS) {
-            const int c = s / K, i = s - c * K;
-            if (i < __ldcg(&CC[c])) {
-                const uint64_t v = __ldcg(&C[(int64_t)c * KMAX + i]);
-                if (v >= kth) sm.L[o2++] = v;
-            }
-        }
-        __syncthreads();
-        sort_list_desc(sm, tot2);
-        kw = K;
+        return total < K ? total : K;
     }
-    finish_row(a, row, p, kw, sm);
+    // heavy ties: exact radix selection over all list entries
+    const uint64_t kth = radix_kth(
+        [&](auto fn) {
+            for (int s = tid; s < slots; s += NTHREADS) {
+                const int c = s / K, i = s - c * K;
+                if (i < __ldcg(&CC[c * cstride])) fn(__ldcg(&C[c * lstride + i]));
+            }
+        },
+        K, sm);
+    int c2 = 0;
+    for (int s = tid; s < slots; s += NTHREADS) {
+        const int c = s / K, i = s - c * K;
+        if (i < __ldcg(&CC[c * cstride]) && __ldcg(&C[c * lstride + i]) >= kth) c2++;
+    }
+    int tot2;
+    int o2 = block_excl_scan(c2, &tot2, sm.scan);
+    for (int s = tid; s < slots; s += NTHREADS) {
+        const int c = s / K, i = s - c * K;
+        if (i < __ldcg(&CC[c * cstride])) {
+            const uint64_t v = __ldcg(&C[c * lstride + i]);
+            if (v >= kth) sm.L[o2++] = v;
+        }
+    }
+    __syncthreads();
+    sort_list_desc(sm, tot2);
+    return K;
+}
+
+// Stage 2 of a row (last-arriving CTA): merge the per-chunk lists, then
+// sample, or (vocabulary-sharded mode) publish the row's sorted top-K.
+__device__ void topk_merge(const SampleArgs &a, int row, const g4s_params &p, TopkSmem &sm)
+{
+    const int nch = a.nch, tid = threadIdx.x;
+    const int kw = merge_lists(p.top_k, sm, a.cand + (int64_t)row * nch * KMAX, KMAX,
+                               a.cand_cnt + (int64_t)row * nch, 1, nch);
+    if (a.list_out) {
+        __syncthreads();
+        for (int i = tid; i < kw; i += NTHREADS) a.list_out[(int64_t)row * KMAX + i] = sm.L[i];
+        if (tid == 0) a.list_cnt[row] = kw;
+    } else {
+        finish_row(a, row, p, kw, sm);
+    }
     if (tid == 0) a.counters_topk[row] = 0;  // ready for the next call
+}
+
+// Vocabulary-sharded mode, after the all-gather: one CTA per row merges the
+// shards' sorted lists (exact: the row's top K lie in the union of the
+// shards' top K) and runs the sampling tail.
+__global__ void __launch_bounds__(NTHREADS) shard_merge_kernel(SampleArgs a)
+{
+    __shared__ TopkSmem sm;
+    const int row = blockIdx.x;
+    const g4s_params p = a.params.get(row);
+    const int K = p.top_k;
+    if (!(K > 0 && K <= KMAX)) return;  // the host admits top-K rows only
+    const int kw = merge_lists(K, sm, a.glists + (int64_t)row * KMAX, (int64_t)a.rows * KMAX, a.gcnts + row,
+                               a.rows, a.gworld);
+    finish_row(a, row, p, kw, sm);
 }
 
 // Heavy ties in a chunk (more than CAP1 keys at or above the bound): exact
@@ -368,7 +399,8 @@ __device__ void topk_merge(const SampleArgs &a, int row, const g4s_params &p, To
 // Out of line and rare: it rereads the chunk from global memory in rolled
 // loops, so the register-resident fast path does not carry its code.
 template <int DT, int EPT>
-__device__ __noinline__ int chunk_select_radix(const void *rowp, int64_t c0, int n, int K, TopkSmem &sm)
+__device__ __noinline__ int chunk_select_radix(const void *rowp, int64_t c0, int n, int K, int id_offset,
+                                              TopkSmem &sm)
 {
     using T = DtypeTraits<DT>;
     constexpr int VW = T::VW;
@@ -377,7 +409,7 @@ __device__ __noinline__ int chunk_select_radix(const void *rowp, int64_t c0, int
         const int e = (i / VW) * (NTHREADS * VW) + tid * VW + (i % VW);
         if (e >= n) return false;
         const uint32_t k = cand_key(T::load1(rowp, c0 + e));
-        c = composite(k, (uint32_t)(c0 + e));
+        c = composite(k, (uint32_t)(id_offset + c0 + e));
         return k >= 1;
     };
     const uint64_t kth = radix_kth(
@@ -427,7 +459,7 @@ __device__ __forceinline__ int chunk_select(const SampleArgs &a, int row, int64_
         tmax = key[i] > tmax ? key[i] : tmax;
     }
     auto idof = [&](int i) -> uint32_t {
-        return (uint32_t)(c0 + (i / VW) * (NTHREADS * VW) + tid * VW + (i % VW));
+        return (uint32_t)(a.id_offset + c0 + (i / VW) * (NTHREADS * VW) + tid * VW + (i % VW));
     };
 
     // lower bound on the chunk's K-th largest key
@@ -456,7 +488,7 @@ __device__ __forceinline__ int chunk_select(const SampleArgs &a, int row, int64_
         sort_list_desc(sm, total);
         m = total < K ? total : K;
     } else {
-        m = chunk_select_radix<DT, EPT>(rowp, c0, n, K, sm);
+        m = chunk_select_radix<DT, EPT>(rowp, c0, n, K, a.id_offset, sm);
     }
     return m;
 }
@@ -607,6 +639,12 @@ static cudaError_t launch_cluster_t(const SampleArgs &a, cudaStream_t s)
     cfg.attrs = at;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, topk_cluster_kernel<DT, VEC>, a);
+}
+
+cudaError_t launch_shard_merge(const SampleArgs &a, cudaStream_t s)
+{
+    shard_merge_kernel<<<a.rows, NTHREADS, 0, s>>>(a);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_topk_cluster(const SampleArgs &a, bool vec, cudaStream_t s)

@@ -57,7 +57,23 @@ SIGNATURES = {
                                   POINTER(Params), c_int32, c_float, c_void_p, c_void_p]),
     "g4s_sample_topk_noalloc": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_int64, POINTER(Params),
                                           c_float, c_void_p, c_void_p, c_void_p]),
+    "g4s_shard_lists": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int64, c_int32, c_int32,
+                                  POINTER(Params), c_int32, c_void_p, c_void_p, c_void_p]),
+    "g4s_shard_merge": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, POINTER(Params),
+                                  c_int32, c_float, c_void_p, c_void_p, POINTER(Outputs), c_void_p]),
+    "g4s_shard_unique_id": (c_int32, [c_void_p]),
+    "g4s_shard_init": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_void_p]),
+    "g4s_shard_sample": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int64, POINTER(Params), c_int32,
+                                   c_float, c_void_p, c_void_p, POINTER(Outputs), c_void_p]),
 }
+SHARD_LIST = 256       # G4S_SHARD_LIST
+SHARD_UID_BYTES = 128  # G4S_SHARD_UID_BYTES
+
+
+def shard_slices(vocab: int, world: int):
+    """Rank r's [start, stop) of the vocabulary (contiguous, ceil(vocab/world) ids)."""
+    S = -(-vocab // world)
+    return [(r * S, min(vocab, (r + 1) * S)) for r in range(world)]
 
 _lib = None
 
@@ -76,6 +92,16 @@ def load(path: str = LIB_PATH):
         fn.argtypes = args
     _lib = lib
     return lib
+
+
+def shard_unique_id() -> bytes:
+    """g4s_shard_unique_id: the 128 bytes every rank passes to shard_init."""
+    lib = load()
+    buf = ctypes.create_string_buffer(SHARD_UID_BYTES)
+    rc = lib.g4s_shard_unique_id(buf)
+    if rc != OK:
+        raise G4SError(rc, lib.g4s_last_error(None).decode())
+    return buf.raw
 
 
 class G4SError(RuntimeError):
@@ -151,6 +177,47 @@ class Sampler:
         if check:
             self._check(rc)
         return rc
+
+    @staticmethod
+    def _params(params, rows):
+        if isinstance(params, Params):
+            return (Params * 1)(params), 0
+        return params_array(params), 1
+
+    def shard_lists(self, logits_ptr: int, dtype: int, rows: int, slice_vocab: int, row_stride: int,
+                    id_offset: int, vocab_total: int, params, lists_ptr: int, counts_ptr: int,
+                    stream: int | None = None, check: bool = True) -> int:
+        parr, pstride = self._params(params, rows)
+        rc = self.lib.g4s_shard_lists(self.h, c_void_p(logits_ptr), dtype, rows, slice_vocab, row_stride, id_offset,
+                                      vocab_total, parr, pstride, c_void_p(lists_ptr), c_void_p(counts_ptr),
+                                      c_void_p(stream) if stream else None)
+        if check:
+            self._check(rc)
+        return rc
+
+    def shard_merge(self, lists_ptr: int, counts_ptr: int, world: int, rows: int, vocab_total: int, params,
+                    softcap: float, u_ptr: int, out_ptr: int, outputs: Outputs | None = None,
+                    stream: int | None = None, check: bool = True) -> int:
+        parr, pstride = self._params(params, rows)
+        rc = self.lib.g4s_shard_merge(self.h, c_void_p(lists_ptr), c_void_p(counts_ptr), world, rows, vocab_total,
+                                      parr, pstride, softcap, c_void_p(u_ptr), c_void_p(out_ptr),
+                                      ctypes.byref(outputs) if outputs is not None else None,
+                                      c_void_p(stream) if stream else None)
+        if check:
+            self._check(rc)
+        return rc
+
+    def shard_init(self, world: int, rank: int, vocab_total: int, uid: bytes) -> None:
+        buf = ctypes.create_string_buffer(bytes(uid), SHARD_UID_BYTES)
+        self._check(self.lib.g4s_shard_init(self.h, world, rank, vocab_total, buf))
+
+    def shard_sample(self, logits_ptr: int, dtype: int, rows: int, row_stride: int, params, softcap: float,
+                     u_ptr: int, out_ptr: int, outputs: Outputs | None = None, stream: int | None = None) -> None:
+        parr, pstride = self._params(params, rows)
+        self._check(self.lib.g4s_shard_sample(self.h, c_void_p(logits_ptr), dtype, rows, row_stride, parr, pstride,
+                                              softcap, c_void_p(u_ptr), c_void_p(out_ptr),
+                                              ctypes.byref(outputs) if outputs is not None else None,
+                                              c_void_p(stream) if stream else None))
 
     def sample_host(self, logits, dtype: int, params, softcap: float, u, tokens_out=None):
         """g4s_sample_host on numpy arrays (logits [rows, row_stride] f32 or uint16 bf16 bits)."""

@@ -190,6 +190,52 @@ int32_t g4s_sample_topk_noalloc(const void *logits, int32_t dtype, int32_t rows,
                                 int64_t row_stride, const g4s_params *params, float softcap,
                                 const double *u, int32_t *out_tokens, void *stream);
 
+/*
+ * Vocabulary-sharded mode (no counterpart in the reference, which samples one
+ * row on one host thread).  Each of W ranks holds a contiguous slice of every
+ * row's logits; rows must have 0 < top_k <= 256 below the slice length (full-
+ * vocabulary rows are sampled with a row split: plain g4s_sample per rank on
+ * its own rows).  The row's top K lie in the union of the slices' top K, so
+ * the merge is exact and every rank draws the same token as g4s_sample on the
+ * whole row (ties at the K-th place to the lower global id).
+ *
+ * Two compute phases, usable with any collective:
+ *   g4s_shard_lists  one slice -> per row the slice's top-K composites sorted
+ *                    descending: out_lists [rows][G4S_SHARD_LIST] uint64
+ *                    (value key << 32 | ~global_id), out_counts [rows] int32
+ *   g4s_shard_merge  the W ranks' lists gathered as lists [W][rows][G4S_SHARD_LIST]
+ *                    and counts [W][rows] -> tokens (and the optional outputs
+ *                    of g4s_sample_ex for top-K rows)
+ * and the NCCL form: g4s_shard_unique_id on one rank, the 128 bytes passed to
+ * every rank, g4s_shard_init on each, then g4s_shard_sample per step (lists,
+ * two ncclAllGather over NVLink, merge; stream-ordered, asynchronous).  Every
+ * rank passes the same rows, params, softcap and u.  NCCL is loaded at the
+ * first g4s_shard_unique_id / g4s_shard_init (libnccl.so.2).
+ */
+#define G4S_SHARD_LIST 256
+#define G4S_SHARD_UID_BYTES 128
+
+int32_t g4s_shard_lists(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t rows, int32_t slice_vocab,
+                        int64_t row_stride, int32_t id_offset, int32_t vocab_total, const g4s_params *params,
+                        int32_t params_stride, uint64_t *out_lists, int32_t *out_counts, void *stream);
+
+int32_t g4s_shard_merge(g4s_ctx *ctx, const uint64_t *lists, const int32_t *counts, int32_t world, int32_t rows,
+                        int32_t vocab_total, const g4s_params *params, int32_t params_stride, float softcap,
+                        const double *u, int32_t *out_tokens, const g4s_outputs *extra, void *stream);
+
+/* 128 bytes (an ncclUniqueId) to hand to every rank's g4s_shard_init. */
+int32_t g4s_shard_unique_id(uint8_t *uid);
+
+/* Joins ctx to a W-rank sampler (ncclCommInitRank; collective over the ranks).
+   Rank r owns ids [r * S, min(vocab_total, (r + 1) * S)), S = ceil(vocab_total / W). */
+int32_t g4s_shard_init(g4s_ctx *ctx, int32_t world, int32_t rank, int32_t vocab_total, const uint8_t *uid);
+
+/* One sharded step: logits_slice is this rank's slice (rows x row_stride
+   elements, device memory); u and out_tokens are device pointers. */
+int32_t g4s_shard_sample(g4s_ctx *ctx, const void *logits_slice, int32_t dtype, int32_t rows, int64_t row_stride,
+                         const g4s_params *params, int32_t params_stride, float softcap, const double *u,
+                         int32_t *out_tokens, const g4s_outputs *extra, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
