@@ -263,6 +263,55 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_c5_sharded(s_unused, rank, world, local, dev, peak, steps=200):
+    """Config C5 in the vocabulary-sharded mode: 1024 fp32 rows, each rank
+    holding a contiguous V/world slice of every row (per-row T, top-K, top-P);
+    per step: the slice's top-K lists, two NCCL all-gathers, the merge and the
+    draw.  Device time per step, max over ranks."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import g4sampler as g4
+    import synth
+
+    rows = 1024
+    lo, hi = g4.shard_slices(VOCAB, world)[rank]
+    n = hi - lo
+    sets = [torch.from_numpy(synth.c5_logits(rows, vocab=n, step=100 * rank + k)).to(dev) for k in range(2)]
+    prm = synth.c5_params(rows)
+    u = torch.from_numpy(synth.uniforms(rows, synth.SEEDS["c5"])).to(dev)
+    out = torch.empty(rows, dtype=torch.int32, device=dev)
+    sh = g4.Sampler(local, rows, n)
+    uid = torch.zeros(g4.SHARD_UID_BYTES, dtype=torch.uint8, device=dev)
+    if rank == 0:
+        uid.copy_(torch.frombuffer(bytearray(g4.shard_unique_id()), dtype=torch.uint8))
+    dist.broadcast(uid, 0)
+    sh.shard_init(world, rank, VOCAB, bytes(uid.cpu().numpy().tobytes()))
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    for i in range(5):
+        sh.shard_sample(sets[i % 2].data_ptr(), g4.F32, rows, n, prm, SOFTCAP, u.data_ptr(), out.data_ptr(),
+                        stream=stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(steps):
+        sh.shard_sample(sets[i % 2].data_ptr(), g4.F32, rows, n, prm, SOFTCAP, u.data_ptr(), out.data_ptr(),
+                        stream=stream)
+    t1.record()
+    torch.cuda.synchronize()
+    ms = allreduce_max(t0.elapsed_time(t1), world)
+    sh.close()
+    us = ms * 1e3 / steps
+    return {"rows_per_s": rows / (us * 1e-6), "us_per_step": us, "world": world,
+            "per_gpu_hbm_frac_of_peak": rows * n * 4 / (us * 1e-6) / 1e9 / peak,
+            "allgather_bytes_per_rank": rows * (g4.SHARD_LIST * 8 + 4),
+            "config": f"C5 sharded: B=1024 x V=262144 fp32, a {n}-id slice per rank; per-row T~U[0.3,1.5], "
+                      "K in {1,20,64,200}, P~U[0.5,1]; lists -> ncclAllGather x2 -> merge; "
+                      f"{steps} steps, host loop, CUDA events, max over ranks"}
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -448,6 +497,7 @@ def main():
                          "C oracle port of TModel.DoSample, fp32 transcription"}
 
     s.close()
+    c5 = run_c5_sharded(None, rank, world, local, dev, peak) if world > 1 else None
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": K, "warmup": W,
@@ -472,6 +522,7 @@ def main():
                          "step_hbm_frac": ROWS * BYTES_PER_ROW / (total_ms_max / K * 1e-3) / 1e9 / peak},
             "latency_b1": lat,
             "c2": c2,
+            "c5_sharded": c5,
             "e2e": e2e,
             "cpu_baseline": cpu,
             "gpu_launches": 2 * K,

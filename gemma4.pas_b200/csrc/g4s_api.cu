@@ -19,6 +19,7 @@ namespace g4s {
 constexpr int KMAX_ = 256;
 constexpr int NCH_MAX_ = 1024;
 constexpr int LK_SLOTS = 16;
+constexpr int PSLOTS = 4;  // per-row params staging slots
 }  // namespace g4s
 
 using namespace g4s;
@@ -44,9 +45,12 @@ struct g4s_ctx {
     int32_t *lk_idx = nullptr;
     float *lk_val = nullptr;
     g4s_params *params_dev = nullptr;
+    // per-row params staging: a ring of PSLOTS pinned slots and device slots,
+    // so the host can enqueue a few calls ahead of the GPU
     g4s_params *params_pinned = nullptr;
-    cudaEvent_t params_ev = nullptr;
-    bool params_ev_pending = false;
+    cudaEvent_t params_ev[4] = {nullptr, nullptr, nullptr, nullptr};
+    bool params_ev_pending[4] = {false, false, false, false};
+    int params_slot = 0;
     // vocabulary-sharded mode (g4s_shard_init)
     void *nccl_comm = nullptr;
     int shard_world = 0, shard_rank = 0, shard_vocab = 0, shard_slice = 0;
@@ -90,6 +94,13 @@ struct DeviceGuard {
 };
 
 static int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+static bool create_param_events(g4s_ctx *ctx)
+{
+    for (int k = 0; k < PSLOTS; k++)
+        if (cudaEventCreateWithFlags(&ctx->params_ev[k], cudaEventDisableTiming) != cudaSuccess) return false;
+    return true;
+}
 
 // Chunk size for a call: 2048 ids (8 per thread) when big chunks would leave
 // the GPU under two CTAs per SM, else 8192 ids (32 per thread).
@@ -162,24 +173,36 @@ static int32_t stage_params(g4s_ctx *ctx, const char *who, const g4s_params *par
                             int rows, cudaStream_t s, RowParams &out)
 {
     if (params_stride) {
-        // the pinned staging may still feed the previous call's copy
-        if (ctx->params_ev_pending && cudaEventSynchronize(ctx->params_ev) != cudaSuccess)
-            return fail(ctx, G4S_ERR_CUDA, "%s: waiting on the previous params copy failed", who);
-        memcpy(ctx->params_pinned, params, (size_t)rows * sizeof(g4s_params));
-        float *inv_t = (float *)(ctx->params_pinned + rows);
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+            cudaGetLastError();
+            return fail(ctx, G4S_ERR_STATE,
+                        "%s: per-row params are staged through host memory, which a captured graph would read at "
+                        "replay; capture calls with broadcast params (params_stride 0)", who);
+        }
+        // slot k's pinned copy may still feed the copy of the call PSLOTS calls ago
+        const int k = ctx->params_slot;
+        ctx->params_slot = (k + 1) % PSLOTS;
+        if (ctx->params_ev_pending[k] && cudaEventSynchronize(ctx->params_ev[k]) != cudaSuccess)
+            return fail(ctx, G4S_ERR_CUDA, "%s: waiting on an earlier params copy failed", who);
+        const size_t slot_bytes = (size_t)ctx->max_rows * (sizeof(g4s_params) + sizeof(float));
+        g4s_params *hp = (g4s_params *)((char *)ctx->params_pinned + k * slot_bytes);
+        g4s_params *dp = (g4s_params *)((char *)ctx->params_dev + k * slot_bytes);
+        memcpy(hp, params, (size_t)rows * sizeof(g4s_params));
+        float *inv_t = (float *)(hp + rows);
         for (int r = 0; r < rows; r++) {
             const float T = params[r].temperature;
             inv_t[r] = (T > 0.0f && T != 1.0f) ? 1.0f / T : 1.0f;
         }
-        if (cudaMemcpyAsync(ctx->params_dev, ctx->params_pinned, (size_t)rows * (sizeof(g4s_params) + sizeof(float)),
-                            cudaMemcpyHostToDevice, s) != cudaSuccess ||
-            cudaEventRecord(ctx->params_ev, s) != cudaSuccess) {
+        if (cudaMemcpyAsync(dp, hp, (size_t)rows * (sizeof(g4s_params) + sizeof(float)), cudaMemcpyHostToDevice, s) !=
+                cudaSuccess ||
+            cudaEventRecord(ctx->params_ev[k], s) != cudaSuccess) {
             cudaError_t e = cudaGetLastError();
             return fail(ctx, G4S_ERR_CUDA, "%s: params upload failed: %s", who, cudaGetErrorString(e));
         }
-        ctx->params_ev_pending = true;
-        out.dev = ctx->params_dev;
-        out.inv_t_dev = (const float *)(ctx->params_dev + rows);
+        ctx->params_ev_pending[k] = true;
+        out.dev = dp;
+        out.inv_t_dev = (const float *)(dp + rows);
     } else {
         out.dev = nullptr;
         out.p0 = params[0];
@@ -308,7 +331,7 @@ int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t
     const size_t o_rs = off; off = align(off + (size_t)max_rows * sizeof(RowStat));
     const size_t o_li = off; off = align(off + (size_t)LK_SLOTS * max_vocab * sizeof(int32_t));
     const size_t o_lv = off; off = align(off + (size_t)LK_SLOTS * max_vocab * sizeof(float));
-    const size_t o_pd = off; off = align(off + (size_t)max_rows * (sizeof(g4s_params) + sizeof(float)));
+    const size_t o_pd = off; off = align(off + (size_t)PSLOTS * max_rows * (sizeof(g4s_params) + sizeof(float)));
     ctx->ws_bytes = off;
     if (cudaMalloc(&ctx->ws, off) != cudaSuccess) {
         cudaGetLastError();
@@ -326,9 +349,9 @@ int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t
     ctx->params_dev = (g4s_params *)(base + o_pd);
     if (cudaMemset(ctx->ws, 0, off) != cudaSuccess ||
         cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaHostAlloc((void **)&ctx->params_pinned, (size_t)max_rows * (sizeof(g4s_params) + sizeof(float)),
+        cudaHostAlloc((void **)&ctx->params_pinned, (size_t)PSLOTS * max_rows * (sizeof(g4s_params) + sizeof(float)),
                       cudaHostAllocDefault) != cudaSuccess ||
-        cudaEventCreateWithFlags(&ctx->params_ev, cudaEventDisableTiming) != cudaSuccess) {
+        !create_param_events(ctx)) {
         cudaGetLastError();
         g4s_destroy(ctx);
         return fail(nullptr, G4S_ERR_CUDA, "g4s_create: stream/event/pinned setup failed");
@@ -350,7 +373,8 @@ int32_t g4s_destroy(g4s_ctx *ctx)
     if (!ctx) return G4S_OK;
     DeviceGuard guard(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
-    if (ctx->params_ev) cudaEventDestroy(ctx->params_ev);
+    for (int k = 0; k < PSLOTS; k++)
+        if (ctx->params_ev[k]) cudaEventDestroy(ctx->params_ev[k]);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     if (ctx->params_pinned) cudaFreeHost(ctx->params_pinned);
     if (ctx->ws) cudaFree(ctx->ws);
