@@ -225,7 +225,7 @@ def cpu_reference(rows_bf16, u, nthreads, min_cpu_s=10.0):
             return done / el, done, el
 
 
-def run_reference(args):
+def run_reference(args, emit):
     """--impl reference: the reference's algorithm for the path on the host cores."""
     import numpy as np
 
@@ -260,7 +260,7 @@ def run_reference(args):
                                    "TModel.DoSample (the Delphi reference does not build here)"},
         "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def run_c5_sharded(s_unused, rank, world, local, dev, peak, steps=200):
@@ -314,8 +314,17 @@ def run_c5_sharded(s_unused, rank, world, local, dev, peak, steps=200):
 
 def main():
     args = parse()
+    # the one JSON line goes to the original stdout; everything else printed in
+    # this process (libraries too, e.g. NCCL's version banner) goes to stderr
+    json_fd = os.dup(1)
+    sys.stdout.flush()
+    os.dup2(2, 1)
+
+    def emit(line):
+        os.write(json_fd, (json.dumps(line) + "\n").encode())
+
     if args.impl == "reference":
-        run_reference(args)
+        run_reference(args, emit)
         return
     import numpy as np
     import torch
@@ -529,7 +538,7 @@ def main():
             "clocks": clk,
             "tokens_in_range": tokens_ok,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         import torch.distributed as dist
 
