@@ -56,6 +56,10 @@ struct g4s_ctx {
     int shard_world = 0, shard_rank = 0, shard_vocab = 0, shard_slice = 0;
     uint64_t *sh_send = nullptr;  // [max_rows][KMAX] this rank's lists, then [max_rows] counts
     uint64_t *sh_recv = nullptr;  // [world][max_rows][KMAX], then [world][max_rows] counts
+    // LM head workspace (first g4s_lmhead_sample call): fp32 logits and fp16 hidden
+    float *lm_logits = nullptr;
+    void *lm_xh = nullptr;
+    size_t lm_logits_n = 0, lm_xh_n = 0;
     // g4s_sample_host staging
     void *h_logits = nullptr;
     double *h_u = nullptr;
@@ -382,6 +386,8 @@ int32_t g4s_destroy(g4s_ctx *ctx)
     if (ctx->h_u) cudaFree(ctx->h_u);
     if (ctx->h_tok) cudaFree(ctx->h_tok);
     shard_release(ctx);
+    if (ctx->lm_logits) cudaFree(ctx->lm_logits);
+    if (ctx->lm_xh) cudaFree(ctx->lm_xh);
     delete ctx;
     return G4S_OK;
 }
@@ -525,6 +531,70 @@ int32_t g4s_sample_host(g4s_ctx *ctx, const void *host_logits, int32_t dtype, in
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "g4s_sample_host: %s", cudaGetErrorString(e));
     return G4S_OK;
+}
+
+// ---------------------------------------------------------------------------
+// LM head + sampling (config C4)
+// ---------------------------------------------------------------------------
+int32_t g4s_q4_repack(const uint8_t *blocks, int32_t vocab, int32_t hidden, uint8_t *nibbles, uint16_t *scales,
+                      void *stream)
+{
+    if (!blocks || !nibbles || !scales) return fail(nullptr, G4S_ERR_ARG, "g4s_q4_repack: NULL buffer");
+    if (vocab < 1 || hidden < 32 || hidden % 32)
+        return fail(nullptr, G4S_ERR_ARG, "g4s_q4_repack: vocab %d / hidden %d (a multiple of 32)", vocab, hidden);
+    const cudaError_t e = launch_q4_repack(blocks, vocab, hidden, nibbles, scales, (cudaStream_t)stream);
+    if (e != cudaSuccess) return fail(nullptr, G4S_ERR_CUDA, "g4s_q4_repack: %s", cudaGetErrorString(e));
+    return G4S_OK;
+}
+
+int32_t g4s_lmhead_sample(g4s_ctx *ctx, const float *hidden, int32_t rows, int32_t hidden_size,
+                          const uint8_t *nibbles, const uint16_t *scales, int32_t vocab, const g4s_params *params,
+                          int32_t params_stride, float softcap, const double *u, int32_t *out_tokens,
+                          const g4s_outputs *extra, float *out_logits, void *stream)
+{
+    static const char *who = "g4s_lmhead_sample";
+    if (!ctx) return fail(nullptr, G4S_ERR_ARG, "%s: ctx is NULL", who);
+    if (!hidden || !nibbles || !scales || !params || !out_tokens)
+        return fail(ctx, G4S_ERR_ARG, "%s: hidden, nibbles, scales, params and out_tokens must be non-NULL", who);
+    if (rows < 1 || rows > LMHEAD_MAX_ROWS || rows > ctx->max_rows)
+        return fail(ctx, G4S_ERR_CAPACITY, "%s: rows %d outside [1, %d]", who, rows,
+                    std::min(LMHEAD_MAX_ROWS, ctx->max_rows));
+    if (hidden_size < 128 || hidden_size % 128)
+        return fail(ctx, G4S_ERR_ARG, "%s: hidden %d must be a positive multiple of 128", who, hidden_size);
+    if (vocab < 8 || vocab % 8 || vocab > ctx->max_vocab)
+        return fail(ctx, G4S_ERR_ARG, "%s: vocab %d must be a multiple of 8 within max_vocab %d", who, vocab,
+                    ctx->max_vocab);
+    DeviceGuard guard(ctx->device);
+    if (!guard.ok) return fail(ctx, G4S_ERR_CUDA, "%s: cannot select device %d", who, ctx->device);
+    cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
+    float *logits = out_logits;
+    const size_t need_l = (size_t)rows * vocab, need_x = (size_t)LMHEAD_MAX_ROWS * hidden_size;
+    if (!logits && ctx->lm_logits_n < need_l) {
+        if (ctx->lm_logits) cudaFree(ctx->lm_logits);
+        ctx->lm_logits = nullptr;
+        ctx->lm_logits_n = 0;
+        if (cudaMalloc(&ctx->lm_logits, need_l * sizeof(float)) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(ctx, G4S_ERR_NOMEM, "%s: cannot allocate %zu bytes of logits", who, need_l * sizeof(float));
+        }
+        ctx->lm_logits_n = need_l;
+    }
+    if (ctx->lm_xh_n < need_x) {
+        if (ctx->lm_xh) cudaFree(ctx->lm_xh);
+        ctx->lm_xh = nullptr;
+        ctx->lm_xh_n = 0;
+        if (cudaMalloc(&ctx->lm_xh, need_x * sizeof(uint16_t)) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(ctx, G4S_ERR_NOMEM, "%s: cannot allocate the fp16 hidden buffer", who);
+        }
+        ctx->lm_xh_n = need_x;
+    }
+    if (!logits) logits = ctx->lm_logits;
+    const cudaError_t e = launch_lmhead(hidden, rows, hidden_size, nibbles, scales, vocab, (__half *)ctx->lm_xh,
+                                        logits, s);
+    if (e != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "%s: launch failed: %s", who, cudaGetErrorString(e));
+    return g4s_sample_ex(ctx, logits, G4S_F32, rows, vocab, vocab, params, params_stride, softcap, u, out_tokens,
+                         extra, s);
 }
 
 // ---------------------------------------------------------------------------

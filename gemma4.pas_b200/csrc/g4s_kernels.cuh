@@ -80,6 +80,17 @@ cudaError_t launch_full(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
 cudaError_t launch_full_probs(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
 cudaError_t launch_largek(const SampleArgs &a, cudaStream_t s);
 cudaError_t launch_topk_cluster(const SampleArgs &a, bool vec, cudaStream_t s);
+// LM head (config C4): Q4_0 weights repacked to nibble / scale planes, fp16
+// tensor-core GEMM of up to 64 rows of hidden states into fp32 logits.
+}  // namespace g4s
+#include <cuda_fp16.h>
+namespace g4s {
+cudaError_t launch_q4_repack(const uint8_t *blocks, int vocab, int hidden, uint8_t *nib, uint16_t *scales,
+                             cudaStream_t s);
+cudaError_t launch_lmhead(const float *hidden, int rows, int H, const uint8_t *nib, const uint16_t *scales, int vocab,
+                          __half *xh, float *logits, cudaStream_t s);
+constexpr int LMHEAD_MAX_ROWS = 64;
+
 // Vocabulary-sharded mode: the gathered per-shard lists merged into each row's
 // top-K, then the sampling tail (one CTA per row).
 cudaError_t launch_shard_merge(const SampleArgs &a, cudaStream_t s);

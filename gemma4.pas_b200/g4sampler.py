@@ -57,6 +57,10 @@ SIGNATURES = {
                                   POINTER(Params), c_int32, c_float, c_void_p, c_void_p]),
     "g4s_sample_topk_noalloc": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_int64, POINTER(Params),
                                           c_float, c_void_p, c_void_p, c_void_p]),
+    "g4s_q4_repack": (c_int32, [c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
+    "g4s_lmhead_sample": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_int32,
+                                    POINTER(Params), c_int32, c_float, c_void_p, c_void_p, POINTER(Outputs),
+                                    c_void_p, c_void_p]),
     "g4s_shard_lists": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int64, c_int32, c_int32,
                                   POINTER(Params), c_int32, c_void_p, c_void_p, c_void_p]),
     "g4s_shard_merge": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, POINTER(Params),
@@ -92,6 +96,15 @@ def load(path: str = LIB_PATH):
         fn.argtypes = args
     _lib = lib
     return lib
+
+
+def q4_repack(blocks_ptr: int, vocab: int, hidden: int, nib_ptr: int, scales_ptr: int, stream: int | None = None):
+    """g4s_q4_repack: reference Q4_0 blocks -> nibble / scale planes (device pointers)."""
+    lib = load()
+    rc = lib.g4s_q4_repack(c_void_p(blocks_ptr), vocab, hidden, c_void_p(nib_ptr), c_void_p(scales_ptr),
+                           c_void_p(stream) if stream else None)
+    if rc != OK:
+        raise G4SError(rc, lib.g4s_last_error(None).decode())
 
 
 def shard_unique_id() -> bytes:
@@ -218,6 +231,20 @@ class Sampler:
                                               softcap, c_void_p(u_ptr), c_void_p(out_ptr),
                                               ctypes.byref(outputs) if outputs is not None else None,
                                               c_void_p(stream) if stream else None))
+
+    def lmhead_sample(self, hidden_ptr: int, rows: int, hidden: int, nib_ptr: int, scales_ptr: int, vocab: int,
+                      params, softcap: float, u_ptr: int, out_ptr: int, outputs: Outputs | None = None,
+                      logits_ptr: int = 0, stream: int | None = None, check: bool = True) -> int:
+        """g4s_lmhead_sample: logits = hidden x W^T (Q4_0, repacked) then sampling."""
+        parr, pstride = self._params(params, rows)
+        rc = self.lib.g4s_lmhead_sample(self.h, c_void_p(hidden_ptr), rows, hidden, c_void_p(nib_ptr),
+                                        c_void_p(scales_ptr), vocab, parr, pstride, softcap, c_void_p(u_ptr),
+                                        c_void_p(out_ptr), ctypes.byref(outputs) if outputs is not None else None,
+                                        c_void_p(logits_ptr) if logits_ptr else None,
+                                        c_void_p(stream) if stream else None)
+        if check:
+            self._check(rc)
+        return rc
 
     def sample_host(self, logits, dtype: int, params, softcap: float, u, tokens_out=None):
         """g4s_sample_host on numpy arrays (logits [rows, row_stride] f32 or uint16 bf16 bits)."""

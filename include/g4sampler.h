@@ -191,6 +191,30 @@ int32_t g4s_sample_topk_noalloc(const void *logits, int32_t dtype, int32_t rows,
                                 const double *u, int32_t *out_tokens, void *stream);
 
 /*
+ * LM head + sampling (config C4; the reference's last matvec, CpuMatVecQ4
+ * src/Gemma4.Tensors.pas:546-590, then DoSample).  Weights are the reference's
+ * Q4_0 blocks (TQ4Block, src/Gemma4.Types.pas:139-142: fp16 scale + 16 bytes,
+ * byte j = element 2j in the low nibble, 2j+1 in the high nibble, value =
+ * nibble - 8), repacked once on the device by g4s_q4_repack into
+ *   nibbles [vocab][hidden/2]   the 16 nibble bytes of each block
+ *   scales  [vocab][hidden/32]  the fp16 scale bits
+ * g4s_lmhead_sample computes logits[r][v] = sum_k hidden[r][k] * w[v][k] for
+ * rows <= 64 (hidden fp32 on the device, rounded to fp16; w = (nibble - 8) *
+ * scale rounded once to fp16; fp16 tensor-core products, fp32 accumulation),
+ * then samples them exactly as g4s_sample_ex.  hidden must be a multiple of
+ * 128, vocab of 8.  out_logits (device, rows x vocab fp32) receives the logits
+ * when non-NULL; otherwise they stay in a context buffer allocated by the
+ * first call.
+ */
+int32_t g4s_q4_repack(const uint8_t *blocks, int32_t vocab, int32_t hidden, uint8_t *nibbles, uint16_t *scales,
+                      void *stream);
+
+int32_t g4s_lmhead_sample(g4s_ctx *ctx, const float *hidden, int32_t rows, int32_t hidden_size,
+                          const uint8_t *nibbles, const uint16_t *scales, int32_t vocab, const g4s_params *params,
+                          int32_t params_stride, float softcap, const double *u, int32_t *out_tokens,
+                          const g4s_outputs *extra, float *out_logits, void *stream);
+
+/*
  * Vocabulary-sharded mode (no counterpart in the reference, which samples one
  * row on one host thread).  Each of W ranks holds a contiguous slice of every
  * row's logits; rows must have 0 < top_k <= 256 below the slice length (full-

@@ -1,0 +1,86 @@
+"""LM head + sampling (config C4) through the C ABI: Q4_0 weights in the
+reference block format (TQ4Block, src/Gemma4.Types.pas:139-142), repacked on
+the device, logits by the fp16 tensor-core GEMM, then the sampler.
+
+Logits are checked against the fp64 matvec of the same quantized weights
+(restating CpuMatVecQ4, src/Gemma4.Tensors.pas:546-590, in exact arithmetic)
+with the bound of the kernel's arithmetic: hidden and each weight are rounded
+to fp16 (relative 2^-11 each) and products are summed in fp32, so
+|err| <= 2^-9 * sum_k |w_k x_k| + 1e-6.  Tokens must equal the oracle's top-K
+DoSample applied to the kernel's own logits (that path is bit-exact)."""
+import numpy as np
+import pytest
+
+import synth
+from gpu_util import F32, check_topk_rows
+
+pytestmark = pytest.mark.gpu
+CAP = 30.0
+
+
+def _dequant(blocks, vocab, hidden):
+    b = blocks.reshape(vocab, hidden // 32, 18)
+    sc = (b[:, :, 0].astype(np.uint16) | (b[:, :, 1].astype(np.uint16) << 8)).view(np.float16).astype(np.float64)
+    nb = b[:, :, 2:]
+    q = np.empty((vocab, hidden // 32, 32), dtype=np.float64)
+    q[:, :, 0::2] = (nb & 0xF).astype(np.float64) - 8
+    q[:, :, 1::2] = (nb >> 4).astype(np.float64) - 8
+    return (q * sc[:, :, None]).reshape(vocab, hidden)
+
+
+def _run(g4, torch, s, h, blocks, vocab, hidden, prm, u):
+    rows = h.shape[0]
+    bd = torch.from_numpy(blocks).cuda()
+    nib = torch.empty(vocab * hidden // 2, dtype=torch.uint8, device="cuda")
+    sc = torch.empty(vocab * hidden // 32, dtype=torch.int16, device="cuda")
+    g4.q4_repack(bd.data_ptr(), vocab, hidden, nib.data_ptr(), sc.data_ptr())
+    hd = torch.from_numpy(h).cuda()
+    ud = torch.from_numpy(u).cuda()
+    out = torch.full((rows,), -5, dtype=torch.int32, device="cuda")
+    logits = torch.empty((rows, vocab), dtype=torch.float32, device="cuda")
+    s.lmhead_sample(hd.data_ptr(), rows, hidden, nib.data_ptr(), sc.data_ptr(), vocab, prm, CAP, ud.data_ptr(),
+                    out.data_ptr(), logits_ptr=logits.data_ptr())
+    torch.cuda.synchronize()
+    return out.cpu().numpy(), logits.cpu().numpy()
+
+
+@pytest.mark.parametrize("rows,vocab", [(64, 8192), (5, 4104), (1, 2048)])
+def test_lmhead_logits_and_tokens(g4, torch_cuda, oracle, rows, vocab):
+    hidden = 2560
+    h, blocks = synth.c4_inputs(rows, hidden, vocab)
+    prm = [(1.0, 64, 0.95), (0.7, 20, 0.9), (0.0, 64, 0.9)] * (rows // 3 + 1)
+    prm = prm[:rows]
+    u = synth.uniforms(rows, 0xC4)
+    s = g4.Sampler(0, 64, 262144)
+    try:
+        tok, lg = _run(g4, torch_cuda, s, h, blocks, vocab, hidden, prm, u)
+    finally:
+        s.close()
+    W = _dequant(blocks, vocab, hidden)
+    want = h.astype(np.float64) @ W.T
+    bound = 2.0 ** -9 * (np.abs(h.astype(np.float64)) @ np.abs(W).T) + 1e-6
+    err = np.abs(lg - want)
+    assert (err <= bound).all(), float((err / bound).max())
+    # the oracle's serial fp32 CpuMatVecQ4 on a few rows, for the record
+    ref32 = oracle.matvec_q4(blocks, h[0], vocab, hidden)
+    assert np.abs(ref32 - want[0]).max() < 1e-3
+    check_topk_rows(oracle, lg, F32, prm, CAP, u, {"tokens": tok})
+
+
+def test_lmhead_full_size_sample(g4, torch_cuda, oracle):
+    # config C4 shapes: 64 x 2560 hidden, 262144 x 2560 Q4_0 weights (377 MB)
+    rows, hidden, vocab = 64, 2560, 262144
+    h, blocks = synth.c4_inputs(rows, hidden, vocab)
+    u = synth.uniforms(rows, 0xC4, 1)
+    prm = g4.make_params(1.0, 64, 0.95)
+    s = g4.Sampler(0, 64, vocab)
+    try:
+        tok, lg = _run(g4, torch_cuda, s, h, blocks, vocab, hidden, prm, u)
+    finally:
+        s.close()
+    pick = np.random.default_rng(4).choice(vocab, 3000, replace=False)
+    W = _dequant(blocks.reshape(vocab, -1)[pick].reshape(-1), len(pick), hidden)
+    want = h.astype(np.float64) @ W.T
+    bound = 2.0 ** -9 * (np.abs(h.astype(np.float64)) @ np.abs(W).T) + 1e-6
+    assert (np.abs(lg[:, pick] - want) <= bound).all()
+    check_topk_rows(oracle, lg[::8], F32, prm, CAP, u[::8], {"tokens": tok[::8]})
