@@ -47,6 +47,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--only", choices=["c4"], default=None,
+                    help="run config C4 alone and print its record (for profiling)")
     return ap.parse_args()
 
 
@@ -263,6 +265,62 @@ def run_reference(args, emit):
     emit(line)
 
 
+def run_c4(dev, peak, steps=20):
+    """Config C4: LM head (64 x 2560 hidden, 262144 x 2560 Q4_0 weights, 377 MB)
+    + top-K sampling, one g4s_lmhead_sample call per step; device time per step
+    from a CUDA graph of `steps` calls (weights 377 MB > L2: streamed each step)."""
+    import torch
+
+    import g4sampler as g4
+    import synth
+
+    rows, H = 64, 2560
+    h, blocks = synth.c4_inputs(rows, H, VOCAB)
+    bd = torch.from_numpy(blocks).to(dev)
+    nib = torch.empty(VOCAB * H // 2, dtype=torch.uint8, device=dev)
+    sc = torch.empty(VOCAB * H // 32, dtype=torch.int16, device=dev)
+    g4.q4_repack(bd.data_ptr(), VOCAB, H, nib.data_ptr(), sc.data_ptr())
+    torch.cuda.synchronize()
+    del bd
+    hd = torch.from_numpy(h).to(dev)
+    u = torch.from_numpy(synth.uniforms(rows, synth.SEEDS["c4"])).to(dev)
+    out = torch.empty(rows, dtype=torch.int32, device=dev)
+    s = g4.Sampler(dev.index or 0, rows, VOCAB)
+    p = g4.make_params(1.0, 64, 0.95)
+    cap = torch.cuda.Stream(device=dev)
+
+    def call(st=None):
+        s.lmhead_sample(hd.data_ptr(), rows, H, nib.data_ptr(), sc.data_ptr(), VOCAB, p, SOFTCAP, u.data_ptr(),
+                        out.data_ptr(), stream=st)
+
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=cap):
+        for _ in range(steps):
+            call(cap.cuda_stream)
+    g.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(5):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b) * 1e3 / steps)
+    del g
+    s.close()
+    us = statistics.median(ts)
+    wbytes = VOCAB * (H // 32) * 18
+    return {"us_per_step": us, "rows_per_s": rows / (us * 1e-6), "weight_gbs": wbytes / (us * 1e-6) / 1e9,
+            "hbm_frac_of_peak": wbytes / (us * 1e-6) / 1e9 / peak,
+            "tflops": 2.0 * rows * VOCAB * H / (us * 1e-6) / 1e12,
+            "config": "C4: hidden 64 x 2560 fp32 -> LM head 262144 x 2560 Q4_0 (fp16 tensor-core GEMM, fp32 "
+                      "accumulate) -> top_k 64, T=1, top_p 0.95; median of 5 replays of a 20-call CUDA graph"}
+
+
 def run_c5_sharded(s_unused, rank, world, local, dev, peak, steps=200):
     """Config C5 in the vocabulary-sharded mode: 1024 fp32 rows, each rank
     holding a contiguous V/world slice of every row (per-row T, top-K, top-P);
@@ -336,6 +394,9 @@ def main():
     dev = torch.device("cuda", local)
     K, W = args.steps, args.warmup
     peak, peak_kind = load_peak()
+    if args.only == "c4":
+        emit({"c4": run_c4(dev, peak)})
+        return
 
     # ---- inputs: 4 rotating sets of C3 rows (4 x 128 MiB > 126 MB L2) ----
     base = synth.c3_logits(ROWS, step=rank)
@@ -476,6 +537,7 @@ def main():
                         "(256 MiB > L2); 200 calls per CUDA graph, median of 5 replays"}
         del g2, c2sets
 
+    c4 = run_c4(dev, peak) if rank == 0 and args.only is None else None
     # ---- end to end through g4s_sample_host (pinned host memory, PCIe inside) ----
     e2e = None
     if not args.no_e2e:
@@ -531,6 +593,7 @@ def main():
                          "step_hbm_frac": ROWS * BYTES_PER_ROW / (total_ms_max / K * 1e-3) / 1e9 / peak},
             "latency_b1": lat,
             "c2": c2,
+            "c4": c4,
             "c5_sharded": c5,
             "e2e": e2e,
             "cpu_baseline": cpu,
