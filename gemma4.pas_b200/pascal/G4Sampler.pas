@@ -41,6 +41,14 @@ const
   G4S_ROW_FULL_PATH = 4;
   G4S_ROW_GREEDY    = 8;
 
+  G4S_PHASE_FULL_STREAM_ONLY = 1;
+
+  G4S_NOALLOC_MAX_ROWS  = 64;
+  G4S_NOALLOC_MAX_LISTS = 1024;
+
+  G4S_SHARD_LIST      = 256;   { composites per row per shard list }
+  G4S_SHARD_UID_BYTES = 128;
+
 type
   { Same layout as TSamplingParams (src/Gemma4.Model.pas:70-76): four 4-byte
     fields at offsets 0/4/8/12, so a TSamplingParams can be passed by address. }
@@ -88,6 +96,38 @@ function g4s_sample_host(Ctx: PG4SCtx; HostLogits: Pointer; DType, Rows,
   Vocab: Int32; RowStride: Int64; Params: PG4SParams; ParamsStride: Int32;
   Softcap: Single; HostU: PDouble; HostTokens: PInt32): Int32; cdecl;
   external G4SLib;
+
+{ Top-K sampling without a context or any allocation (static scratch). }
+function g4s_sample_topk_noalloc(Logits: Pointer; DType, Rows, Vocab: Int32;
+  RowStride: Int64; Params: PG4SParams; Softcap: Single; U: PDouble;
+  OutTokens: PInt32; Stream: Pointer): Int32; cdecl; external G4SLib;
+
+{ LM head (CpuMatVecQ4, src/Gemma4.Tensors.pas:546-590) + DoSample: TQ4Block
+  weights repacked once on the device, then one call per step. }
+function g4s_q4_repack(Blocks: Pointer; Vocab, Hidden: Int32; Nibbles: Pointer;
+  Scales: Pointer; Stream: Pointer): Int32; cdecl; external G4SLib;
+function g4s_lmhead_sample(Ctx: PG4SCtx; Hidden: PSingle; Rows, HiddenSize: Int32;
+  Nibbles: Pointer; Scales: Pointer; Vocab: Int32; Params: PG4SParams;
+  ParamsStride: Int32; Softcap: Single; U: PDouble; OutTokens: PInt32;
+  Extra: PG4SOutputs; OutLogits: PSingle; Stream: Pointer): Int32; cdecl;
+  external G4SLib;
+
+{ Vocabulary-sharded mode: compute phases (any collective) and the NCCL form. }
+function g4s_shard_lists(Ctx: PG4SCtx; Logits: Pointer; DType, Rows, SliceVocab: Int32;
+  RowStride: Int64; IdOffset, VocabTotal: Int32; Params: PG4SParams;
+  ParamsStride: Int32; OutLists: Pointer; OutCounts: PInt32;
+  Stream: Pointer): Int32; cdecl; external G4SLib;
+function g4s_shard_merge(Ctx: PG4SCtx; Lists: Pointer; Counts: PInt32;
+  World, Rows, VocabTotal: Int32; Params: PG4SParams; ParamsStride: Int32;
+  Softcap: Single; U: PDouble; OutTokens: PInt32; Extra: PG4SOutputs;
+  Stream: Pointer): Int32; cdecl; external G4SLib;
+function g4s_shard_unique_id(Uid: PByte): Int32; cdecl; external G4SLib;
+function g4s_shard_init(Ctx: PG4SCtx; World, Rank, VocabTotal: Int32;
+  Uid: PByte): Int32; cdecl; external G4SLib;
+function g4s_shard_sample(Ctx: PG4SCtx; LogitsSlice: Pointer; DType, Rows: Int32;
+  RowStride: Int64; Params: PG4SParams; ParamsStride: Int32; Softcap: Single;
+  U: PDouble; OutTokens: PInt32; Extra: PG4SOutputs;
+  Stream: Pointer): Int32; cdecl; external G4SLib;
 
 implementation
 
