@@ -29,7 +29,7 @@
 namespace g4s {
 
 struct TopkSmem {
-    uint64_t L[CAP2];
+    alignas(16) uint64_t L[CAP2];
     alignas(16) float tv[KMAX];
     int32_t ids[KMAX];
     uint32_t hist[256];
@@ -98,6 +98,8 @@ __device__ void topk_tail(const SampleArgs &a, int row, const g4s_params &p, int
                           TopkSmem &sm)
 {
     const int lane = threadIdx.x & 31;
+    // the draw is needed only at the end; its load is issued first
+    const double u_row = (lane == 0 && p.temperature > 0.0f && kw > 0) ? a.u[row] : 0.0;
     int32_t flags = p.temperature > 0.0f ? 0 : G4S_ROW_GREEDY;
     int32_t token = -1;
     float tprob = 0.0f;
@@ -129,6 +131,7 @@ __device__ void topk_tail(const SampleArgs &a, int row, const g4s_params &p, int
             // four values per shared-memory load; only the fp32 adds are serial
             float s = 0.0f;
             int i = 0;
+#pragma unroll 4
             for (; i + 4 <= kw; i += 4) {
                 const float4 q = *reinterpret_cast<const float4 *>(&sm.tv[i]);
                 s = __fadd_rn(s, q.x);
@@ -160,7 +163,7 @@ __device__ void topk_tail(const SampleArgs &a, int row, const g4s_params &p, int
         // index-order cumulative draw against fl32(Random * TopP) (src/Gemma4.Model.pas:2809-2824)
         if (p.temperature > 0.0f) {
             if (lane == 0) {
-                const float thr = __double2float_rn(a.u[row] * (double)p.top_p);
+                const float thr = __double2float_rn(u_row * (double)p.top_p);
                 float cum = 0.0f;
                 int found = -1;
                 int i = 0;
@@ -212,9 +215,20 @@ __device__ __forceinline__ void sort_list_desc(TopkSmem &sm, int n)
         const int t = threadIdx.x;
         if (t < n) {
             const uint64_t v = sm.L[t];
-            int r = 0;
-            for (int q = 0; q < n; q++) r += sm.L[q] > v;
-            out[r] = v;
+            // two keys per 16-byte load, four independent counts: the loads of
+            // consecutive iterations overlap instead of chaining
+            int r0 = 0, r1 = 0, r2 = 0, r3 = 0, q = 0;
+            const ulonglong2 *L2 = reinterpret_cast<const ulonglong2 *>(sm.L);
+#pragma unroll 4
+            for (; q + 4 <= n; q += 4) {
+                const ulonglong2 x = L2[q >> 1], y = L2[(q >> 1) + 1];
+                r0 += x.x > v;
+                r1 += x.y > v;
+                r2 += y.x > v;
+                r3 += y.y > v;
+            }
+            for (; q < n; q++) r0 += sm.L[q] > v;
+            out[r0 + r1 + r2 + r3] = v;
         }
         __syncthreads();
         if (t < n) sm.L[t] = out[t];
