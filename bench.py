@@ -47,6 +47,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-c4", action="store_true", help="skip the config C4 (LM head) record")
     ap.add_argument("--only", choices=["c4"], default=None,
                     help="run config C4 alone and print its record (for profiling)")
     return ap.parse_args()
@@ -537,7 +538,7 @@ def main():
                         "(256 MiB > L2); 200 calls per CUDA graph, median of 5 replays"}
         del g2, c2sets
 
-    c4 = run_c4(dev, peak) if rank == 0 and args.only is None else None
+    c4 = run_c4(dev, peak) if rank == 0 and not args.no_c4 else None
     # ---- end to end through g4s_sample_host (pinned host memory, PCIe inside) ----
     e2e = None
     if not args.no_e2e:

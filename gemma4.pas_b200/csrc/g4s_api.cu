@@ -548,9 +548,10 @@ int32_t g4s_q4_repack(const uint8_t *blocks, int32_t vocab, int32_t hidden, uint
 }
 
 int32_t g4s_lmhead_sample(g4s_ctx *ctx, const float *hidden, int32_t rows, int32_t hidden_size,
-                          const uint8_t *nibbles, const uint16_t *scales, int32_t vocab, const g4s_params *params,
-                          int32_t params_stride, float softcap, const double *u, int32_t *out_tokens,
-                          const g4s_outputs *extra, float *out_logits, void *stream)
+                          const float *norm_weight, float norm_eps, const uint8_t *nibbles, const uint16_t *scales,
+                          int32_t vocab, const g4s_params *params, int32_t params_stride, float softcap,
+                          const double *u, int32_t *out_tokens, const g4s_outputs *extra, float *out_logits,
+                          void *stream)
 {
     static const char *who = "g4s_lmhead_sample";
     if (!ctx) return fail(nullptr, G4S_ERR_ARG, "%s: ctx is NULL", who);
@@ -590,8 +591,8 @@ int32_t g4s_lmhead_sample(g4s_ctx *ctx, const float *hidden, int32_t rows, int32
         ctx->lm_xh_n = need_x;
     }
     if (!logits) logits = ctx->lm_logits;
-    const cudaError_t e = launch_lmhead(hidden, rows, hidden_size, nibbles, scales, vocab, (__half *)ctx->lm_xh,
-                                        logits, s);
+    const cudaError_t e = launch_lmhead(hidden, rows, hidden_size, norm_weight, norm_eps, nibbles, scales, vocab,
+                                        (__half *)ctx->lm_xh, logits, s);
     if (e != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "%s: launch failed: %s", who, cudaGetErrorString(e));
     return g4s_sample_ex(ctx, logits, G4S_F32, rows, vocab, vocab, params, params_stride, softcap, u, out_tokens,
                          extra, s);

@@ -64,13 +64,40 @@ __global__ void q4_repack_kernel(const uint8_t *__restrict__ blocks, int64_t nbl
     *reinterpret_cast<uint4 *>(nib + b * 16) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// hidden fp32 [rows][H] -> fp16 [64][H] in the permuted block order; rows >= rows are zero.
-__global__ void lmhead_prep_kernel(const float *__restrict__ hidden, int rows, int H, __half *__restrict__ xh)
+// hidden fp32 [rows][H] -> fp16 [64][H] in the permuted block order; rows >= rows
+// are zero.  With norm_w, the final RMSNorm first (CpuRmsNorm,
+// src/Gemma4.Layers.pas:142-175): rms = sqrt(sum(x^2) / H + eps), scale = 1/rms,
+// x * scale * w -- the same per-element fp32 operations; the sum of squares is a
+// block reduction (the reference adds serially; both are fp32 sums of H terms).
+// One CTA per row.
+__global__ void __launch_bounds__(256) lmhead_prep_kernel(const float *__restrict__ hidden, int rows, int H,
+                                                          const float *__restrict__ norm_w, float eps,
+                                                          __half *__restrict__ xh)
 {
-    const int m = blockIdx.y;
-    for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < H; k += gridDim.x * blockDim.x) {
-        const int base = k & ~31;
-        const float v = m < rows ? hidden[(int64_t)m * H + base + lm_phys(k & 31)] : 0.0f;
+    __shared__ float red[8];
+    const int m = blockIdx.x, tid = threadIdx.x;
+    const float *x = hidden + (int64_t)m * H;
+    float scale = 1.0f;
+    if (norm_w && m < rows) {
+        float ss = 0.0f;
+        for (int k = tid; k < H; k += 256) ss = __fmaf_rn(x[k], x[k], ss);
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+        if ((tid & 31) == 0) red[tid >> 5] = ss;
+        __syncthreads();
+        ss = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; w++) ss += red[w];
+        const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), eps));
+        scale = __fdiv_rn(1.0f, rms);
+    }
+    for (int k = tid; k < H; k += 256) {
+        const int src = (k & ~31) + lm_phys(k & 31);
+        float v = 0.0f;
+        if (m < rows) {
+            v = x[src];
+            if (norm_w) v = __fmul_rn(__fmul_rn(v, scale), norm_w[src]);
+        }
         xh[(int64_t)m * H + k] = __float2half_rn(v);
     }
 }
@@ -217,8 +244,8 @@ cudaError_t launch_q4_repack(const uint8_t *blocks, int vocab, int hidden, uint8
     return cudaGetLastError();
 }
 
-cudaError_t launch_lmhead(const float *hidden, int rows, int H, const uint8_t *nib, const uint16_t *scales, int vocab,
-                          __half *xh, float *logits, cudaStream_t s)
+cudaError_t launch_lmhead(const float *hidden, int rows, int H, const float *norm_w, float eps, const uint8_t *nib,
+                          const uint16_t *scales, int vocab, __half *xh, float *logits, cudaStream_t s)
 {
     static bool attr = false;
     if (!attr) {
@@ -227,7 +254,7 @@ cudaError_t launch_lmhead(const float *hidden, int rows, int H, const uint8_t *n
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    lmhead_prep_kernel<<<dim3((unsigned)((H + 255) / 256), LM_M), 256, 0, s>>>(hidden, rows, H, xh);
+    lmhead_prep_kernel<<<LM_M, 256, 0, s>>>(hidden, rows, H, norm_w, eps, xh);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     lmhead_gemm_kernel<<<(unsigned)((vocab + LM_N - 1) / LM_N), LM_THREADS, sizeof(LmSmem), s>>>(xh, nib, scales, rows,

@@ -58,9 +58,9 @@ SIGNATURES = {
     "g4s_sample_topk_noalloc": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_int64, POINTER(Params),
                                           c_float, c_void_p, c_void_p, c_void_p]),
     "g4s_q4_repack": (c_int32, [c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
-    "g4s_lmhead_sample": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_int32,
-                                    POINTER(Params), c_int32, c_float, c_void_p, c_void_p, POINTER(Outputs),
-                                    c_void_p, c_void_p]),
+    "g4s_lmhead_sample": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_float, c_void_p, c_void_p,
+                                    c_int32, POINTER(Params), c_int32, c_float, c_void_p, c_void_p,
+                                    POINTER(Outputs), c_void_p, c_void_p]),
     "g4s_shard_lists": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int64, c_int32, c_int32,
                                   POINTER(Params), c_int32, c_void_p, c_void_p, c_void_p]),
     "g4s_shard_merge": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, POINTER(Params),
@@ -234,10 +234,12 @@ class Sampler:
 
     def lmhead_sample(self, hidden_ptr: int, rows: int, hidden: int, nib_ptr: int, scales_ptr: int, vocab: int,
                       params, softcap: float, u_ptr: int, out_ptr: int, outputs: Outputs | None = None,
-                      logits_ptr: int = 0, stream: int | None = None, check: bool = True) -> int:
-        """g4s_lmhead_sample: logits = hidden x W^T (Q4_0, repacked) then sampling."""
+                      logits_ptr: int = 0, stream: int | None = None, check: bool = True, norm_ptr: int = 0,
+                      norm_eps: float = 1e-6) -> int:
+        """g4s_lmhead_sample: [final RMSNorm,] logits = hidden x W^T (Q4_0, repacked), sampling."""
         parr, pstride = self._params(params, rows)
-        rc = self.lib.g4s_lmhead_sample(self.h, c_void_p(hidden_ptr), rows, hidden, c_void_p(nib_ptr),
+        rc = self.lib.g4s_lmhead_sample(self.h, c_void_p(hidden_ptr), rows, hidden,
+                                        c_void_p(norm_ptr) if norm_ptr else None, norm_eps, c_void_p(nib_ptr),
                                         c_void_p(scales_ptr), vocab, parr, pstride, softcap, c_void_p(u_ptr),
                                         c_void_p(out_ptr), ctypes.byref(outputs) if outputs is not None else None,
                                         c_void_p(logits_ptr) if logits_ptr else None,

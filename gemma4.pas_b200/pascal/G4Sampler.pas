@@ -107,6 +107,7 @@ function g4s_sample_topk_noalloc(Logits: Pointer; DType, Rows, Vocab: Int32;
 function g4s_q4_repack(Blocks: Pointer; Vocab, Hidden: Int32; Nibbles: Pointer;
   Scales: Pointer; Stream: Pointer): Int32; cdecl; external G4SLib;
 function g4s_lmhead_sample(Ctx: PG4SCtx; Hidden: PSingle; Rows, HiddenSize: Int32;
+  NormWeight: PSingle; NormEps: Single;
   Nibbles: Pointer; Scales: Pointer; Vocab: Int32; Params: PG4SParams;
   ParamsStride: Int32; Softcap: Single; U: PDouble; OutTokens: PInt32;
   Extra: PG4SOutputs; OutLogits: PSingle; Stream: Pointer): Int32; cdecl;

@@ -202,7 +202,10 @@ int32_t g4s_sample_topk_noalloc(const void *logits, int32_t dtype, int32_t rows,
  * rows <= 64 (hidden fp32 on the device, rounded to fp16; w = (nibble - 8) *
  * scale rounded once to fp16; fp16 tensor-core products, fp32 accumulation),
  * then samples them exactly as g4s_sample_ex.  hidden must be a multiple of
- * 128, vocab of 8.  out_logits (device, rows x vocab fp32) receives the logits
+ * 128, vocab of 8.  norm_weight (device, hidden fp32; NULL = the hidden
+ * states are already normalized) applies the model's final RMSNorm first,
+ * CpuRmsNorm (src/Gemma4.Layers.pas:142-175) with eps norm_eps (1e-6 in the
+ * reference, src/Gemma4.Types.pas:48), fused into the activation prologue.  out_logits (device, rows x vocab fp32) receives the logits
  * when non-NULL; otherwise they stay in a context buffer allocated by the
  * first call.
  */
@@ -210,9 +213,10 @@ int32_t g4s_q4_repack(const uint8_t *blocks, int32_t vocab, int32_t hidden, uint
                       void *stream);
 
 int32_t g4s_lmhead_sample(g4s_ctx *ctx, const float *hidden, int32_t rows, int32_t hidden_size,
-                          const uint8_t *nibbles, const uint16_t *scales, int32_t vocab, const g4s_params *params,
-                          int32_t params_stride, float softcap, const double *u, int32_t *out_tokens,
-                          const g4s_outputs *extra, float *out_logits, void *stream);
+                          const float *norm_weight, float norm_eps, const uint8_t *nibbles, const uint16_t *scales,
+                          int32_t vocab, const g4s_params *params, int32_t params_stride, float softcap,
+                          const double *u, int32_t *out_tokens, const g4s_outputs *extra, float *out_logits,
+                          void *stream);
 
 /*
  * Vocabulary-sharded mode (no counterpart in the reference, which samples one

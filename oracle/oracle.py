@@ -76,6 +76,8 @@ def load():
     lib.ref_sample_batch.restype = c_int32
     lib.ref_sample_batch.argtypes = [c_void_p, c_int32, c_int32, c_int32, c_int64, c_void_p, c_int32,
                                      c_float, c_void_p, c_int32, c_int32, c_void_p, c_int32]
+    lib.ref_rmsnorm.restype = None
+    lib.ref_rmsnorm.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_float]
     lib.ref_matvec_q4.restype = None
     lib.ref_matvec_q4.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int32]
     lib.ref_matvec_q4_f64.restype = None
@@ -151,4 +153,14 @@ def matvec_q4(blocks: np.ndarray, vec: np.ndarray, rows: int, cols: int, f64=Fal
     blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
     out = np.empty(rows, dtype=np.float64 if f64 else np.float32)
     (lib.ref_matvec_q4_f64 if f64 else lib.ref_matvec_q4)(_ptr(blocks), _ptr(vec), _ptr(out), rows, cols)
+    return out
+
+
+def rmsnorm(x, w, eps=1e-6):
+    """CpuRmsNorm on one fp32 vector."""
+    lib = load()
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    out = np.empty_like(x)
+    lib.ref_rmsnorm(_ptr(x), _ptr(w), _ptr(out), x.shape[0], eps)
     return out

@@ -619,3 +619,14 @@ void ref_matvec_q4_f64(const uint8_t *blocks, const float *vec, double *dst, int
         dst[r] = sum;
     }
 }
+
+/* CpuRmsNorm (src/Gemma4.Layers.pas:142-175): serial fp32 sum of squares,
+   rms = sqrt(sum / n + eps), scale = 1 / rms, out = x * scale * w. */
+void ref_rmsnorm(const float *x, const float *w, float *out, int32_t n, float eps)
+{
+    float ss = 0.0f;
+    for (int32_t i = 0; i < n; i++) ss = ss + x[i] * x[i];
+    const float rms = sqrtf(ss / (float)n + eps);
+    const float scale = 1.0f / rms;
+    for (int32_t i = 0; i < n; i++) out[i] = (x[i] * scale) * w[i];
+}

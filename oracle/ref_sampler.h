@@ -21,6 +21,7 @@
  *   src/Gemma4.Layers.pas:300-316         CpuLogitSoftcap
  *   src/Gemma4.Tensors.pas:638-674        CpuSoftmaxF32
  *   src/Gemma4.Tensors.pas:546-590        CpuMatVecQ4 (LM-head GEMV, Q4_0)
+ *   src/Gemma4.Layers.pas:142-175         CpuRmsNorm (final norm before the LM head)
  *   src/Gemma4.Types.pas:139-142          TQ4Block
  *   src/Gemma4.Types.pas:417-500          TBFloat16 / TFloat16 codecs
  *
@@ -126,6 +127,9 @@ void ref_matvec_q4(const uint8_t *blocks, const float *vec, float *dst, int32_t 
 /* Same, fp64 accumulation (exact-product reference for tolerance checks). */
 void ref_matvec_q4_f64(const uint8_t *blocks, const float *vec, double *dst, int32_t rows,
                        int32_t cols);
+
+/* Final RMSNorm (src/Gemma4.Layers.pas:142-175), the LM head's input. */
+void ref_rmsnorm(const float *x, const float *w, float *out, int32_t n, float eps);
 
 #ifdef __cplusplus
 }

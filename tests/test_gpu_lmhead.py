@@ -84,3 +84,39 @@ def test_lmhead_full_size_sample(g4, torch_cuda, oracle):
     bound = 2.0 ** -9 * (np.abs(h.astype(np.float64)) @ np.abs(W).T) + 1e-6
     assert (np.abs(lg[:, pick] - want) <= bound).all()
     check_topk_rows(oracle, lg[::8], F32, prm, CAP, u[::8], {"tokens": tok[::8]})
+
+
+def test_lmhead_with_fused_final_norm(g4, torch_cuda, oracle):
+    # raw hidden states + the final RMSNorm weight: the prologue applies
+    # CpuRmsNorm before the fp16 conversion
+    torch = torch_cuda
+    rows, hidden, vocab = 12, 2560, 4096
+    h, blocks = synth.c4_inputs(rows, hidden, vocab)
+    rng = np.random.default_rng(21)
+    h = (h * rng.uniform(0.5, 3.0, (rows, 1)) + 0.1).astype(np.float32)  # not normalized
+    gamma = rng.uniform(0.5, 1.5, hidden).astype(np.float32)
+    u = synth.uniforms(rows, 0x4E)
+    prm = g4.make_params(0.8, 40, 0.9)
+    bd = torch.from_numpy(blocks).cuda()
+    nib = torch.empty(vocab * hidden // 2, dtype=torch.uint8, device="cuda")
+    sc = torch.empty(vocab * hidden // 32, dtype=torch.int16, device="cuda")
+    g4.q4_repack(bd.data_ptr(), vocab, hidden, nib.data_ptr(), sc.data_ptr())
+    hd, gd, ud = (torch.from_numpy(a).cuda() for a in (h, gamma, u))
+    out = torch.full((rows,), -5, dtype=torch.int32, device="cuda")
+    logits = torch.empty((rows, vocab), dtype=torch.float32, device="cuda")
+    s = g4.Sampler(0, 64, vocab)
+    try:
+        s.lmhead_sample(hd.data_ptr(), rows, hidden, nib.data_ptr(), sc.data_ptr(), vocab, prm, CAP, ud.data_ptr(),
+                        out.data_ptr(), logits_ptr=logits.data_ptr(), norm_ptr=gd.data_ptr(), norm_eps=1e-6)
+        torch.cuda.synchronize()
+    finally:
+        s.close()
+    lg, tok = logits.cpu().numpy(), out.cpu().numpy()
+    xn = np.stack([oracle.rmsnorm(h[r], gamma, 1e-6) for r in range(rows)]).astype(np.float64)
+    W = _dequant(blocks, vocab, hidden)
+    want = xn @ W.T
+    # fp32 norm differences (block vs serial sum of squares) are ~1e-7 relative,
+    # far inside the fp16 bound
+    bound = 2.0 ** -9 * (np.abs(xn) @ np.abs(W).T) + 1e-5
+    assert (np.abs(lg - want) <= bound).all()
+    check_topk_rows(oracle, lg, F32, prm, CAP, u, {"tokens": tok})

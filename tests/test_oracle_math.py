@@ -56,3 +56,14 @@ def test_g4_tanhf_edges(oracle):
     assert lib.g4_tanhf(0.0) == 0.0
     assert lib.g4_tanhf(50.0) == 1.0
     assert lib.g4_tanhf(-7.0) == -lib.g4_tanhf(7.0)
+
+
+def test_rmsnorm_restatement(oracle):
+    # CpuRmsNorm (src/Gemma4.Layers.pas:142-175) against an fp64 evaluation
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal(2560).astype(np.float32) * 3
+    w = rng.uniform(0.5, 1.5, 2560).astype(np.float32)
+    got = oracle.rmsnorm(x, w, 1e-6)
+    xd = x.astype(np.float64)
+    want = xd / np.sqrt(np.mean(xd * xd) + 1e-6) * w
+    assert np.max(np.abs(got - want) / np.abs(want)) < 1e-5
