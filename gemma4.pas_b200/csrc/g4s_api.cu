@@ -59,6 +59,7 @@ struct g4s_ctx {
     // LM head workspace (first g4s_lmhead_sample call): fp32 logits and fp16 hidden
     float *lm_logits = nullptr;
     void *lm_xh = nullptr;
+    int *dev_err = nullptr;  // device error flag (a bounded wait that ran out), read by g4s_device_status
     size_t lm_logits_n = 0, lm_xh_n = 0;
     // g4s_sample_host staging
     void *h_logits = nullptr;
@@ -388,6 +389,7 @@ int32_t g4s_destroy(g4s_ctx *ctx)
     shard_release(ctx);
     if (ctx->lm_logits) cudaFree(ctx->lm_logits);
     if (ctx->lm_xh) cudaFree(ctx->lm_xh);
+    if (ctx->dev_err) cudaFree(ctx->dev_err);
     delete ctx;
     return G4S_OK;
 }
@@ -591,11 +593,35 @@ int32_t g4s_lmhead_sample(g4s_ctx *ctx, const float *hidden, int32_t rows, int32
         ctx->lm_xh_n = need_x;
     }
     if (!logits) logits = ctx->lm_logits;
+    if (!ctx->dev_err) {
+        if (cudaMalloc(&ctx->dev_err, sizeof(int)) != cudaSuccess || cudaMemset(ctx->dev_err, 0, sizeof(int)) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(ctx, G4S_ERR_NOMEM, "%s: cannot allocate the error flag", who);
+        }
+    }
     const cudaError_t e = launch_lmhead(hidden, rows, hidden_size, norm_weight, norm_eps, nibbles, scales, vocab,
-                                        (__half *)ctx->lm_xh, logits, s);
+                                        (__half *)ctx->lm_xh, logits, ctx->dev_err, s);
     if (e != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "%s: launch failed: %s", who, cudaGetErrorString(e));
     return g4s_sample_ex(ctx, logits, G4S_F32, rows, vocab, vocab, params, params_stride, softcap, u, out_tokens,
                          extra, s);
+}
+
+int32_t g4s_device_status(g4s_ctx *ctx)
+{
+    if (!ctx) return fail(nullptr, G4S_ERR_ARG, "g4s_device_status: ctx is NULL");
+    if (!ctx->dev_err) return G4S_OK;
+    DeviceGuard guard(ctx->device);
+    int v = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess ||
+        cudaMemcpy(&v, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaError_t e = cudaGetLastError();
+        return fail(ctx, G4S_ERR_CUDA, "g4s_device_status: %s", cudaGetErrorString(e));
+    }
+    if (v) {
+        cudaMemset(ctx->dev_err, 0, sizeof(int));
+        return fail(ctx, G4S_ERR_TIMEOUT, "g4s_device_status: a kernel's bounded wait ran out (its results are invalid)");
+    }
+    return G4S_OK;
 }
 
 // ---------------------------------------------------------------------------

@@ -88,7 +88,7 @@ namespace g4s {
 cudaError_t launch_q4_repack(const uint8_t *blocks, int vocab, int hidden, uint8_t *nib, uint16_t *scales,
                              cudaStream_t s);
 cudaError_t launch_lmhead(const float *hidden, int rows, int H, const float *norm_w, float eps, const uint8_t *nib,
-                          const uint16_t *scales, int vocab, __half *xh, float *logits, cudaStream_t s);
+                          const uint16_t *scales, int vocab, __half *xh, float *logits, int *err, cudaStream_t s);
 constexpr int LMHEAD_MAX_ROWS = 64;
 
 // Vocabulary-sharded mode: the gathered per-shard lists merged into each row's

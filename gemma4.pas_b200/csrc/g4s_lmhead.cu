@@ -1,23 +1,15 @@
 // g4s_lmhead.cu -- LM head for the sampler (config C4): logits = hidden x W^T
 // with W in Q4_0 (src/Gemma4.Tensors.pas:546-590 CpuMatVecQ4; block format
 // src/Gemma4.Types.pas:139-142: fp16 scale, then 16 bytes whose byte j holds
-// element 2j in its low nibble and 2j+1 in its high nibble; value = nibble - 8).
+// element 2j in its low nibble and 2j+1 in its high nibble; value = nibble - 8),
+// on the 5th-generation tensor cores (tcgen05, accumulators in TMEM).
 //
 // Layout on the device (q4_repack_kernel, once per weight set, as the
-// reference repacks its GPU copy at load time, src/Gemma4.Model.pas:508-530):
-//   nibbles [vocab][hidden/2]  the 16 nibble bytes of each block, contiguous
-//   scales  [vocab][hidden/32] fp16 bits
-// so every row is 16-byte aligned for cp.async.
-//
-// lmhead_gemm_kernel: one CTA computes a 64 (batch rows, zero-padded) x 256
-// (vocab rows) tile over the whole hidden dimension with fp16 tensor-core MMAs
-// (mma.sync m16n8k16, fp32 accumulation); hidden chunks of 128 go through a
-// two-stage cp.async pipeline.  Each lane's B fragments for one Q4 block come
-// from ONE 32-bit word of nibbles: the half2 pairs that a shift and a LOP3 make
-// cheaply are (n0,n4), (n1,n5), (n2,n6), (n3,n7), so the MMA's k order inside a
-// block is permuted to match and the activations are permuted the same way
-// when they are converted to fp16 (lmhead_prep_kernel).  Weights dequantize
-// exactly as (nibble - 8) * scale rounded once to fp16.
+// reference repacks its GPU copy at load time, src/Gemma4.Model.pas:508-530),
+// grouped by pairs of hidden blocks so that one pipeline stage (64 hidden
+// elements) of a CTA's 256 vocabulary rows is one contiguous 8 KiB read:
+//   nibbles [hidden/64][vocab][2][16]  the 16 nibble bytes of block 2g+i of row v
+//   scales  [hidden/64][vocab][2]      fp16 bits
 #include <cuda_fp16.h>
 
 #include "g4s_device.cuh"
@@ -25,110 +17,23 @@
 
 namespace g4s {
 
-constexpr int LM_M = 64;        // batch rows per tile (rows are zero-padded to 64)
-constexpr int LM_N = 256;       // vocab rows per CTA
-constexpr int LM_KC = 128;      // hidden elements per pipeline stage (4 Q4 blocks)
-constexpr int LM_THREADS = 256;
-constexpr int LM_AS = LM_KC + 8;          // A row stride in halfs (272 B: ldmatrix conflict-free)
-constexpr int LM_WS = LM_KC / 2 + 16;     // nibble row stride in bytes (80 B: conflict-free words)
-constexpr int LM_SS = LM_KC / 32;         // scales per row per stage
+constexpr int Q4_GROUP = 2;  // hidden blocks per group of the device layout
 
-struct LmSmem {
-    __half a[2][LM_M][LM_AS];
-    uint8_t w[2][LM_N][LM_WS];
-    __half s[2][LM_N][LM_SS];
-};
-
-// Physical element (0..31) of a Q4 block that logical MMA position L (0..31)
-// reads: lane t's word t supplies (8t, 8t+4), (8t+1, 8t+5) for k-step 0 and
-// (8t+2, 8t+6), (8t+3, 8t+7) for k-step 1.
-__host__ __device__ __forceinline__ int lm_phys(int L)
-{
-    const int s = L >> 4, r = L & 15;
-    const int t = (r & 7) >> 1, hi8 = r >> 3, e = r & 1;
-    return 8 * t + 2 * s + hi8 + 4 * e;
-}
-
-__global__ void q4_repack_kernel(const uint8_t *__restrict__ blocks, int64_t nblocks, uint8_t *__restrict__ nib,
+__global__ void q4_repack_kernel(const uint8_t *__restrict__ blocks, int vocab, int bpr, uint8_t *__restrict__ nib,
                                  uint16_t *__restrict__ scales)
 {
-    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (b >= nblocks) return;
-    const uint8_t *src = blocks + b * 18;
-    scales[b] = (uint16_t)(src[0] | (src[1] << 8));
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // source block, row-major
+    if (i >= (int64_t)vocab * bpr) return;
+    const int v = (int)(i / bpr), b = (int)(i - (int64_t)v * bpr);
+    const uint8_t *src = blocks + i * 18;
+    const int64_t dst = ((int64_t)(b / Q4_GROUP) * vocab + v) * Q4_GROUP + b % Q4_GROUP;
+    scales[dst] = (uint16_t)(src[0] | (src[1] << 8));
     uint32_t w[4];
 #pragma unroll
-    for (int i = 0; i < 4; i++)
-        w[i] = (uint32_t)src[2 + 4 * i] | ((uint32_t)src[3 + 4 * i] << 8) | ((uint32_t)src[4 + 4 * i] << 16) |
-               ((uint32_t)src[5 + 4 * i] << 24);
-    *reinterpret_cast<uint4 *>(nib + b * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-}
-
-// hidden fp32 [rows][H] -> fp16 [64][H] in the permuted block order; rows >= rows
-// are zero.  With norm_w, the final RMSNorm first (CpuRmsNorm,
-// src/Gemma4.Layers.pas:142-175): rms = sqrt(sum(x^2) / H + eps), scale = 1/rms,
-// x * scale * w -- the same per-element fp32 operations; the sum of squares is a
-// block reduction (the reference adds serially; both are fp32 sums of H terms).
-// One CTA per row.
-__global__ void __launch_bounds__(256) lmhead_prep_kernel(const float *__restrict__ hidden, int rows, int H,
-                                                          const float *__restrict__ norm_w, float eps,
-                                                          __half *__restrict__ xh)
-{
-    __shared__ float red[8];
-    const int m = blockIdx.x, tid = threadIdx.x;
-    const float *x = hidden + (int64_t)m * H;
-    float scale = 1.0f;
-    if (norm_w && m < rows) {
-        float ss = 0.0f;
-        for (int k = tid; k < H; k += 256) ss = __fmaf_rn(x[k], x[k], ss);
-#pragma unroll
-        for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
-        if ((tid & 31) == 0) red[tid >> 5] = ss;
-        __syncthreads();
-        ss = 0.0f;
-#pragma unroll
-        for (int w = 0; w < 8; w++) ss += red[w];
-        const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), eps));
-        scale = __fdiv_rn(1.0f, rms);
-    }
-    for (int k = tid; k < H; k += 256) {
-        const int src = (k & ~31) + lm_phys(k & 31);
-        float v = 0.0f;
-        if (m < rows) {
-            v = x[src];
-            if (norm_w) v = __fmul_rn(__fmul_rn(v, scale), norm_w[src]);
-        }
-        xh[(int64_t)m * H + k] = __float2half_rn(v);
-    }
-}
-
-__device__ __forceinline__ void lm_cp16(void *smem, const void *gmem, bool valid)
-{
-    const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
-    const int n = valid ? 16 : 0;  // zero-fill rows past the vocabulary
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sa), "l"(gmem), "r"(n) : "memory");
-}
-__device__ __forceinline__ void lm_cp8(void *smem, const void *gmem, bool valid)
-{
-    const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
-    const int n = valid ? 8 : 0;
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(sa), "l"(gmem), "r"(n) : "memory");
-}
-
-__device__ __forceinline__ void ldmatrix_x4(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, const void *p)
-{
-    const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(a));
-}
-
-__device__ __forceinline__ void mma16816(float *d, const uint32_t *a, uint32_t b0, uint32_t b1)
-{
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                 "{%0,%1,%2,%3};"
-                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    for (int k = 0; k < 4; k++)
+        w[k] = (uint32_t)src[2 + 4 * k] | ((uint32_t)src[3 + 4 * k] << 8) | ((uint32_t)src[4 + 4 * k] << 16) |
+               ((uint32_t)src[5 + 4 * k] << 24);
+    *reinterpret_cast<uint4 *>(nib + dst * 16) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 // One word of 8 nibbles -> 4 half2 (n_i, n_{i+4}) * scale, each (nibble - 8) * scale rounded once.
@@ -144,121 +49,374 @@ __device__ __forceinline__ void dequant_word(uint32_t w, __half2 sc, uint32_t *h
     }
 }
 
-__global__ void __launch_bounds__(LM_THREADS, 2) lmhead_gemm_kernel(const __half *__restrict__ xh,
-                                                                 const uint8_t *__restrict__ nib,
-                                                                 const uint16_t *__restrict__ scales, int rows,
-                                                                 int vocab, int H, float *__restrict__ logits)
+// ---------------------------------------------------------------------------
+// lmhead_tc_kernel
+//
+// D[v][b] = sum_k W[v][k] x[b][k]: A = dequantized weights (M = 128 vocab rows
+// per MMA, two M-tiles per CTA), B = fp16 activations (N = 64 batch rows),
+// K = 16 per tcgen05.mma, fp32 accumulators in TMEM (128 lanes x 64 columns per
+// M-tile).  One hidden block (32) per iteration:
+//   - the block's nibbles and scales for the CTA's 256 rows (4 KiB + 512 B,
+//     contiguous) arrive by 1-D bulk copies (TMA engine, no multicast) four
+//     iterations ahead (ring of 4), counted on mbarriers;
+//   - each thread dequantizes its row's block into the A tile, laid out in the
+//     canonical K-major, unswizzled core-matrix form (8 rows x 16 bytes), and
+//     fences the writes to the tensor core's proxy (fence.proxy.async);
+//   - one thread issues 4 MMAs (2 k-steps x 2 M-tiles) and commits them to the
+//     stage's mbarrier;
+//   - the next block's activation tile (4 KiB, L2-resident) is a bulk copy
+//     into the other stage once that stage's previous MMAs completed.
+// The only generic-proxy writes to operand memory are each thread's own
+// dequantized rows, so the proxy fence does not wait on any copy in flight.
+// Dequantization, copies and MMAs run in separate warps that meet only at
+// mbarriers (no block barrier inside the loop); three A/B stages and a ring of
+// four nibble stages.  Every mbarrier wait is bounded: on a timeout the
+// kernel sets the error flag, drains (bounded) and frees its TMEM.  The
+// epilogue reads TMEM with tcgen05.ld (warp w: lanes 32*(w%4).., M-tile w/4)
+// and stores the logits.
+//
+// Inside each 8-element K-chunk the k order is permuted: position p holds
+// element (p >> 1) + 4 * (p & 1) of the chunk -- the order in which a shift and
+// a LOP3 pull half2 pairs (n_i, n_{i+4}) out of one 32-bit word of nibbles;
+// lmhead_prep_tc_kernel lays the activations out in the same order.
+// ---------------------------------------------------------------------------
+constexpr int TC_ROWS = 256;                    // vocab rows per CTA (2 M-tiles of 128)
+constexpr int TC_KC = 64;                       // hidden elements per stage (Q4_GROUP blocks)
+constexpr int TC_G = TC_KC / 32;
+static_assert(TC_G == Q4_GROUP, "a stage is one group of the device layout");
+constexpr int TC_THREADS = 256;                // dequant threads (one per vocab row of the CTA)
+constexpr int TC_DQ_WARPS = TC_THREADS / 32;
+constexpr int TC_LOAD_WARP = TC_DQ_WARPS;       // bulk-copy issuer
+constexpr int TC_MMA_WARP = TC_DQ_WARPS + 1;    // tcgen05.mma issuer, TMEM owner
+constexpr int TC_THREADS_ALL = TC_THREADS + 64;
+#ifndef G4S_TC_RS
+#define G4S_TC_RS 4
+#endif
+constexpr int TC_RS = G4S_TC_RS;                // nibble staging ring depth
+#ifndef G4S_TC_AS
+#define G4S_TC_AS 2
+#endif
+constexpr int TC_AS = G4S_TC_AS;                // A/B tile stages (MMA groups in flight)
+constexpr int TC_B_BYTES = 64 * TC_KC * 2;      // 8 KB:  [j 0..7][g 0..7][8 rows][16 B]
+constexpr int TC_RAW_BYTES = TC_ROWS * 16 * TC_G;  // 8 KB of nibbles per stage
+constexpr int TC_SC_BYTES = TC_ROWS * 2 * TC_G;    // 1 KB of scales per stage
+constexpr int TC_RAW_STAGE = TC_RAW_BYTES + TC_SC_BYTES;
+constexpr int TC_SMEM = TC_AS * TC_B_BYTES + TC_RS * TC_RAW_STAGE + 8 * (2 * TC_RS + 3 * TC_AS) + 16;  // + mbarriers, TMEM address
+// TMEM columns: accumulators [mt][64 batch columns] at 0..127, dequantized A
+// operands at 128 + (stage * 2 + mt) * 32 (32 columns = 64 fp16 k-values per lane)
+constexpr int TC_TMEM_COLS = 256;
+constexpr int TC_TMEM_A = 128;
+static_assert(TC_TMEM_A + TC_AS * 2 * (TC_KC / 2) <= TC_TMEM_COLS, "A stages exceed the TMEM allocation");
+// Two CTAs of 256 TMEM columns fill an SM's 512; the launch asks for enough
+// shared memory that a third cannot become resident and wait in tcgen05.alloc.
+constexpr int TC_SMEM_LAUNCH = TC_SMEM > 80 * 1024 ? TC_SMEM : 80 * 1024;
+constexpr uint32_t TC_IDESC = (1u << 4) | ((64u >> 3) << 17) | ((128u >> 4) << 24);  // f16 x f16 -> f32, M128 N64, K-major
+constexpr long TC_WAIT_LIMIT = 1L << 20;
+
+__device__ __forceinline__ int tc_phys8(int p) { return (p >> 1) + 4 * (p & 1); }
+
+// hidden fp32 [rows][H] (optional final RMSNorm) -> fp16 B tiles in global
+// memory: tile c (hidden [32c, 32c+32)) = [j][g][r][8 halfs], batch row 8g + r.
+__global__ void __launch_bounds__(256) lmhead_prep_tc_kernel(const float *__restrict__ hidden, int rows, int H,
+                                                             const float *__restrict__ norm_w, float eps,
+                                                             __half *__restrict__ xt)
 {
-    extern __shared__ __align__(128) uint8_t lm_raw[];
-    LmSmem &sm = *reinterpret_cast<LmSmem *>(lm_raw);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int g = lane >> 2, t = lane & 3;
-    const int v0 = blockIdx.x * LM_N;
-    const int nchunks = H / LM_KC;
-    const int64_t nrow = H / 2, srow = H / 32;
-
-    auto issue = [&](int c, int st) {
-        const int k0 = c * LM_KC;
-        // A: 64 rows x 128 halfs = 64 x 16 vectors of 16 B
-        for (int i = tid; i < LM_M * (LM_KC / 8); i += LM_THREADS) {
-            const int m = i / (LM_KC / 8), j = i % (LM_KC / 8);
-            lm_cp16(&sm.a[st][m][j * 8], xh + (int64_t)m * H + k0 + j * 8, true);
-        }
-        // W nibbles: 256 rows x 64 B = 256 x 4 vectors
-        for (int i = tid; i < LM_N * (LM_KC / 32); i += LM_THREADS) {
-            const int n = i / (LM_KC / 32), j = i % (LM_KC / 32);
-            const bool ok = v0 + n < vocab;
-            lm_cp16(&sm.w[st][n][j * 16], nib + (int64_t)(ok ? v0 + n : 0) * nrow + k0 / 2 + j * 16, ok);
-        }
-        // scales: 256 rows x 4 fp16 (8 B)
-        for (int n = tid; n < LM_N; n += LM_THREADS) {
-            const bool ok = v0 + n < vocab;
-            lm_cp8(&sm.s[st][n][0], scales + (int64_t)(ok ? v0 + n : 0) * srow + k0 / 32, ok);
-        }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-    };
-
-    float acc[4][4][4];  // [m-tile][n-tile][fragment]
+    __shared__ float red[8];
+    const int m = blockIdx.x, tid = threadIdx.x;
+    const float *x = hidden + (int64_t)m * H;
+    float scale = 1.0f;
+    if (norm_w && m < rows) {
+        // CpuRmsNorm (src/Gemma4.Layers.pas:142-175): rms = sqrt(sum(x^2) / H + eps),
+        // scale = 1/rms, x * scale * w; the sum of squares is a block reduction
+        float ss = 0.0f;
+        for (int k = tid; k < H; k += 256) ss = __fmaf_rn(x[k], x[k], ss);
 #pragma unroll
-    for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++)
-#pragma unroll
-            for (int q = 0; q < 4; q++) acc[i][j][q] = 0.0f;
-
-    issue(0, 0);
-    for (int c = 0; c < nchunks; c++) {
-        const int st = c & 1;
-        if (c + 1 < nchunks) {
-            issue(c + 1, st ^ 1);
-            asm volatile("cp.async.wait_group 1;" ::: "memory");
-        } else {
-            asm volatile("cp.async.wait_group 0;" ::: "memory");
-        }
+        for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+        if ((tid & 31) == 0) red[tid >> 5] = ss;
         __syncthreads();
+        ss = 0.0f;
 #pragma unroll
-        for (int b = 0; b < LM_KC / 32; b++) {
-            // B fragments of this warp's 4 n-tiles for block b (2 k-steps)
-            uint32_t bf[4][4];
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int n = warp * 32 + j * 8 + g;
-                const uint32_t w = *reinterpret_cast<const uint32_t *>(&sm.w[st][n][b * 16 + t * 4]);
-                const __half sc = sm.s[st][n][b];
-                dequant_word(w, __halves2half2(sc, sc), bf[j]);
-            }
-#pragma unroll
-            for (int ks = 0; ks < 2; ks++) {
-                const int kk = b * 32 + ks * 16;
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    uint32_t af[4];
-                    ldmatrix_x4(af[0], af[1], af[2], af[3], &sm.a[st][i * 16 + (lane & 15)][kk + (lane >> 4) * 8]);
-#pragma unroll
-                    for (int j = 0; j < 4; j++) mma16816(acc[i][j], af, bf[j][2 * ks], bf[j][2 * ks + 1]);
-                }
-            }
-        }
-        __syncthreads();  // the stage is refilled next iteration
+        for (int w = 0; w < 8; w++) ss += red[w];
+        const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), eps));
+        scale = __fdiv_rn(1.0f, rms);
     }
-    // fragments: (row g, cols 2t, 2t+1) and (row g + 8, same cols)
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int col = v0 + warp * 32 + j * 8 + 2 * t;
-            if (col >= vocab) continue;
-            const int r0 = i * 16 + g, r1 = r0 + 8;
-            if (r0 < rows) *reinterpret_cast<float2 *>(&logits[(int64_t)r0 * vocab + col]) = make_float2(acc[i][j][0], acc[i][j][1]);
-            if (r1 < rows) *reinterpret_cast<float2 *>(&logits[(int64_t)r1 * vocab + col]) = make_float2(acc[i][j][2], acc[i][j][3]);
+    const int g = m >> 3, r = m & 7;
+    for (int k = tid; k < H; k += 256) {
+        const int c = k / TC_KC, j = (k % TC_KC) >> 3, p = k & 7;
+        const int src = c * TC_KC + j * 8 + tc_phys8(p);
+        float v = 0.0f;
+        if (m < rows) {
+            v = x[src];
+            if (norm_w) v = __fmul_rn(__fmul_rn(v, scale), norm_w[src]);
         }
+        xt[(int64_t)c * (64 * TC_KC) + ((j * 8 + g) * 8 + r) * 8 + p] = __float2half_rn(v);
+    }
 }
 
-size_t lmhead_smem_bytes() { return sizeof(LmSmem); }
+__device__ __forceinline__ uint64_t tc_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo)
+{
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);  // version 1, no swizzle
+}
+
+__device__ __forceinline__ bool tc_wait(uint32_t bar, uint32_t parity)
+{
+    for (long n = 0; n < TC_WAIT_LIMIT; n++) {
+        uint32_t ok;
+        asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                     : "=r"(ok)
+                     : "r"(bar), "r"(parity)
+                     : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void tc_expect(uint32_t bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+// 1-D bulk copy global -> this CTA's shared memory (no multicast), completion
+// counted on `bar`; addresses 16-byte aligned, size a multiple of 16
+__device__ __forceinline__ void tc_bulk(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_arrive(uint32_t bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Warp roles: warps 0-7 dequantize (thread = vocab row of the CTA), warp 8
+// (one lane) issues the bulk copies, warp 9 (one lane) issues the MMAs.  They
+// meet only at mbarriers:
+//   raw_full[r]  nibbles+scales of a block landed       (copy engine, tx count)
+//   raw_empty[r] the 8 dequant warps consumed a ring slot (8 arrivals)
+//   b_full[s]    activation tile of a block landed        (copy engine, tx count)
+//   a_full[s]    the 8 dequant warps wrote a block's A tile (8 arrivals)
+//   ab_empty[s]  the block's MMAs completed                (tcgen05.commit)
+// A wait for the u-th completion of a barrier uses parity u & 1; a wait for a
+// slot to be released before its first use uses parity 1, which a fresh
+// barrier reports as complete.
+__global__ void __launch_bounds__(TC_THREADS_ALL, 2) lmhead_tc_kernel(const __half *__restrict__ xt,
+                                                                      const uint8_t *__restrict__ nib,
+                                                                      const uint16_t *__restrict__ scales, int rows,
+                                                                      int vocab, int H, float *__restrict__ logits,
+                                                                      int *__restrict__ err)
+{
+    extern __shared__ __align__(1024) uint8_t tc_raw[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int v0 = blockIdx.x * TC_ROWS;
+    const int nch = H / TC_KC;
+    const int nrows = min(TC_ROWS, vocab - v0);  // a multiple of 8 (vocab is)
+    const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(tc_raw);
+    uint8_t *rawbase = tc_raw + TC_AS * TC_B_BYTES;
+    const uint32_t rawb = sbase + TC_AS * TC_B_BYTES;
+    const uint32_t bars = rawb + TC_RS * TC_RAW_STAGE;
+    auto raw_full = [&](int i) { return bars + 8 * i; };
+    auto raw_empty = [&](int i) { return bars + 8 * (TC_RS + i); };
+    auto b_full = [&](int i) { return bars + 8 * (2 * TC_RS + i); };
+    auto a_full = [&](int i) { return bars + 8 * (2 * TC_RS + TC_AS + i); };
+    auto ab_empty = [&](int i) { return bars + 8 * (2 * TC_RS + 2 * TC_AS + i); };
+    constexpr int NBARS = 2 * TC_RS + 3 * TC_AS;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(rawbase + TC_RS * TC_RAW_STAGE + 8 * NBARS);
+
+    if (warp == TC_MMA_WARP) {
+        const uint32_t slot = (uint32_t)__cvta_generic_to_shared(tmem_slot);
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "n"(TC_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        for (int i = 0; i < TC_RS; i++) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(raw_full(i)) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(raw_empty(i)), "r"(TC_DQ_WARPS) : "memory");
+        }
+        for (int i = 0; i < TC_AS; i++) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(b_full(i)) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(a_full(i)), "r"(TC_DQ_WARPS) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(ab_empty(i)) : "memory");
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    // rows past the vocabulary dequantize zero nibbles with zero scales (the
+    // copies cover rows < nrows only)
+    if (tid < TC_ROWS && tid >= nrows)
+        for (int rs = 0; rs < TC_RS; rs++) {
+#pragma unroll
+            for (int b = 0; b < TC_G; b++) {
+                *reinterpret_cast<uint4 *>(rawbase + rs * TC_RAW_STAGE + (tid * TC_G + b) * 16) = make_uint4(0, 0, 0, 0);
+                reinterpret_cast<uint16_t *>(rawbase + rs * TC_RAW_STAGE + TC_RAW_BYTES)[tid * TC_G + b] = 0;
+            }
+        }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+    bool failed = false;
+
+    if (warp == TC_LOAD_WARP) {
+        if (lane == 0) {
+            int nraw = 0, nb = 0;  // blocks whose copies were issued
+            auto issue_raw = [&](int c) {
+                const int r = c % TC_RS, u = c / TC_RS;
+                if (!tc_wait(raw_empty(r), (u + 1) & 1)) return false;
+                tc_expect(raw_full(r), nrows * 18 * TC_G);
+                tc_bulk(rawb + r * TC_RAW_STAGE, nib + ((int64_t)c * vocab + v0) * 16 * TC_G, nrows * 16 * TC_G,
+                        raw_full(r));
+                tc_bulk(rawb + r * TC_RAW_STAGE + TC_RAW_BYTES, scales + ((int64_t)c * vocab + v0) * TC_G, nrows * 2 * TC_G,
+                        raw_full(r));
+                nraw = c + 1;
+                return true;
+            };
+            for (int c = 0; c < TC_RS - 1 && c < nch && !failed; c++) failed = !issue_raw(c);
+            for (int c = 0; c < nch && !failed; c++) {
+                if (c + TC_RS - 1 < nch) failed = !issue_raw(c + TC_RS - 1);
+                if (failed) break;
+                const int st = c % TC_AS, u = c / TC_AS;
+                if (!tc_wait(ab_empty(st), (u + 1) & 1)) { failed = true; break; }
+                tc_expect(b_full(st), TC_B_BYTES);
+                tc_bulk(sbase + st * TC_B_BYTES, xt + (int64_t)c * (64 * TC_KC), TC_B_BYTES, b_full(st));
+                nb = c + 1;
+            }
+            // the last issued copies land before the CTA may leave (bounded)
+            for (int c = max(0, nraw - TC_RS); c < nraw; c++) tc_wait(raw_full(c % TC_RS), (c / TC_RS) & 1);
+            for (int c = max(0, nb - TC_AS); c < nb; c++) tc_wait(b_full(c % TC_AS), (c / TC_AS) & 1);
+        }
+    } else if (warp == TC_MMA_WARP) {
+        if (lane == 0) {
+            int nmma = 0;
+            for (int c = 0; c < nch && !failed; c++) {
+                const int st = c % TC_AS, u = c / TC_AS;
+                if (!tc_wait(a_full(st), u & 1) || !tc_wait(b_full(st), u & 1)) { failed = true; break; }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t bbase = sbase + st * TC_B_BYTES;
+#pragma unroll
+                for (int ks = 0; ks < TC_KC / 16; ks++) {
+                    const uint64_t bd = tc_desc(bbase + ks * 2 * 1024, 1024, 128);
+#pragma unroll
+                    for (int mt = 0; mt < 2; mt++) {
+                        const uint32_t at = tmem + TC_TMEM_A + (st * 2 + mt) * (TC_KC / 2) + ks * 8;
+                        const uint32_t acc = (c > 0 || ks > 0) ? 1u : 0u;
+                        asm volatile("{ .reg .pred p; setp.ne.b32 p, %4, 0; "
+                                     "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p; }" ::"r"(tmem + mt * 64),
+                                     "r"(at), "l"(bd), "r"(TC_IDESC), "r"(acc)
+                                     : "memory");
+                    }
+                }
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                 ab_empty(st))
+                             : "memory");
+                nmma = c + 1;
+            }
+            // the committed MMAs finish before TMEM is read or freed (bounded)
+            if (nmma > 0) tc_wait(ab_empty((nmma - 1) % TC_AS), ((nmma - 1) / TC_AS) & 1);
+        }
+    } else {
+        // dequant warps: row tid of every block, into TMEM lane (tid & 127) of A
+        // stage st, M-tile tid >> 7, once the stage's previous MMAs completed
+        const int mt = tid >> 7;
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + TC_TMEM_A + mt * (TC_KC / 2);
+        for (int c = 0; c < nch && !failed; c++) {
+            const int rs = c % TC_RS, st = c % TC_AS;
+            if (!tc_wait(raw_full(rs), (c / TC_RS) & 1) || !tc_wait(ab_empty(st), ((c / TC_AS) + 1) & 1)) {
+                failed = true;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint8_t *rp = rawbase + rs * TC_RAW_STAGE;
+            const uint4 w0 = *reinterpret_cast<const uint4 *>(rp + tid * 32);
+            const uint4 w1 = *reinterpret_cast<const uint4 *>(rp + tid * 32 + 16);
+            const __half2 sc = reinterpret_cast<const __half2 *>(rp + TC_RAW_BYTES)[tid];
+            __syncwarp();
+            if (lane == 0) tc_arrive(raw_empty(rs));  // this warp is done with the ring slot
+            const __half2 s0 = __low2half2(sc), s1 = __high2half2(sc);
+            uint32_t h[32];  // column 4j + i = k-positions (2i, 2i+1) of chunk j
+            dequant_word(w0.x, s0, h + 0);
+            dequant_word(w0.y, s0, h + 4);
+            dequant_word(w0.z, s0, h + 8);
+            dequant_word(w0.w, s0, h + 12);
+            dequant_word(w1.x, s1, h + 16);
+            dequant_word(w1.y, s1, h + 20);
+            dequant_word(w1.z, s1, h + 24);
+            dequant_word(w1.w, s1, h + 28);
+            asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+                         "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+                         ::"r"(lane_base + st * 2 * (TC_KC / 2)), "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3]), "r"(h[4]),
+                         "r"(h[5]), "r"(h[6]), "r"(h[7]), "r"(h[8]), "r"(h[9]), "r"(h[10]), "r"(h[11]), "r"(h[12]),
+                         "r"(h[13]), "r"(h[14]), "r"(h[15]), "r"(h[16]), "r"(h[17]), "r"(h[18]), "r"(h[19]), "r"(h[20]),
+                         "r"(h[21]), "r"(h[22]), "r"(h[23]), "r"(h[24]), "r"(h[25]), "r"(h[26]), "r"(h[27]), "r"(h[28]),
+                         "r"(h[29]), "r"(h[30]), "r"(h[31])
+                         : "memory");
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) tc_arrive(a_full(st));
+        }
+        // the last block's MMAs (and so all of them) completed: read the accumulators
+        if (!failed && !tc_wait(ab_empty((nch - 1) % TC_AS), ((nch - 1) / TC_AS) & 1)) failed = true;
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    const bool bad = __syncthreads_or(failed);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (bad) {
+        if (tid == 0) atomicExch(err, 1);
+    } else if (warp < TC_DQ_WARPS) {
+        // warp w reads TMEM lanes 32*(w%4).. of M-tile w/4: one vocab row, 64 batch columns
+        const int mt = warp >> 2, q = warp & 3;
+        uint32_t d[64];
+        const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + mt * 64;
+#pragma unroll
+        for (int h = 0; h < 4; h++) {
+            asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                         : "=r"(d[16 * h + 0]), "=r"(d[16 * h + 1]), "=r"(d[16 * h + 2]), "=r"(d[16 * h + 3]),
+                           "=r"(d[16 * h + 4]), "=r"(d[16 * h + 5]), "=r"(d[16 * h + 6]), "=r"(d[16 * h + 7]),
+                           "=r"(d[16 * h + 8]), "=r"(d[16 * h + 9]), "=r"(d[16 * h + 10]), "=r"(d[16 * h + 11]),
+                           "=r"(d[16 * h + 12]), "=r"(d[16 * h + 13]), "=r"(d[16 * h + 14]), "=r"(d[16 * h + 15])
+                         : "r"(taddr + 16 * h));
+        }
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        const int v = v0 + mt * 128 + 32 * q + lane;
+        if (v < vocab) {
+#pragma unroll
+            for (int b = 0; b < 64; b++)
+                if (b < rows) logits[(int64_t)b * vocab + v] = __uint_as_float(d[b]);
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (warp == TC_MMA_WARP)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(TC_TMEM_COLS) : "memory");
+}
 
 cudaError_t launch_q4_repack(const uint8_t *blocks, int vocab, int hidden, uint8_t *nib, uint16_t *scales,
                              cudaStream_t s)
 {
-    const int64_t nb = (int64_t)vocab * (hidden / 32);
-    q4_repack_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, s>>>(blocks, nb, nib, scales);
+    const int bpr = hidden / 32;
+    const int64_t nb = (int64_t)vocab * bpr;
+    q4_repack_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, s>>>(blocks, vocab, bpr, nib, scales);
     return cudaGetLastError();
 }
 
 cudaError_t launch_lmhead(const float *hidden, int rows, int H, const float *norm_w, float eps, const uint8_t *nib,
-                          const uint16_t *scales, int vocab, __half *xh, float *logits, cudaStream_t s)
+                          const uint16_t *scales, int vocab, __half *xh, float *logits, int *err, cudaStream_t s)
 {
     static bool attr = false;
     if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(lmhead_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)sizeof(LmSmem));
+        cudaError_t e = cudaFuncSetAttribute(lmhead_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_LAUNCH);
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    lmhead_prep_kernel<<<LM_M, 256, 0, s>>>(hidden, rows, H, norm_w, eps, xh);
+    lmhead_prep_tc_kernel<<<64, 256, 0, s>>>(hidden, rows, H, norm_w, eps, xh);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    lmhead_gemm_kernel<<<(unsigned)((vocab + LM_N - 1) / LM_N), LM_THREADS, sizeof(LmSmem), s>>>(xh, nib, scales, rows,
-                                                                                               vocab, H, logits);
+    lmhead_tc_kernel<<<(unsigned)((vocab + TC_ROWS - 1) / TC_ROWS), TC_THREADS_ALL, TC_SMEM_LAUNCH, s>>>(xh, nib, scales, rows,
+                                                                                              vocab, H, logits, err);
     return cudaGetLastError();
 }
 

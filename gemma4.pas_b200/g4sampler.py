@@ -57,6 +57,7 @@ SIGNATURES = {
                                   POINTER(Params), c_int32, c_float, c_void_p, c_void_p]),
     "g4s_sample_topk_noalloc": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_int64, POINTER(Params),
                                           c_float, c_void_p, c_void_p, c_void_p]),
+    "g4s_device_status": (c_int32, [c_void_p]),
     "g4s_q4_repack": (c_int32, [c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
     "g4s_lmhead_sample": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_float, c_void_p, c_void_p,
                                     c_int32, POINTER(Params), c_int32, c_float, c_void_p, c_void_p,

@@ -102,6 +102,9 @@ function g4s_sample_topk_noalloc(Logits: Pointer; DType, Rows, Vocab: Int32;
   RowStride: Int64; Params: PG4SParams; Softcap: Single; U: PDouble;
   OutTokens: PInt32; Stream: Pointer): Int32; cdecl; external G4SLib;
 
+{ G4S_ERR_TIMEOUT when a kernel gave up a bounded wait since the last check. }
+function g4s_device_status(Ctx: PG4SCtx): Int32; cdecl; external G4SLib;
+
 { LM head (CpuMatVecQ4, src/Gemma4.Tensors.pas:546-590) + DoSample: TQ4Block
   weights repacked once on the device, then one call per step. }
 function g4s_q4_repack(Blocks: Pointer; Vocab, Hidden: Int32; Nibbles: Pointer;

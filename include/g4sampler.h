@@ -195,20 +195,27 @@ int32_t g4s_sample_topk_noalloc(const void *logits, int32_t dtype, int32_t rows,
  * src/Gemma4.Tensors.pas:546-590, then DoSample).  Weights are the reference's
  * Q4_0 blocks (TQ4Block, src/Gemma4.Types.pas:139-142: fp16 scale + 16 bytes,
  * byte j = element 2j in the low nibble, 2j+1 in the high nibble, value =
- * nibble - 8), repacked once on the device by g4s_q4_repack into
- *   nibbles [vocab][hidden/2]   the 16 nibble bytes of each block
- *   scales  [vocab][hidden/32]  the fp16 scale bits
+ * nibble - 8), repacked once on the device by g4s_q4_repack into pairs of
+ * hidden blocks (blocks 2g and 2g+1 of a row are adjacent):
+ *   nibbles [hidden/64][vocab][2][16]  the 16 nibble bytes of each block
+ *   scales  [hidden/64][vocab][2]      the fp16 scale bits
+ * (vocab * hidden / 2 and vocab * hidden / 32 * 2 bytes, 16-byte aligned).
  * g4s_lmhead_sample computes logits[r][v] = sum_k hidden[r][k] * w[v][k] for
  * rows <= 64 (hidden fp32 on the device, rounded to fp16; w = (nibble - 8) *
- * scale rounded once to fp16; fp16 tensor-core products, fp32 accumulation),
- * then samples them exactly as g4s_sample_ex.  hidden must be a multiple of
- * 128, vocab of 8.  norm_weight (device, hidden fp32; NULL = the hidden
- * states are already normalized) applies the model's final RMSNorm first,
- * CpuRmsNorm (src/Gemma4.Layers.pas:142-175) with eps norm_eps (1e-6 in the
- * reference, src/Gemma4.Types.pas:48), fused into the activation prologue.  out_logits (device, rows x vocab fp32) receives the logits
- * when non-NULL; otherwise they stay in a context buffer allocated by the
- * first call.
+ * scale rounded once to fp16; products on the tcgen05 tensor cores with fp32
+ * accumulation), then samples them exactly as g4s_sample_ex.  hidden must be
+ * a multiple of 128, vocab of 8.  norm_weight (device, hidden fp32; NULL = the
+ * hidden states are already normalized) applies the model's final RMSNorm
+ * first, CpuRmsNorm (src/Gemma4.Layers.pas:142-175) with eps norm_eps (1e-6 in
+ * the reference, src/Gemma4.Types.pas:48), fused into the activation
+ * prologue.  out_logits (device, rows x vocab fp32) receives the logits when
+ * non-NULL; otherwise they stay in a context buffer allocated by the first
+ * call.
  */
+/* Waits for the device, then reports whether a kernel of this context gave up
+   a bounded wait (G4S_ERR_TIMEOUT; the flag is cleared) since the last check. */
+int32_t g4s_device_status(g4s_ctx *ctx);
+
 int32_t g4s_q4_repack(const uint8_t *blocks, int32_t vocab, int32_t hidden, uint8_t *nibbles, uint16_t *scales,
                       void *stream);
 

@@ -41,6 +41,7 @@ def _run(g4, torch, s, h, blocks, vocab, hidden, prm, u):
     s.lmhead_sample(hd.data_ptr(), rows, hidden, nib.data_ptr(), sc.data_ptr(), vocab, prm, CAP, ud.data_ptr(),
                     out.data_ptr(), logits_ptr=logits.data_ptr())
     torch.cuda.synchronize()
+    assert s.lib.g4s_device_status(s.h) == g4.OK, s.last_error()  # no bounded wait ran out
     return out.cpu().numpy(), logits.cpu().numpy()
 
 
@@ -109,6 +110,7 @@ def test_lmhead_with_fused_final_norm(g4, torch_cuda, oracle):
         s.lmhead_sample(hd.data_ptr(), rows, hidden, nib.data_ptr(), sc.data_ptr(), vocab, prm, CAP, ud.data_ptr(),
                         out.data_ptr(), logits_ptr=logits.data_ptr(), norm_ptr=gd.data_ptr(), norm_eps=1e-6)
         torch.cuda.synchronize()
+        assert s.lib.g4s_device_status(s.h) == g4.OK, s.last_error()
     finally:
         s.close()
     lg, tok = logits.cpu().numpy(), out.cpu().numpy()
