@@ -36,14 +36,24 @@ __global__ void q4_repack_kernel(const uint8_t *__restrict__ blocks, int vocab, 
     *reinterpret_cast<uint4 *>(nib + dst * 16) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// One word of 8 nibbles -> 4 half2 (n_i, n_{i+4}) * scale, each (nibble - 8) * scale rounded once.
+// One word of 8 nibbles (n_j at bits 4j) -> 4 half2 (n_i, n_{i+4}) * scale for
+// i = 0..3, each (nibble - 8) * scale rounded once to fp16.  The even pairs are
+// masked in place as (1024 + n) and the odd ones as (1024 + 16 n) (both exact
+// in fp16); n - 8 is then exact as (1024 + n) - 1032 or (1024 + 16 n) / 16 - 72
+// (one fused multiply-add with the power of two 1/16), and the product with
+// the scale is the single rounding.
 __device__ __forceinline__ void dequant_word(uint32_t w, __half2 sc, uint32_t *h)
 {
     const __half2 bias = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));  // 1032
+    const __half2 sixteenth = __halves2half2(__ushort_as_half(0x2C00), __ushort_as_half(0x2C00));  // 1/16
+    const __half2 m72 = __halves2half2(__ushort_as_half(0xD480), __ushort_as_half(0xD480));  // -72
+    const uint32_t w8 = w >> 8;
+    uint32_t v[4] = {(w & 0x000F000Fu) | 0x64006400u, (w & 0x00F000F0u) | 0x64006400u,
+                     (w8 & 0x000F000Fu) | 0x64006400u, (w8 & 0x00F000F0u) | 0x64006400u};
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        const uint32_t v = ((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u;  // (1024 + n_i, 1024 + n_{i+4})
-        __half2 q = __hsub2(*reinterpret_cast<const __half2 *>(&v), bias);
+        const __half2 x = *reinterpret_cast<const __half2 *>(&v[i]);
+        __half2 q = (i & 1) ? __hfma2(x, sixteenth, m72) : __hsub2(x, bias);
         q = __hmul2(q, sc);
         h[i] = *reinterpret_cast<uint32_t *>(&q);
     }
@@ -52,64 +62,72 @@ __device__ __forceinline__ void dequant_word(uint32_t w, __half2 sc, uint32_t *h
 // ---------------------------------------------------------------------------
 // lmhead_tc_kernel
 //
-// D[v][b] = sum_k W[v][k] x[b][k]: A = dequantized weights (M = 128 vocab rows
-// per MMA, two M-tiles per CTA), B = fp16 activations (N = 64 batch rows),
-// K = 16 per tcgen05.mma, fp32 accumulators in TMEM (128 lanes x 64 columns per
-// M-tile).  One hidden block (32) per iteration:
-//   - the block's nibbles and scales for the CTA's 256 rows (4 KiB + 512 B,
-//     contiguous) arrive by 1-D bulk copies (TMA engine, no multicast) four
-//     iterations ahead (ring of 4), counted on mbarriers;
-//   - each thread dequantizes its row's block into the A tile, laid out in the
-//     canonical K-major, unswizzled core-matrix form (8 rows x 16 bytes), and
-//     fences the writes to the tensor core's proxy (fence.proxy.async);
-//   - one thread issues 4 MMAs (2 k-steps x 2 M-tiles) and commits them to the
-//     stage's mbarrier;
-//   - the next block's activation tile (4 KiB, L2-resident) is a bulk copy
-//     into the other stage once that stage's previous MMAs completed.
-// The only generic-proxy writes to operand memory are each thread's own
-// dequantized rows, so the proxy fence does not wait on any copy in flight.
-// Dequantization, copies and MMAs run in separate warps that meet only at
-// mbarriers (no block barrier inside the loop); three A/B stages and a ring of
-// four nibble stages.  Every mbarrier wait is bounded: on a timeout the
-// kernel sets the error flag, drains (bounded) and frees its TMEM.  The
-// epilogue reads TMEM with tcgen05.ld (warp w: lanes 32*(w%4).., M-tile w/4)
-// and stores the logits.
+// D[v][b] = sum_k W[v][k] x[b][k] on the 5th-generation tensor cores: A = the
+// dequantized weights (M = 128 vocab rows per MMA, two M-tiles per CTA), B =
+// fp16 activations (N = 64 batch rows), K = 16 per tcgen05.mma, fp32
+// accumulators in TMEM (128 lanes x 64 columns per M-tile).  A CTA owns 256
+// vocab rows; one pipeline stage covers 64 hidden elements (two Q4 blocks):
+//   - the stage's nibbles and scales for the CTA's rows (8 KiB + 1 KiB, each
+//     contiguous in the grouped layout) arrive by 1-D bulk copies (TMA engine,
+//     no multicast) into a ring of TC_RS slots;
+//   - the stage's activation tile (8 KiB, L2-resident, already in the
+//     canonical K-major core-matrix layout) arrives into a ring of TC_BS slots;
+//   - each dequant thread turns its row's 64 nibbles into fp16 and writes them
+//     to TMEM with one tcgen05.st (the A operand is read from TMEM by the MMA:
+//     no shared-memory round trip for the weights);
+//   - warp TC_MMA_WARP + mt issues M-tile mt's 4 MMAs and commits them.
+// Roles run in separate warps that meet only at mbarriers (no block barrier
+// inside the loop); two CTAs per SM split its 512 TMEM columns (256 each: two
+// A stages), so one CTA's pipeline fill and epilogue overlap the other's main
+// loop, and four MMA issuers per SM keep the tensor core fed at N = 64.  Every
+// mbarrier wait is bounded: on a timeout the kernel sets the error flag,
+// drains (bounded) and frees its TMEM.  The epilogue reads TMEM with
+// tcgen05.ld (warp w: lanes 32*(w%4).., M-tile w/4) and stores the logits.
 //
 // Inside each 8-element K-chunk the k order is permuted: position p holds
-// element (p >> 1) + 4 * (p & 1) of the chunk -- the order in which a shift and
-// a LOP3 pull half2 pairs (n_i, n_{i+4}) out of one 32-bit word of nibbles;
-// lmhead_prep_tc_kernel lays the activations out in the same order.
+// element (p >> 1) + 4 * (p & 1) of the chunk -- the order in which the masks
+// of dequant_word pull half2 pairs (n_i, n_{i+4}) out of one 32-bit word of
+// nibbles; lmhead_prep_tc_kernel lays the activations out in the same order.
 // ---------------------------------------------------------------------------
 constexpr int TC_ROWS = 256;                    // vocab rows per CTA (2 M-tiles of 128)
 constexpr int TC_KC = 64;                       // hidden elements per stage (Q4_GROUP blocks)
 constexpr int TC_G = TC_KC / 32;
 static_assert(TC_G == Q4_GROUP, "a stage is one group of the device layout");
-constexpr int TC_THREADS = 256;                // dequant threads (one per vocab row of the CTA)
-constexpr int TC_DQ_WARPS = TC_THREADS / 32;
-constexpr int TC_LOAD_WARP = TC_DQ_WARPS;       // bulk-copy issuer
-constexpr int TC_MMA_WARP = TC_DQ_WARPS + 1;    // tcgen05.mma issuer, TMEM owner
-constexpr int TC_THREADS_ALL = TC_THREADS + 64;
+constexpr int TC_CPS = 2;                       // CTAs per SM (they share its 512 TMEM columns)
+constexpr int TC_DQ_WARPS = TC_ROWS / 32;       // one dequant thread per vocab row of the CTA
+constexpr int TC_LOAD_WARP = TC_DQ_WARPS;       // bulk copies of nibbles and scales
+constexpr int TC_BLOAD_WARP = TC_DQ_WARPS + 1;  // bulk copies of activation tiles
+constexpr int TC_MMA_WARP = TC_DQ_WARPS + 2;    // tcgen05.mma issuers (M-tile 0, then 1); TMEM owner
+constexpr int TC_THREADS_ALL = TC_DQ_WARPS * 32 + 128;
 #ifndef G4S_TC_RS
-#define G4S_TC_RS 4
+#define G4S_TC_RS 6
 #endif
 constexpr int TC_RS = G4S_TC_RS;                // nibble staging ring depth
-#ifndef G4S_TC_AS
-#define G4S_TC_AS 2
+#ifndef G4S_TC_BS
+#define G4S_TC_BS 6
 #endif
-constexpr int TC_AS = G4S_TC_AS;                // A/B tile stages (MMA groups in flight)
+constexpr int TC_BS = G4S_TC_BS;                // activation tile ring depth
+constexpr int TC_TMEM_COLS = 512 / TC_CPS;
+constexpr int TC_TMEM_A = 128;
+constexpr int TC_AS = (TC_TMEM_COLS - TC_TMEM_A) / 64;  // A stages in TMEM (both M-tiles)
 constexpr int TC_B_BYTES = 64 * TC_KC * 2;      // 8 KB:  [j 0..7][g 0..7][8 rows][16 B]
 constexpr int TC_RAW_BYTES = TC_ROWS * 16 * TC_G;  // 8 KB of nibbles per stage
 constexpr int TC_SC_BYTES = TC_ROWS * 2 * TC_G;    // 1 KB of scales per stage
 constexpr int TC_RAW_STAGE = TC_RAW_BYTES + TC_SC_BYTES;
-constexpr int TC_SMEM = TC_AS * TC_B_BYTES + TC_RS * TC_RAW_STAGE + 8 * (2 * TC_RS + 3 * TC_AS) + 16;  // + mbarriers, TMEM address
+constexpr int TC_NBARS = 2 * TC_RS + 2 * TC_BS + 4 * TC_AS;
+constexpr int TC_SMEM = TC_BS * TC_B_BYTES + TC_RS * TC_RAW_STAGE + 8 * TC_NBARS + 16;  // + mbarriers, TMEM address
 // TMEM columns: accumulators [mt][64 batch columns] at 0..127, dequantized A
 // operands at 128 + (stage * 2 + mt) * 32 (32 columns = 64 fp16 k-values per lane)
-constexpr int TC_TMEM_COLS = 256;
-constexpr int TC_TMEM_A = 128;
 static_assert(TC_TMEM_A + TC_AS * 2 * (TC_KC / 2) <= TC_TMEM_COLS, "A stages exceed the TMEM allocation");
-// Two CTAs of 256 TMEM columns fill an SM's 512; the launch asks for enough
-// shared memory that a third cannot become resident and wait in tcgen05.alloc.
-constexpr int TC_SMEM_LAUNCH = TC_SMEM > 80 * 1024 ? TC_SMEM : 80 * 1024;
+// The parity waits rely on these depths: a ring slot's previous use was
+// consumed before the slot is refilled, and a stage's A slot is rewritten only
+// after the MMAs of stage c - TC_AS, which follow the previous stage's.
+static_assert(TC_RS > TC_AS && TC_BS > TC_AS, "pipeline depths");
+// TC_CPS CTAs share the SM's 512 TMEM columns; the launch asks for enough
+// shared memory that one more cannot become resident and wait in tcgen05.alloc.
+constexpr int TC_SMEM_MIN = (228 * 1024) / (TC_CPS + 1) - 1023;
+constexpr int TC_SMEM_LAUNCH = TC_SMEM > TC_SMEM_MIN ? TC_SMEM : TC_SMEM_MIN;
+static_assert(TC_CPS * (TC_SMEM_LAUNCH + 1024) <= 228 * 1024, "TC_CPS CTAs per SM");
 constexpr uint32_t TC_IDESC = (1u << 4) | ((64u >> 3) << 17) | ((128u >> 4) << 24);  // f16 x f16 -> f32, M128 N64, K-major
 constexpr long TC_WAIT_LIMIT = 1L << 20;
 
@@ -190,18 +208,24 @@ __device__ __forceinline__ void tc_arrive(uint32_t bar)
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-// Warp roles: warps 0-7 dequantize (thread = vocab row of the CTA), warp 8
-// (one lane) issues the bulk copies, warp 9 (one lane) issues the MMAs.  They
-// meet only at mbarriers:
-//   raw_full[r]  nibbles+scales of a block landed       (copy engine, tx count)
-//   raw_empty[r] the 8 dequant warps consumed a ring slot (8 arrivals)
-//   b_full[s]    activation tile of a block landed        (copy engine, tx count)
-//   a_full[s]    the 8 dequant warps wrote a block's A tile (8 arrivals)
-//   ab_empty[s]  the block's MMAs completed                (tcgen05.commit)
+// Warp roles: warps 0..7 dequantize (a thread = a vocab row of the CTA; warps
+// 0-3 M-tile 0, warps 4-7 M-tile 1), the next two warps (one lane each) issue
+// the bulk copies of the weights and of the activation tiles, so that neither
+// waits behind the other, the last two (one lane each) issue the MMAs of
+// M-tile 0 and 1: two issuers keep the tensor core busy at N = 64, where one
+// alone reaches about 60% of its rate.  The roles meet only at mbarriers:
+//   raw_full[r]     nibbles+scales of a stage landed            (copy engine, tx count)
+//   raw_empty[r]    the 8 dequant warps consumed a ring slot  (8 arrivals)
+//   b_full[b]       activation tile of a stage landed           (copy engine, tx count)
+//   b_empty[b]      both M-tiles' MMAs reading it completed     (2 tcgen05.commit)
+//   a_full[mt][a]   stage ready for M-tile mt: its 4 dequant warps wrote the A
+//                   tile, and the activation loader saw the B tile land
+//                   (5 arrivals, so the MMA warp polls one barrier per stage)
+//   ab_empty[mt][a] M-tile mt's MMAs of the stage in A slot a completed (tcgen05.commit)
 // A wait for the u-th completion of a barrier uses parity u & 1; a wait for a
 // slot to be released before its first use uses parity 1, which a fresh
 // barrier reports as complete.
-__global__ void __launch_bounds__(TC_THREADS_ALL, 2) lmhead_tc_kernel(const __half *__restrict__ xt,
+__global__ void __launch_bounds__(TC_THREADS_ALL, TC_CPS) lmhead_tc_kernel(const __half *__restrict__ xt,
                                                                       const uint8_t *__restrict__ nib,
                                                                       const uint16_t *__restrict__ scales, int rows,
                                                                       int vocab, int H, float *__restrict__ logits,
@@ -213,16 +237,16 @@ __global__ void __launch_bounds__(TC_THREADS_ALL, 2) lmhead_tc_kernel(const __ha
     const int nch = H / TC_KC;
     const int nrows = min(TC_ROWS, vocab - v0);  // a multiple of 8 (vocab is)
     const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(tc_raw);
-    uint8_t *rawbase = tc_raw + TC_AS * TC_B_BYTES;
-    const uint32_t rawb = sbase + TC_AS * TC_B_BYTES;
+    uint8_t *rawbase = tc_raw + TC_BS * TC_B_BYTES;
+    const uint32_t rawb = sbase + TC_BS * TC_B_BYTES;
     const uint32_t bars = rawb + TC_RS * TC_RAW_STAGE;
     auto raw_full = [&](int i) { return bars + 8 * i; };
     auto raw_empty = [&](int i) { return bars + 8 * (TC_RS + i); };
     auto b_full = [&](int i) { return bars + 8 * (2 * TC_RS + i); };
-    auto a_full = [&](int i) { return bars + 8 * (2 * TC_RS + TC_AS + i); };
-    auto ab_empty = [&](int i) { return bars + 8 * (2 * TC_RS + 2 * TC_AS + i); };
-    constexpr int NBARS = 2 * TC_RS + 3 * TC_AS;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(rawbase + TC_RS * TC_RAW_STAGE + 8 * NBARS);
+    auto b_empty = [&](int i) { return bars + 8 * (2 * TC_RS + TC_BS + i); };
+    auto a_full = [&](int mt, int i) { return bars + 8 * (2 * TC_RS + 2 * TC_BS + mt * TC_AS + i); };
+    auto ab_empty = [&](int mt, int i) { return bars + 8 * (2 * TC_RS + 2 * TC_BS + 2 * TC_AS + mt * TC_AS + i); };
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(rawbase + TC_RS * TC_RAW_STAGE + 8 * TC_NBARS);
 
     if (warp == TC_MMA_WARP) {
         const uint32_t slot = (uint32_t)__cvta_generic_to_shared(tmem_slot);
@@ -235,11 +259,16 @@ __global__ void __launch_bounds__(TC_THREADS_ALL, 2) lmhead_tc_kernel(const __ha
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(raw_full(i)) : "memory");
             asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(raw_empty(i)), "r"(TC_DQ_WARPS) : "memory");
         }
-        for (int i = 0; i < TC_AS; i++) {
+        for (int i = 0; i < TC_BS; i++) {
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(b_full(i)) : "memory");
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(a_full(i)), "r"(TC_DQ_WARPS) : "memory");
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(ab_empty(i)) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 2;" ::"r"(b_empty(i)) : "memory");
         }
+        for (int i = 0; i < TC_AS; i++)
+            for (int mt = 0; mt < 2; mt++) {
+                asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(a_full(mt, i)), "r"(TC_DQ_WARPS / 2 + 1)
+                             : "memory");
+                asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(ab_empty(mt, i)) : "memory");
+            }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
@@ -261,77 +290,105 @@ __global__ void __launch_bounds__(TC_THREADS_ALL, 2) lmhead_tc_kernel(const __ha
 
     if (warp == TC_LOAD_WARP) {
         if (lane == 0) {
-            int nraw = 0, nb = 0;  // blocks whose copies were issued
-            auto issue_raw = [&](int c) {
+            int nraw = 0;  // stages whose copies were issued
+            for (int c = 0; c < nch; c++) {
                 const int r = c % TC_RS, u = c / TC_RS;
-                if (!tc_wait(raw_empty(r), (u + 1) & 1)) return false;
+                if (!tc_wait(raw_empty(r), (u + 1) & 1)) {
+                    failed = true;
+                    break;
+                }
                 tc_expect(raw_full(r), nrows * 18 * TC_G);
                 tc_bulk(rawb + r * TC_RAW_STAGE, nib + ((int64_t)c * vocab + v0) * 16 * TC_G, nrows * 16 * TC_G,
                         raw_full(r));
                 tc_bulk(rawb + r * TC_RAW_STAGE + TC_RAW_BYTES, scales + ((int64_t)c * vocab + v0) * TC_G, nrows * 2 * TC_G,
                         raw_full(r));
                 nraw = c + 1;
-                return true;
-            };
-            for (int c = 0; c < TC_RS - 1 && c < nch && !failed; c++) failed = !issue_raw(c);
-            for (int c = 0; c < nch && !failed; c++) {
-                if (c + TC_RS - 1 < nch) failed = !issue_raw(c + TC_RS - 1);
-                if (failed) break;
-                const int st = c % TC_AS, u = c / TC_AS;
-                if (!tc_wait(ab_empty(st), (u + 1) & 1)) { failed = true; break; }
-                tc_expect(b_full(st), TC_B_BYTES);
-                tc_bulk(sbase + st * TC_B_BYTES, xt + (int64_t)c * (64 * TC_KC), TC_B_BYTES, b_full(st));
-                nb = c + 1;
             }
             // the last issued copies land before the CTA may leave (bounded)
             for (int c = max(0, nraw - TC_RS); c < nraw; c++) tc_wait(raw_full(c % TC_RS), (c / TC_RS) & 1);
-            for (int c = max(0, nb - TC_AS); c < nb; c++) tc_wait(b_full(c % TC_AS), (c / TC_AS) & 1);
         }
-    } else if (warp == TC_MMA_WARP) {
+    } else if (warp == TC_BLOAD_WARP) {
         if (lane == 0) {
+            // stage c's tile is announced on a_full once it landed and the MMAs of
+            // stage c - TC_AS (the previous users of the A slot, whose a_full phase
+            // must be over) completed; right after, the copy for stage
+            // c + TC_BS - TC_AS goes out, whose slot those same MMAs released
+            constexpr int LEAD = TC_BS - TC_AS;
+            int nb = 0;  // stages whose copy was issued
+            auto issue_b = [&](int c) {
+                const int b = c % TC_BS;
+                if (!tc_wait(b_empty(b), ((c / TC_BS) + 1) & 1)) return false;
+                tc_expect(b_full(b), TC_B_BYTES);
+                tc_bulk(sbase + b * TC_B_BYTES, xt + (int64_t)c * (64 * TC_KC), TC_B_BYTES, b_full(b));
+                nb = c + 1;
+                return true;
+            };
+            for (int c = 0; c < LEAD && c < nch && !failed; c++) failed = !issue_b(c);
+            for (int c = 0; c < nch && !failed; c++) {
+                const int a = c % TC_AS, par = ((c / TC_AS) + 1) & 1;
+                if (!tc_wait(b_full(c % TC_BS), (c / TC_BS) & 1) || !tc_wait(ab_empty(0, a), par) ||
+                    !tc_wait(ab_empty(1, a), par)) {
+                    failed = true;
+                    break;
+                }
+                tc_arrive(a_full(0, a));
+                tc_arrive(a_full(1, a));
+                if (c + LEAD < nch) failed = !issue_b(c + LEAD);
+            }
+            for (int c = max(0, nb - TC_BS); c < nb; c++) tc_wait(b_full(c % TC_BS), (c / TC_BS) & 1);
+        }
+    } else if (warp >= TC_MMA_WARP) {
+        if (lane == 0) {
+            // M-tile mt: D = TMEM columns [64 mt, 64 mt + 64), A of stage st at
+            // 128 + (2 st + mt) * 32, k-step ks 8 columns further
+            const int mt = warp - TC_MMA_WARP;
             int nmma = 0;
             for (int c = 0; c < nch && !failed; c++) {
                 const int st = c % TC_AS, u = c / TC_AS;
-                if (!tc_wait(a_full(st), u & 1) || !tc_wait(b_full(st), u & 1)) { failed = true; break; }
+                if (!tc_wait(a_full(mt, st), u & 1)) {
+                    failed = true;
+                    break;
+                }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t bbase = sbase + st * TC_B_BYTES;
+                const uint32_t bbase = sbase + (c % TC_BS) * TC_B_BYTES;
+                const uint32_t at = tmem + TC_TMEM_A + (st * 2 + mt) * (TC_KC / 2);
 #pragma unroll
                 for (int ks = 0; ks < TC_KC / 16; ks++) {
                     const uint64_t bd = tc_desc(bbase + ks * 2 * 1024, 1024, 128);
-#pragma unroll
-                    for (int mt = 0; mt < 2; mt++) {
-                        const uint32_t at = tmem + TC_TMEM_A + (st * 2 + mt) * (TC_KC / 2) + ks * 8;
-                        const uint32_t acc = (c > 0 || ks > 0) ? 1u : 0u;
-                        asm volatile("{ .reg .pred p; setp.ne.b32 p, %4, 0; "
-                                     "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p; }" ::"r"(tmem + mt * 64),
-                                     "r"(at), "l"(bd), "r"(TC_IDESC), "r"(acc)
-                                     : "memory");
-                    }
+                    const uint32_t acc = (c > 0 || ks > 0) ? 1u : 0u;
+                    asm volatile("{ .reg .pred p; setp.ne.b32 p, %4, 0; "
+                                 "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p; }" ::"r"(tmem + mt * 64),
+                                 "r"(at + ks * 8), "l"(bd), "r"(TC_IDESC), "r"(acc)
+                                 : "memory");
                 }
                 asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                                 ab_empty(st))
+                                 ab_empty(mt, st))
+                             : "memory");
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                 b_empty(c % TC_BS))
                              : "memory");
                 nmma = c + 1;
             }
             // the committed MMAs finish before TMEM is read or freed (bounded)
-            if (nmma > 0) tc_wait(ab_empty((nmma - 1) % TC_AS), ((nmma - 1) / TC_AS) & 1);
+            if (nmma > 0) tc_wait(ab_empty(mt, (nmma - 1) % TC_AS), ((nmma - 1) / TC_AS) & 1);
         }
     } else {
-        // dequant warps: row tid of every block, into TMEM lane (tid & 127) of A
-        // stage st, M-tile tid >> 7, once the stage's previous MMAs completed
-        const int mt = tid >> 7;
+        // dequant warps: thread row = vocab row of the CTA, into TMEM lane
+        // (row & 127) of A stage st, M-tile row >> 7, once that M-tile's MMAs of
+        // stage c - TC_AS completed
+        const int row = tid, mt = row >> 7;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + TC_TMEM_A + mt * (TC_KC / 2);
         for (int c = 0; c < nch && !failed; c++) {
             const int rs = c % TC_RS, st = c % TC_AS;
-            if (!tc_wait(raw_full(rs), (c / TC_RS) & 1) || !tc_wait(ab_empty(st), ((c / TC_AS) + 1) & 1)) {
+            if (!tc_wait(raw_full(rs), (c / TC_RS) & 1) || !tc_wait(ab_empty(mt, st), ((c / TC_AS) + 1) & 1)) {
                 failed = true;
                 break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint8_t *rp = rawbase + rs * TC_RAW_STAGE;
-            const uint4 w0 = *reinterpret_cast<const uint4 *>(rp + tid * 32);
-            const uint4 w1 = *reinterpret_cast<const uint4 *>(rp + tid * 32 + 16);
-            const __half2 sc = reinterpret_cast<const __half2 *>(rp + TC_RAW_BYTES)[tid];
+            const uint4 w0 = *reinterpret_cast<const uint4 *>(rp + row * 32);
+            const uint4 w1 = *reinterpret_cast<const uint4 *>(rp + row * 32 + 16);
+            const __half2 sc = reinterpret_cast<const __half2 *>(rp + TC_RAW_BYTES)[row];
             __syncwarp();
             if (lane == 0) tc_arrive(raw_empty(rs));  // this warp is done with the ring slot
             const __half2 s0 = __low2half2(sc), s1 = __high2half2(sc);
@@ -355,10 +412,10 @@ __global__ void __launch_bounds__(TC_THREADS_ALL, 2) lmhead_tc_kernel(const __ha
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
-            if (lane == 0) tc_arrive(a_full(st));
+            if (lane == 0) tc_arrive(a_full(mt, st));
         }
-        // the last block's MMAs (and so all of them) completed: read the accumulators
-        if (!failed && !tc_wait(ab_empty((nch - 1) % TC_AS), ((nch - 1) / TC_AS) & 1)) failed = true;
+        // this M-tile's last MMAs (and so all of them) completed: read the accumulators
+        if (!failed && !tc_wait(ab_empty(mt, (nch - 1) % TC_AS), ((nch - 1) / TC_AS) & 1)) failed = true;
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     const bool bad = __syncthreads_or(failed);
