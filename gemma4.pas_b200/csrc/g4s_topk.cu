@@ -92,77 +92,103 @@ __device__ uint64_t radix_kth(ForEach for_each, int K, TopkSmem &sm)
     return prefix;
 }
 
-// The tail of the top-K path on kw survivors (sm.tv = raw logits, sm.ids =
-// vocab ids, ascending ids).  Runs on warp 0 only.
-__device__ void topk_tail(const SampleArgs &a, int row, const g4s_params &p, int kw,
-                          TopkSmem &sm)
+// The tail of the top-K path on the kw winners, sorted by ascending vocab id
+// (sm.L: (~id) << 32 | key, descending), on all NTHREADS threads: thread i
+// < kw takes winner i through softcap, temperature and Exp in registers; the
+// serial parts (the fp32 sum and the cumulative draw in index order, which the
+// reference computes serially) run on thread 0 between block barriers.
+__device__ void topk_tail(const SampleArgs &a, int row, const g4s_params &p, int kw, TopkSmem &sm)
 {
-    const int lane = threadIdx.x & 31;
+    static_assert(KMAX <= NTHREADS, "one winner per thread");
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     // the draw is needed only at the end; its load is issued first
-    const double u_row = (lane == 0 && p.temperature > 0.0f && kw > 0) ? a.u[row] : 0.0;
-    int32_t flags = p.temperature > 0.0f ? 0 : G4S_ROW_GREEDY;
-    int32_t token = -1;
-    float tprob = 0.0f;
-    if (kw == 0) {
-        flags |= G4S_ROW_EMPTY;
-    } else {
-        const float cap = a.softcap;
-        const bool use_t = p.temperature > 0.0f && p.temperature != 1.0f;
-        const float invT = use_t ? __fdiv_rn(1.0f, p.temperature) : 1.0f;
+    const double u_row = (tid == 0 && p.temperature > 0.0f && kw > 0) ? a.u[row] : 0.0;
+    const bool has = tid < kw;
+    int32_t id = -1;
+    float v = 0.0f;
+    if (has) {
+        const uint64_t e = sm.L[tid];
+        id = (int32_t)(~(uint32_t)(e >> 32));
+        v = key2f((uint32_t)e);
         // softcap cap * tanh(v / cap) and temperature (src/Gemma4.Model.pas:2768-2785)
-        for (int i = lane; i < kw; i += 32) {
-            float v = sm.tv[i];
-            if (cap > 0.0f) v = __fmul_rn(cap, g4_tanhf(__fdiv_rn(v, cap)));
-            if (use_t) v = __fmul_rn(v, invT);
-            sm.tv[i] = v;
-        }
-        __syncwarp();
-        // LMax := LVals[0]; strictly-greater scan (NaN at position 0 sticks)
-        float mx = -__uint_as_float(0x7f800000u);
-        for (int i = lane; i < kw; i += 32) mx = fmaxf(mx, sm.tv[i]);
+        const float cap = a.softcap;
+        if (cap > 0.0f) v = __fmul_rn(cap, g4_tanhf(__fdiv_rn(v, cap)));
+        if (p.temperature > 0.0f && p.temperature != 1.0f) v = __fmul_rn(v, __fdiv_rn(1.0f, p.temperature));
+    }
+    // LMax := LVals[0]; strictly-greater scan: the largest non-NaN value, unless
+    // LVals[0] is NaN, which sticks
+    float mx = has ? v : -__uint_as_float(0x7f800000u);
 #pragma unroll
-        for (int d = 16; d > 0; d >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULLMASK, mx, d));
-        const float v0 = sm.tv[0];
-        if (v0 != v0) mx = v0;
-        for (int i = lane; i < kw; i += 32) sm.tv[i] = g4_expf(__fsub_rn(sm.tv[i], mx));
-        __syncwarp();
-        // serial fp32 sum in ascending-id order (src/Gemma4.Model.pas:2794-2799)
-        if (lane == 0) {
-            // four values per shared-memory load; only the fp32 adds are serial
-            float s = 0.0f;
-            int i = 0;
+    for (int d = 16; d > 0; d >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULLMASK, mx, d));
+    if (lane == 0) sm.wthr[warp] = __float_as_uint(mx);
+    if (tid == 0) sm.fmisc[1] = v;
+    __syncthreads();
+    mx = __uint_as_float(sm.wthr[0]);
+#pragma unroll
+    for (int w = 1; w < NWARPS; w++) mx = fmaxf(mx, __uint_as_float(sm.wthr[w]));
+    const float v0 = sm.fmisc[1];
+    if (kw > 0 && v0 != v0) mx = v0;
+    const float e = has ? g4_expf(__fsub_rn(v, mx)) : 0.0f;
+    if (has) {
+        sm.tv[tid] = e;
+        sm.ids[tid] = id;
+    }
+    __syncthreads();
+    // serial fp32 sum in ascending-id order (src/Gemma4.Model.pas:2794-2799)
+    if (tid == 0) {
+        // four values per shared-memory load; only the fp32 adds are serial
+        float s = 0.0f;
+        int i = 0;
 #pragma unroll 4
-            for (; i + 4 <= kw; i += 4) {
-                const float4 q = *reinterpret_cast<const float4 *>(&sm.tv[i]);
-                s = __fadd_rn(s, q.x);
-                s = __fadd_rn(s, q.y);
-                s = __fadd_rn(s, q.z);
-                s = __fadd_rn(s, q.w);
-            }
-            for (; i < kw; i++) s = __fadd_rn(s, sm.tv[i]);
-            sm.fmisc[0] = s;
+        for (; i + 4 <= kw; i += 4) {
+            const float4 q = *reinterpret_cast<const float4 *>(&sm.tv[i]);
+            s = __fadd_rn(s, q.x);
+            s = __fadd_rn(s, q.y);
+            s = __fadd_rn(s, q.z);
+            s = __fadd_rn(s, q.w);
         }
-        __syncwarp();
-        const float sum = sm.fmisc[0];
-        for (int i = lane; i < kw; i += 32) sm.tv[i] = __fdiv_rn(sm.tv[i], sum);
-        __syncwarp();
-        // argmax, first maximum wins (src/Gemma4.Model.pas:2803-2807)
-        float bv = -1.0f;
-        int bi = 0x7fffffff;
-        for (int i = lane; i < kw; i += 32) {
-            float q = sm.tv[i];
-            if (q > bv) { bv = q; bi = i; }
-        }
+        for (; i < kw; i++) s = __fadd_rn(s, sm.tv[i]);
+        sm.fmisc[0] = s;
+    }
+    __syncthreads();
+    const float prob = has ? __fdiv_rn(e, sm.fmisc[0]) : 0.0f;
+    if (has) sm.tv[tid] = prob;
+    // argmax, first maximum wins (src/Gemma4.Model.pas:2803-2807): per warp here,
+    // across warps on thread 0
+    float bv = (has && prob > -1.0f) ? prob : -1.0f;
+    int bi = (has && prob > -1.0f) ? tid : 0x7fffffff;
 #pragma unroll
-        for (int d = 16; d > 0; d >>= 1) {
-            float ov = __shfl_xor_sync(FULLMASK, bv, d);
-            int oi = __shfl_xor_sync(FULLMASK, bi, d);
-            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    for (int d = 16; d > 0; d >>= 1) {
+        const float ov = __shfl_xor_sync(FULLMASK, bv, d);
+        const int oi = __shfl_xor_sync(FULLMASK, bi, d);
+        if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
         }
-        int best = (sm.tv[0] != sm.tv[0] || bi == 0x7fffffff) ? 0 : bi;
-        // index-order cumulative draw against fl32(Random * TopP) (src/Gemma4.Model.pas:2809-2824)
-        if (p.temperature > 0.0f) {
-            if (lane == 0) {
+    }
+    if (lane == 0) {
+        sm.wthr[warp] = __float_as_uint(bv);
+        sm.scan[warp] = bi;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int32_t flags = p.temperature > 0.0f ? 0 : G4S_ROW_GREEDY;
+        int32_t token = -1;
+        float tprob = 0.0f;
+        if (kw == 0) {
+            flags |= G4S_ROW_EMPTY;
+        } else {
+            for (int w = 1; w < NWARPS; w++) {
+                const float ov = __uint_as_float(sm.wthr[w]);
+                const int oi = sm.scan[w];
+                if (ov > bv || (ov == bv && oi < bi)) {
+                    bv = ov;
+                    bi = oi;
+                }
+            }
+            int best = (sm.tv[0] != sm.tv[0] || bi == 0x7fffffff) ? 0 : bi;
+            // index-order cumulative draw against fl32(Random * TopP) (src/Gemma4.Model.pas:2809-2824)
+            if (p.temperature > 0.0f) {
                 const float thr = __double2float_rn(u_row * (double)p.top_p);
                 float cum = 0.0f;
                 int found = -1;
@@ -182,23 +208,18 @@ __device__ void topk_tail(const SampleArgs &a, int row, const g4s_params &p, int
                     cum = __fadd_rn(cum, sm.tv[i]);
                     if (cum >= thr) found = i;
                 }
-                sm.misc[3] = found;
+                if (found >= 0) best = found;
+                else flags |= G4S_ROW_FALLBACK;
             }
-            __syncwarp();
-            const int found = sm.misc[3];
-            if (found >= 0) best = found;
-            else flags |= G4S_ROW_FALLBACK;
+            token = sm.ids[best];
+            tprob = sm.tv[best];
         }
-        token = sm.ids[best];
-        tprob = sm.tv[best];
-    }
-    if (lane == 0) {
         a.out_tokens[row] = token;
         if (a.token_prob) a.token_prob[row] = tprob;
         if (a.row_flags) a.row_flags[row] = flags;
     }
     if (a.cand_ids || a.cand_probs) {
-        for (int i = lane; i < a.cand_stride; i += 32) {
+        for (int i = tid; i < a.cand_stride; i += NTHREADS) {
             if (a.cand_ids) a.cand_ids[(int64_t)row * a.cand_stride + i] = i < kw ? sm.ids[i] : -1;
             if (a.cand_probs) a.cand_probs[(int64_t)row * a.cand_stride + i] = i < kw ? sm.tv[i] : 0.0f;
         }
@@ -211,25 +232,29 @@ __device__ void topk_tail(const SampleArgs &a, int row, const g4s_params &p, int
 __device__ __forceinline__ void sort_list_desc(TopkSmem &sm, int n)
 {
     if (n <= NTHREADS) {
+        // tpe threads (adjacent lanes) per key split the count of the keys above
+        // it: up to 8 when the list is short
+        int tpe = 1;
+        while (tpe < 8 && tpe * 2 * n <= NTHREADS) tpe *= 2;
         uint64_t *out = sm.L + CAP2 / 2;
-        const int t = threadIdx.x;
-        if (t < n) {
-            const uint64_t v = sm.L[t];
-            // two keys per 16-byte load, four independent counts: the loads of
-            // consecutive iterations overlap instead of chaining
-            int r0 = 0, r1 = 0, r2 = 0, r3 = 0, q = 0;
-            const ulonglong2 *L2 = reinterpret_cast<const ulonglong2 *>(sm.L);
+        const int t = threadIdx.x, i = t / tpe, part = t & (tpe - 1);
+        const uint64_t v = i < n ? sm.L[i] : 0;
+        // two keys per 16-byte load, two independent counts
+        int r0 = 0, r1 = 0;
+        const ulonglong2 *L2 = reinterpret_cast<const ulonglong2 *>(sm.L);
+        if (i < n) {
+            const int np = n >> 1;
 #pragma unroll 4
-            for (; q + 4 <= n; q += 4) {
-                const ulonglong2 x = L2[q >> 1], y = L2[(q >> 1) + 1];
+            for (int q = part; q < np; q += tpe) {
+                const ulonglong2 x = L2[q];
                 r0 += x.x > v;
                 r1 += x.y > v;
-                r2 += y.x > v;
-                r3 += y.y > v;
             }
-            for (; q < n; q++) r0 += sm.L[q] > v;
-            out[r0 + r1 + r2 + r3] = v;
+            if ((n & 1) && part == 0) r0 += sm.L[n - 1] > v;
         }
+        int r = r0 + r1;
+        for (int d = 1; d < tpe; d <<= 1) r += __shfl_xor_sync(FULLMASK, r, d);
+        if (i < n && part == 0) out[r] = v;
         __syncthreads();
         if (t < n) sm.L[t] = out[t];
         __syncthreads();
@@ -264,7 +289,7 @@ __device__ __forceinline__ int prefix_at_least(const uint64_t *list, int cnt, ui
 }
 
 // The kw winners in sm.L[0..kw) (descending composites) re-sorted by ascending
-// vocab id into sm.ids / sm.tv, then the tail on warp 0.
+// vocab id, then the tail.
 __device__ __forceinline__ void finish_row(const SampleArgs &a, int row, const g4s_params &p, int kw, TopkSmem &sm)
 {
     static_assert(KMAX <= NTHREADS, "one winner per thread");
@@ -275,13 +300,7 @@ __device__ __forceinline__ void finish_row(const SampleArgs &a, int row, const g
     if (tid < kw) sm.L[tid] = ((uint64_t)comp_id(mine) ^ 0xffffffffull) << 32 | comp_key(mine);
     __syncthreads();
     sort_list_desc(sm, kw);
-    for (int i = tid; i < kw; i += NTHREADS) {
-        const uint64_t v = sm.L[i];
-        sm.ids[i] = (int32_t)(~(uint32_t)(v >> 32));
-        sm.tv[i] = key2f((uint32_t)v);
-    }
-    __syncthreads();
-    if (tid < 32) topk_tail(a, row, p, kw, sm);
+    topk_tail(a, row, p, kw, sm);
 }
 
 // Merge of nch descending candidate lists (list c: C + c * lstride, length
@@ -551,12 +570,16 @@ template <int DT, bool VEC>
 __global__ void __launch_bounds__(NTHREADS, 1) topk_cluster_kernel(SampleArgs a)
 {
     namespace cg = cooperative_groups;
-    static_assert(TOPK_CLUSTER * TOPK_CLUSTER_KMAX <= CAP2 / 2, "the gathered lists fit half of sm.L");
-    static_assert(TOPK_CLUSTER * TOPK_CLUSTER_KMAX % NTHREADS == 0, "whole gather slots per thread");
+    static_assert(TOPK_CLUSTER * TOPK_CLUSTER_KMAX <= CAP2 / 2, "the pushed lists fit half of sm.L");
     cg::cluster_group cluster = cg::this_cluster();
+    // launched as a programmatic dependent: the launch overlaps the previous
+    // kernel of the stream, and every read of this call's inputs comes after the
+    // wait; the next call may launch as soon as this one is running
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     __shared__ TopkSmem sm;
-    __shared__ int s_cnt;
-    __shared__ int rc[TOPK_CLUSTER];
+    __shared__ int s_cnt, s_push;
+    __shared__ int rc[1];
     __shared__ uint64_t rk[1];
     const int rank = (int)cluster.block_rank();
     const int row = blockIdx.x / TOPK_CLUSTER, tid = threadIdx.x;
@@ -567,61 +590,42 @@ __global__ void __launch_bounds__(NTHREADS, 1) topk_cluster_kernel(SampleArgs a)
     if (!(K > 0 && K < a.vocab && K <= TOPK_CLUSTER_KMAX)) return;
     const int64_t c0 = (int64_t)rank * CSLICE;
     const int n = (int)max((int64_t)0, min((int64_t)CSLICE, (int64_t)a.vocab - c0));
+    if (tid == 0) s_push = 0;  // CTA 0's counter of pushed entries
     const int m = chunk_select<DT, CEPT, VEC>(a, row, c0, n, K, sm);
     if (tid == 0) s_cnt = m;
     cluster.sync();  // every CTA's list is in its shared memory
 
-    // CTA 0: the gathered lists in sm.L[c * KS + i] (KS = TOPK_CLUSTER_KMAX; its
-    // own list is list 0 and is rewritten in place with its own values), the
-    // entries kept for the final sort in W
-    constexpr int KS = TOPK_CLUSTER_KMAX, SPT = TOPK_CLUSTER * KS / NTHREADS;
-    uint64_t *G = sm.L;
-    uint64_t *W = sm.L + CAP2 / 2;
-    int n2 = 0;
-    if (rank == 0) {
-        if (tid < TOPK_CLUSTER) rc[tid] = *cluster.map_shared_rank(&s_cnt, tid);
-        __syncthreads();
-        {
-            uint64_t v[SPT];
-#pragma unroll
-            for (int q = 0; q < SPT; q++) {
-                const int f = tid + q * NTHREADS, c = f / KS, i = f % KS;
-                v[q] = i < rc[c] ? cluster.map_shared_rank(sm.L, c)[i] : 0;
-            }
-            __syncthreads();
-#pragma unroll
-            for (int q = 0; q < SPT; q++) G[tid + q * NTHREADS] = v[q];
+    // lower bound on the row's K-th largest, the same in every CTA: with j0 =
+    // ceil(K / lists), each list holds j0 entries at or above its j0-th, so the
+    // smallest j0-th entry has at least K entries at or above it (no bound, T =
+    // 1, when a list is shorter than j0)
+    const int j0 = (K + TOPK_CLUSTER - 1) / TOPK_CLUSTER;
+    if (tid < 32) {
+        uint64_t h = ~0ull;
+        if (tid < TOPK_CLUSTER) {
+            const int c = *cluster.map_shared_rank(&s_cnt, tid);
+            h = c >= j0 ? cluster.map_shared_rank(sm.L, tid)[j0 - 1] : 0;
         }
-        // lower bound on the row's K-th largest: with j0 = ceil(K / lists), each
-        // list holds j0 entries at or above its j0-th, so the smallest j0-th
-        // entry has at least K entries at or above it (no bound, T = 1, when a
-        // list is shorter than j0)
-        const int j0 = (K + TOPK_CLUSTER - 1) / TOPK_CLUSTER;
-        if (tid < 32) {
-            uint64_t h = ~0ull;
-            if (tid < TOPK_CLUSTER) h = rc[tid] >= j0 ? cluster.map_shared_rank(sm.L, tid)[j0 - 1] : 0;
 #pragma unroll
-            for (int d = 16; d > 0; d >>= 1) {
-                const uint64_t o = __shfl_xor_sync(FULLMASK, h, d);
-                h = o < h ? o : h;
-            }
-            if (tid == 0) rk[0] = h ? h : 1;
+        for (int d = 16; d > 0; d >>= 1) {
+            const uint64_t o = __shfl_xor_sync(FULLMASK, h, d);
+            h = o < h ? o : h;
         }
-        __syncthreads();
-        const uint64_t T = rk[0];
-        int cnt = 0;
-#pragma unroll
-        for (int q = 0; q < SPT; q++) cnt += G[tid + q * NTHREADS] >= T;
-        int off = block_excl_scan(cnt, &n2, sm.scan);
-#pragma unroll
-        for (int q = 0; q < SPT; q++) {
-            const uint64_t e = G[tid + q * NTHREADS];
-            if (e >= T) W[off++] = e;
-        }
+        if (tid == 0) rk[0] = h ? h : 1;
     }
-    cluster.sync();  // CTA 0 is done reading the other CTAs' shared memory
+    __syncthreads();
+    const uint64_t T = rk[0];
+    // each CTA pushes its entries >= T (a prefix of its sorted list) into CTA
+    // 0's W, at an offset reserved with one atomic on CTA 0's counter
+    const bool keep = tid < m && sm.L[tid] >= T;
+    const int c_keep = __syncthreads_count(keep);
+    if (tid == 0) rc[0] = c_keep ? atomicAdd(cluster.map_shared_rank(&s_push, 0), c_keep) : 0;
+    __syncthreads();
+    if (keep) cluster.map_shared_rank(sm.L + CAP2 / 2, 0)[rc[0] + tid] = sm.L[tid];
+    cluster.sync();  // every push has landed in CTA 0
     if (rank != 0) return;
-    for (int i = tid; i < n2; i += NTHREADS) sm.L[i] = W[i];
+    const int n2 = s_push;
+    for (int i = tid; i < n2; i += NTHREADS) sm.L[i] = sm.L[CAP2 / 2 + i];
     __syncthreads();
     sort_list_desc(sm, n2);
     finish_row(a, row, p, n2 < K ? n2 : K, sm);
@@ -645,13 +649,15 @@ static cudaError_t launch_cluster_t(const SampleArgs &a, cudaStream_t s)
     cfg.gridDim = dim3((unsigned)(a.rows * TOPK_CLUSTER));
     cfg.blockDim = dim3(NTHREADS);
     cfg.stream = s;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = TOPK_CLUSTER;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, topk_cluster_kernel<DT, VEC>, a);
 }
 
