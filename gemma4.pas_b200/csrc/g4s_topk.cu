@@ -566,11 +566,15 @@ __global__ void __launch_bounds__(NTHREADS) topk_chunk_kernel(SampleArgs a)
 constexpr int CEPT = 64;
 constexpr int CSLICE = CEPT * NTHREADS;  // 16384 ids per CTA
 
+constexpr int CLUSTER_PUSH_CAP = TOPK_CLUSTER * TOPK_CLUSTER_KMAX;  // CTA 0's slots for pushed entries
+constexpr int CLUSTER_DYN_SMEM = CLUSTER_PUSH_CAP * 8;
+
 template <int DT, bool VEC>
 __global__ void __launch_bounds__(NTHREADS, 1) topk_cluster_kernel(SampleArgs a)
 {
     namespace cg = cooperative_groups;
-    static_assert(TOPK_CLUSTER * TOPK_CLUSTER_KMAX <= CAP2 / 2, "the pushed lists fit half of sm.L");
+    constexpr int PUSH_CAP = CLUSTER_PUSH_CAP;
+    static_assert(PUSH_CAP <= CAP2, "the pushed entries fit sm.L");
     cg::cluster_group cluster = cg::this_cluster();
     // launched as a programmatic dependent: the launch overlaps the previous
     // kernel of the stream, and every read of this call's inputs comes after the
@@ -578,11 +582,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) topk_cluster_kernel(SampleArgs a)
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     __shared__ TopkSmem sm;
-    __shared__ int s_cnt, s_push;
-    __shared__ int rc[1];
-    __shared__ uint64_t rk[1];
+    extern __shared__ __align__(16) uint64_t s_w[];  // CTA 0: entries pushed by the cluster (PUSH_CAP, dynamic)
+    __shared__ uint32_t s_top[NWARPS * 8], s_bound, s_thr;
+    __shared__ int s_push, s_off;
+    using T = DtypeTraits<DT>;
+    constexpr int VW = T::VW;
     const int rank = (int)cluster.block_rank();
-    const int row = blockIdx.x / TOPK_CLUSTER, tid = threadIdx.x;
+    const int row = blockIdx.x / TOPK_CLUSTER, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const g4s_params p = a.params.get(row);
     const int K = p.top_k;
     // the host sends rows with top_k <= TOPK_CLUSTER_KMAX here; others return
@@ -590,42 +596,100 @@ __global__ void __launch_bounds__(NTHREADS, 1) topk_cluster_kernel(SampleArgs a)
     if (!(K > 0 && K < a.vocab && K <= TOPK_CLUSTER_KMAX)) return;
     const int64_t c0 = (int64_t)rank * CSLICE;
     const int n = (int)max((int64_t)0, min((int64_t)CSLICE, (int64_t)a.vocab - c0));
-    if (tid == 0) s_push = 0;  // CTA 0's counter of pushed entries
-    const int m = chunk_select<DT, CEPT, VEC>(a, row, c0, n, K, sm);
-    if (tid == 0) s_cnt = m;
-    cluster.sync();  // every CTA's list is in its shared memory
+    const void *rowp = (const char *)a.logits + (int64_t)row * a.row_stride * T::ESIZE;
+    if (tid == 0) s_push = 0;
 
-    // lower bound on the row's K-th largest, the same in every CTA: with j0 =
-    // ceil(K / lists), each list holds j0 entries at or above its j0-th, so the
-    // smallest j0-th entry has at least K entries at or above it (no bound, T =
-    // 1, when a list is shorter than j0)
+    // this CTA's slice: keys in registers, lane maxima sorted per warp
+    float x[CEPT];
+    load_chunk<DT, CEPT, VEC>(rowp, c0, n, x);
+    uint32_t key[CEPT];
+    uint32_t tmax = 0;
+#pragma unroll
+    for (int i = 0; i < CEPT; i++) {
+        key[i] = cand_key(x[i]);
+        tmax = key[i] > tmax ? key[i] : tmax;
+    }
+    const uint32_t srt = warp_sort_desc_u32(tmax);  // lane l: the warp's (l+1)-th largest lane maximum
+    // local bound: every warp has kp lanes with maxima >= its kp-th, so the CTA
+    // holds at least K keys >= the smallest of them; keys below it are not in
+    // the row's top K
+    const int kp = (K + NWARPS - 1) / NWARPS;
     const int j0 = (K + TOPK_CLUSTER - 1) / TOPK_CLUSTER;
-    if (tid < 32) {
-        uint64_t h = ~0ull;
-        if (tid < TOPK_CLUSTER) {
-            const int c = *cluster.map_shared_rank(&s_cnt, tid);
-            h = c >= j0 ? cluster.map_shared_rank(sm.L, tid)[j0 - 1] : 0;
+    const uint32_t wthr = __shfl_sync(FULLMASK, srt, kp - 1);
+    if (lane == 0) sm.wthr[warp] = wthr;
+    if (lane < j0) s_top[warp * j0 + lane] = srt;
+    __syncthreads();
+    uint32_t tloc = sm.wthr[0];
+#pragma unroll
+    for (int w = 1; w < NWARPS; w++) tloc = sm.wthr[w] < tloc ? sm.wthr[w] : tloc;
+    // the CTA's j0-th largest lane maximum (from the warps' top j0): the CTA
+    // holds j0 keys at or above it
+    if (tid < NWARPS * j0) {
+        const uint32_t v = s_top[tid];
+        int gt = 0, ge = 0;
+        for (int i = 0; i < NWARPS * j0; i++) {
+            const uint32_t o = s_top[i];
+            gt += o > v;
+            ge += o >= v;
         }
+        if (gt < j0 && j0 <= ge) s_bound = v;
+    }
+    cluster.sync();  // every CTA's bound is published
+
+    // the row's bound, the same in every CTA: the cluster holds TOPK_CLUSTER *
+    // j0 >= K keys at or above the smallest CTA bound (1: no bound)
+    if (tid < 32) {
+        uint32_t h = 0xffffffffu;
+        if (tid < TOPK_CLUSTER) h = *cluster.map_shared_rank(&s_bound, tid);
 #pragma unroll
         for (int d = 16; d > 0; d >>= 1) {
-            const uint64_t o = __shfl_xor_sync(FULLMASK, h, d);
+            const uint32_t o = __shfl_xor_sync(FULLMASK, h, d);
             h = o < h ? o : h;
         }
-        if (tid == 0) rk[0] = h ? h : 1;
+        if (tid == 0) s_thr = h;
     }
     __syncthreads();
-    const uint64_t T = rk[0];
-    // each CTA pushes its entries >= T (a prefix of its sorted list) into CTA
-    // 0's W, at an offset reserved with one atomic on CTA 0's counter
-    const bool keep = tid < m && sm.L[tid] >= T;
-    const int c_keep = __syncthreads_count(keep);
-    if (tid == 0) rc[0] = c_keep ? atomicAdd(cluster.map_shared_rank(&s_push, 0), c_keep) : 0;
+    uint32_t thr = s_thr > tloc ? s_thr : tloc;
+    if (thr == 0) thr = 1;
+    int mine = 0;
+#pragma unroll
+    for (int i = 0; i < CEPT; i++) mine += key[i] >= thr;
+    // the CTA's count decides between the push and the exact fallback
+    const int inc = warp_incl_scan(mine);
+    if (lane == 31) sm.scan[warp] = inc;
     __syncthreads();
-    if (keep) cluster.map_shared_rank(sm.L + CAP2 / 2, 0)[rc[0] + tid] = sm.L[tid];
+    int sum = 0;
+#pragma unroll
+    for (int w = 0; w < NWARPS; w++) sum += sm.scan[w];
+    uint64_t *W0 = cluster.map_shared_rank(s_w, 0);
+    int *P0 = cluster.map_shared_rank(&s_push, 0);
+    if (sum <= TOPK_CLUSTER_KMAX) {
+        // push: one atomic per warp on CTA 0's counter, then the entries
+        int base = 0;
+        if (lane == 31 && inc > 0) base = atomicAdd(P0, inc);
+        int o = __shfl_sync(FULLMASK, base, 31) + inc - mine;
+#pragma unroll
+        for (int i = 0; i < CEPT; i++) {
+            if (key[i] >= thr) {
+                const uint32_t id = (uint32_t)(a.id_offset + c0 + (i / VW) * (NTHREADS * VW) + tid * VW + (i % VW));
+                W0[o++] = composite(key[i], id);
+            }
+        }
+    } else {
+        // heavy ties: this CTA's exact top K (at most TOPK_CLUSTER_KMAX), the
+        // prefix at or above the row's bound pushed
+        const int m = chunk_select_radix<DT, CEPT>(rowp, c0, n, K, a.id_offset, sm);
+        const uint64_t tb = (uint64_t)thr << 32;
+        const bool keep = tid < m && sm.L[tid] >= tb;
+        const int ck = __syncthreads_count(keep);
+        if (tid == 0) s_off = ck ? atomicAdd(P0, ck) : 0;
+        __syncthreads();
+        if (keep) W0[s_off + tid] = sm.L[tid];
+    }
     cluster.sync();  // every push has landed in CTA 0
     if (rank != 0) return;
     const int n2 = s_push;
-    for (int i = tid; i < n2; i += NTHREADS) sm.L[i] = sm.L[CAP2 / 2 + i];
+    for (int i = tid; i < n2; i += NTHREADS) sm.L[i] = s_w[i];
     __syncthreads();
     sort_list_desc(sm, n2);
     finish_row(a, row, p, n2 < K ? n2 : K, sm);
@@ -648,6 +712,7 @@ static cudaError_t launch_cluster_t(const SampleArgs &a, cudaStream_t s)
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(a.rows * TOPK_CLUSTER));
     cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = CLUSTER_DYN_SMEM;
     cfg.stream = s;
     cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
@@ -677,11 +742,14 @@ template <int DT, bool VEC>
 static bool cluster_ok_t()
 {
     if (cudaFuncSetAttribute(topk_cluster_kernel<DT, VEC>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
-        cudaSuccess)
+            cudaSuccess ||
+        cudaFuncSetAttribute(topk_cluster_kernel<DT, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             CLUSTER_DYN_SMEM) != cudaSuccess)
         return false;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(TOPK_CLUSTER);
     cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = CLUSTER_DYN_SMEM;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = TOPK_CLUSTER;

@@ -164,12 +164,14 @@ def test_argument_errors(sampler, torch_cuda, g4):
     torch.cuda.synchronize()
 
 
-def test_single_row_cluster_merge_paths(sampler, torch_cuda, oracle, g4):
-    # Rows of a small batch take the one-cluster-per-row kernel (16 slices of
-    # 16384 ids).  Row 0 interleaves the slices' top entries so that more than
-    # half of all list entries lie at or above the merge bound (the heavy-tie
-    # merge through the workspace); row 1 keeps them apart (the direct merge).
-    V, K = 262144, 200
+@pytest.mark.parametrize("K", [128, 200])
+def test_single_row_cluster_merge_paths(sampler, torch_cuda, oracle, g4, K):
+    # Rows of a small batch with top_k <= 128 take the one-cluster-per-row
+    # kernel (16 slices of 16384 ids); K = 200 takes the chunked grid.  Row 0
+    # interleaves the slices' top entries, so every slice holds many entries at
+    # or above the row's bound (the largest pushes, or the exact per-slice
+    # fallback); row 1 keeps them apart (few pushes from most slices).
+    V = 262144
     x = np.full((2, V), -1e30, dtype=np.float32)
     for c in range(16):
         i = np.arange(K)
