@@ -318,8 +318,9 @@ def run_c4(dev, peak, steps=20):
     return {"us_per_step": us, "rows_per_s": rows / (us * 1e-6), "weight_gbs": wbytes / (us * 1e-6) / 1e9,
             "hbm_frac_of_peak": wbytes / (us * 1e-6) / 1e9 / peak,
             "tflops": 2.0 * rows * VOCAB * H / (us * 1e-6) / 1e12,
-            "config": "C4: hidden 64 x 2560 fp32 -> LM head 262144 x 2560 Q4_0 (fp16 tensor-core GEMM, fp32 "
-                      "accumulate) -> top_k 64, T=1, top_p 0.95; median of 5 replays of a 20-call CUDA graph"}
+            "config": "C4: hidden 64 x 2560 fp32 -> LM head 262144 x 2560 Q4_0 (tcgen05 fp16 MMA, dequantized "
+                      "weights in TMEM, fp32 accumulate) -> top_k 64, T=1, top_p 0.95; median of 5 replays of a "
+                      "20-call CUDA graph"}
 
 
 def run_c5_sharded(s_unused, rank, world, local, dev, peak, steps=200):

@@ -1,6 +1,7 @@
 """LM head + sampling (config C4) through the C ABI: Q4_0 weights in the
 reference block format (TQ4Block, src/Gemma4.Types.pas:139-142), repacked on
-the device, logits by the fp16 tensor-core GEMM, then the sampler.
+the device, logits by the tcgen05 fp16 GEMM (dequantized weights in TMEM), then
+the sampler.
 
 Logits are checked against the fp64 matvec of the same quantized weights
 (restating CpuMatVecQ4, src/Gemma4.Tensors.pas:546-590, in exact arithmetic)
