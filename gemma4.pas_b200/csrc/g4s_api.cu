@@ -18,6 +18,9 @@
 namespace g4s {
 constexpr int KMAX_ = 256;
 constexpr int NCH_MAX_ = 1024;
+constexpr int STREAM_TILE_ = 2048;       // ids per tile of the streaming top-K pass
+constexpr int STREAM_MIN_CHUNK_ = 8192;  // shortest chunk given to it (four tiles)
+constexpr int STREAM_MIN_ROWS_ = 64;     // fewer rows: the chunk kernel's shorter chunks win (B = 32 measured)
 constexpr int LK_SLOTS = 16;
 constexpr int PSLOTS = 4;  // per-row params staging slots
 }  // namespace g4s
@@ -59,7 +62,7 @@ struct g4s_ctx {
     // LM head workspace (first g4s_lmhead_sample call): fp32 logits and fp16 hidden
     float *lm_logits = nullptr;
     void *lm_xh = nullptr;
-    int *dev_err = nullptr;  // device error flag (a bounded wait that ran out), read by g4s_device_status
+    int *dev_err = nullptr;  // device error flag in the workspace (a bounded wait that ran out), read by g4s_device_status
     size_t lm_logits_n = 0, lm_xh_n = 0;
     // g4s_sample_host staging
     void *h_logits = nullptr;
@@ -114,6 +117,27 @@ static int choose_ept(const g4s_ctx *ctx, int rows, int vocab)
     const int64_t big = ceil_div(vocab, 8192);
     if ((int64_t)rows * big < 2LL * ctx->sm_count && ceil_div(vocab, 2048) <= NCH_MAX_) return 8;
     return 32;
+}
+
+// Top-K chunking of a call: the streaming pass (long chunks, a running
+// threshold, bulk copies: 16-byte aligned rows) for batches of 64 rows or more
+// where big chunks would be chosen, split so that the grid fills the resident
+// CTA slots once; the chunks of choose_ept otherwise.
+struct TopkChunks {
+    int chunk, nch;
+    bool stream;
+};
+static TopkChunks choose_topk_chunks(const g4s_ctx *ctx, int rows, int vocab, bool vec)
+{
+    const int ept = choose_ept(ctx, rows, vocab);
+    if (ept == 32 && vec && vocab >= STREAM_MIN_CHUNK_ && rows >= STREAM_MIN_ROWS_) {
+        const int64_t slots = (int64_t)topk_stream_blocks_per_sm() * ctx->sm_count;
+        const int64_t splits = std::max<int64_t>(1, slots / rows);
+        int64_t chunk = ceil_div(ceil_div(vocab, splits), STREAM_TILE_) * STREAM_TILE_;
+        if (chunk < STREAM_MIN_CHUNK_) chunk = STREAM_MIN_CHUNK_;
+        return {(int)chunk, (int)ceil_div(vocab, chunk), true};
+    }
+    return {ept * 256, (int)ceil_div(vocab, ept * 256), false};
 }
 
 // NCCL, loaded on first use of the sharded API (the rest of the library does
@@ -337,6 +361,7 @@ int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t
     const size_t o_li = off; off = align(off + (size_t)LK_SLOTS * max_vocab * sizeof(int32_t));
     const size_t o_lv = off; off = align(off + (size_t)LK_SLOTS * max_vocab * sizeof(float));
     const size_t o_pd = off; off = align(off + (size_t)PSLOTS * max_rows * (sizeof(g4s_params) + sizeof(float)));
+    const size_t o_err = off; off = align(off + sizeof(int));
     ctx->ws_bytes = off;
     if (cudaMalloc(&ctx->ws, off) != cudaSuccess) {
         cudaGetLastError();
@@ -352,6 +377,7 @@ int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t
     ctx->lk_idx = (int32_t *)(base + o_li);
     ctx->lk_val = (float *)(base + o_lv);
     ctx->params_dev = (g4s_params *)(base + o_pd);
+    ctx->dev_err = (int *)(base + o_err);
     if (cudaMemset(ctx->ws, 0, off) != cudaSuccess ||
         cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaHostAlloc((void **)&ctx->params_pinned, (size_t)PSLOTS * max_rows * (sizeof(g4s_params) + sizeof(float)),
@@ -389,7 +415,6 @@ int32_t g4s_destroy(g4s_ctx *ctx)
     shard_release(ctx);
     if (ctx->lm_logits) cudaFree(ctx->lm_logits);
     if (ctx->lm_xh) cudaFree(ctx->lm_xh);
-    if (ctx->dev_err) cudaFree(ctx->dev_err);
     delete ctx;
     return G4S_OK;
 }
@@ -436,8 +461,9 @@ int32_t g4s_sample_ex(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t r
     const int esize = dtype == G4S_F32 ? 4 : 2;
     const bool vec = ((uintptr_t)logits % 16u == 0) && (((int64_t)row_stride * esize) % 16 == 0);
     const int ept = choose_ept(ctx, rows, vocab);
-    const int chunk = ept * 256;
-    const int nch = (int)ceil_div(vocab, chunk);
+    const TopkChunks tc = choose_topk_chunks(ctx, rows, vocab, vec);
+    const int chunk = tc.chunk;
+    const int nch = tc.nch;
     if (nch > NCH_MAX_ || (int64_t)rows * nch > ctx->lists_cap)
         return fail(ctx, G4S_ERR_CAPACITY, "g4s_sample: %d rows x %d chunks exceed the workspace", rows, nch);
 
@@ -469,6 +495,7 @@ int32_t g4s_sample_ex(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t r
     a.cand = ctx->cand;
     a.cand_cnt = ctx->cand_cnt;
     a.counters_topk = ctx->counters_topk;
+    a.err = ctx->dev_err;
     a.istat = ctx->istat;
     if (any_full) {
         int &bps = ctx->persist[dtype][vec ? 1 : 0];
@@ -487,7 +514,8 @@ int32_t g4s_sample_ex(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t r
     // a few rows: one thread-block cluster per row (latency); else the chunked grid
     const bool use_cluster = ctx->cluster_ok && rows <= TOPK_CLUSTER_MAX_ROWS && vocab <= TOPK_CLUSTER_MAX_VOCAB &&
                              max_k_small <= TOPK_CLUSTER_KMAX;
-    if (any_topk && e == cudaSuccess) e = use_cluster ? launch_topk_cluster(a, vec, s) : launch_topk(a, ept, vec, s);
+    if (any_topk && e == cudaSuccess)
+        e = use_cluster ? launch_topk_cluster(a, vec, s) : tc.stream ? launch_topk_stream(a, s) : launch_topk(a, ept, vec, s);
     if (any_full && e == cudaSuccess) e = launch_full(a, ept, vec, s);
     if (any_full && ex.full_probs && e == cudaSuccess) e = launch_full_probs(a, ept, vec, s);
     if (any_large && e == cudaSuccess) e = launch_largek(a, s);
@@ -593,12 +621,6 @@ int32_t g4s_lmhead_sample(g4s_ctx *ctx, const float *hidden, int32_t rows, int32
         ctx->lm_xh_n = need_x;
     }
     if (!logits) logits = ctx->lm_logits;
-    if (!ctx->dev_err) {
-        if (cudaMalloc(&ctx->dev_err, sizeof(int)) != cudaSuccess || cudaMemset(ctx->dev_err, 0, sizeof(int)) != cudaSuccess) {
-            cudaGetLastError();
-            return fail(ctx, G4S_ERR_NOMEM, "%s: cannot allocate the error flag", who);
-        }
-    }
     const cudaError_t e = launch_lmhead(hidden, rows, hidden_size, norm_weight, norm_eps, nibbles, scales, vocab,
                                         (__half *)ctx->lm_xh, logits, ctx->dev_err, s);
     if (e != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "%s: launch failed: %s", who, cudaGetErrorString(e));
@@ -651,7 +673,8 @@ int32_t g4s_shard_lists(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t
     const int esize = dtype == G4S_F32 ? 4 : 2;
     const bool vec = ((uintptr_t)logits % 16u == 0) && (((int64_t)row_stride * esize) % 16 == 0);
     const int ept = choose_ept(ctx, rows, slice_vocab);
-    const int nch = (int)ceil_div(slice_vocab, ept * 256);
+    const TopkChunks tc = choose_topk_chunks(ctx, rows, slice_vocab, vec);
+    const int nch = tc.nch;
     if (nch > NCH_MAX_ || (int64_t)rows * nch > ctx->lists_cap)
         return fail(ctx, G4S_ERR_CAPACITY, "%s: %d rows x %d chunks exceed the workspace", who, rows, nch);
     DeviceGuard guard(ctx->device);
@@ -664,17 +687,18 @@ int32_t g4s_shard_lists(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t
     a.rows = rows;
     a.vocab = slice_vocab;
     a.dtype = dtype;
-    a.chunk = ept * 256;
+    a.chunk = tc.chunk;
     a.nch = nch;
     a.cand = ctx->cand;
     a.cand_cnt = ctx->cand_cnt;
     a.counters_topk = ctx->counters_topk;
+    a.err = ctx->dev_err;
     a.id_offset = id_offset;
     a.list_out = out_lists;
     a.list_cnt = out_counts;
     rc = stage_params(ctx, who, params, params_stride, rows, s, a.params);
     if (rc != G4S_OK) return rc;
-    cudaError_t e = launch_topk(a, ept, vec, s);
+    cudaError_t e = tc.stream ? launch_topk_stream(a, s) : launch_topk(a, ept, vec, s);
     if (e != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "%s: launch failed: %s", who, cudaGetErrorString(e));
     return G4S_OK;
 }

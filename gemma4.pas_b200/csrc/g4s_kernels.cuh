@@ -65,6 +65,7 @@ struct SampleArgs {
     const uint64_t *glists;    // shard merge: gathered lists [gworld][rows][KMAX]
     const int32_t *gcnts;      //   and their lengths [gworld][rows]
     int32_t gworld;
+    int *err;                  // device error flag: a bounded wait ran out (nullable)
 };
 
 // Single-row latency path of the top-K selection: one cluster of TOPK_CLUSTER
@@ -76,6 +77,8 @@ constexpr int TOPK_CLUSTER_KMAX = 128;  // largest top_k of the cluster kernel
 
 // Launchers (return the launch status; nothing is launched for rows of other kinds).
 cudaError_t launch_topk(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
+cudaError_t launch_topk_stream(const SampleArgs &a, cudaStream_t s);
+int topk_stream_blocks_per_sm();
 cudaError_t launch_full(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
 cudaError_t launch_full_probs(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
 cudaError_t launch_largek(const SampleArgs &a, cudaStream_t s);

@@ -526,6 +526,243 @@ __device__ __forceinline__ int chunk_select(const SampleArgs &a, int row, int64_
     return m;
 }
 
+// Stage 1 for long chunks (tens of thousands of ids per CTA): one pass with a
+// running threshold.  The chunk streams through a 32 KiB shared-memory ring of
+// tiles filled by 1-D bulk copies (TMA engine, no multicast; completion counted
+// on one mbarrier per slot), so each CTA keeps several tiles in flight without
+// holding them in registers.  Keys >= thr go to the shared candidate buffer
+// sm.L; when the next tile could overflow it, the buffer is compacted to the
+// entries above a bound that keeps at least K of them (stream_cut_to) and thr
+// rises to that bound.  On random logits the buffer is cut about once per
+// chunk, so each logit costs a shared-memory read, a key and a compare.  Leaves the chunk's top min(K,
+// valid) composites sorted descending in sm.L[0..m) and returns m, as
+// chunk_select.
+constexpr int STREAM_TILE = 2048;          // ids per tile (per CTA iteration)
+constexpr int STREAM_RING = 32768;         // bytes of the tile ring per CTA
+constexpr int STREAM_DYN_SMEM = STREAM_RING + 16 * 8;  // ring + one mbarrier per slot
+constexpr long STREAM_WAIT_LIMIT = 1L << 22;
+static_assert(STREAM_TILE * 2 <= CAP2 && KMAX <= STREAM_TILE, "candidate buffer holds two tiles");
+
+// cut the candidate buffer sm.L[0..cnt) (cnt > K) to its K largest composites; returns their smallest
+__device__ uint64_t stream_cut(int cnt, int K, TopkSmem &sm)
+{
+    constexpr int PER = CAP2 / NTHREADS;
+    const int tid = threadIdx.x;
+    const uint64_t kth = radix_kth(
+        [&](auto fn) {
+            for (int i = tid; i < cnt; i += NTHREADS) fn(sm.L[i]);
+        },
+        K, sm);
+    uint64_t keep[PER];
+    int c = 0;
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+        const int i = tid + j * NTHREADS;
+        const uint64_t v = i < cnt ? sm.L[i] : 0;
+        keep[j] = v;
+        c += (i < cnt && v >= kth);
+    }
+    int total;
+    int o = block_excl_scan(c, &total, sm.scan);  // its barriers also end the reads above
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+        const int i = tid + j * NTHREADS;
+        if (i < cnt && keep[j] >= kth) sm.L[o++] = keep[j];
+    }
+    __syncthreads();
+    return kth;
+}
+
+// Compacts the candidate buffer sm.L[0..cnt) to its entries with key >= t',
+// t' = the smallest over warps of each warp's ceil(K / NWARPS)-th largest lane
+// maximum (each warp has that many lanes holding an entry at or above it, so
+// at least K entries survive; on random logits a few times K do).  Raises thr
+// to t'.  Returns the new count.
+__device__ int stream_bound_cut(int cnt, int K, uint32_t &thr, TopkSmem &sm)
+{
+    constexpr int PER = CAP2 / NTHREADS;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint64_t keep[PER];
+    uint32_t mx = 0;
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+        const int i = tid + j * NTHREADS;
+        keep[j] = i < cnt ? sm.L[i] : 0;
+        const uint32_t k = comp_key(keep[j]);
+        mx = k > mx ? k : mx;
+    }
+    const uint32_t srt = warp_sort_desc_u32(mx);
+    const uint32_t wthr = __shfl_sync(FULLMASK, srt, (K + NWARPS - 1) / NWARPS - 1);
+    if (lane == 0) sm.wthr[warp] = wthr;
+    __syncthreads();
+    uint32_t t = sm.wthr[0];
+#pragma unroll
+    for (int w = 1; w < NWARPS; w++) t = sm.wthr[w] < t ? sm.wthr[w] : t;
+    if (t < thr) t = thr;
+    int c = 0;
+#pragma unroll
+    for (int j = 0; j < PER; j++) c += (tid + j * NTHREADS < cnt) && comp_key(keep[j]) >= t;
+    int total;
+    int o = block_excl_scan(c, &total, sm.scan);  // its barriers also end the reads above
+#pragma unroll
+    for (int j = 0; j < PER; j++)
+        if ((tid + j * NTHREADS < cnt) && comp_key(keep[j]) >= t) sm.L[o++] = keep[j];
+    __syncthreads();
+    thr = t;
+    return total;
+}
+
+// Cut for the streaming pass: the bound compaction, and the exact radix cut
+// when ties keep the buffer above `limit` entries.
+__device__ int stream_cut_to(int cnt, int K, int limit, uint32_t &thr, TopkSmem &sm)
+{
+    cnt = stream_bound_cut(cnt, K, thr, sm);
+    if (cnt > limit) {
+        const uint64_t kth = stream_cut(cnt, K, sm);
+        const uint32_t k = comp_key(kth);
+        thr = k > thr ? k : thr;
+        cnt = K;
+    }
+    return cnt;
+}
+
+// rows 16-byte aligned (the host takes the chunk kernel otherwise)
+template <int DT>
+__device__ __forceinline__ int chunk_select_stream(const SampleArgs &a, int row, int64_t c0, int n, int K,
+                                                   TopkSmem &sm, uint8_t *ring)
+{
+    using T = DtypeTraits<DT>;
+    constexpr int VW = T::VW;
+    constexpr int SLOT = STREAM_TILE * T::ESIZE;       // bytes per tile: 8 KiB fp32, 4 KiB bf16
+    constexpr int NSLOT = STREAM_RING / SLOT;          // 4 or 8
+    constexpr int NV = STREAM_TILE / (NTHREADS * VW);  // 16-byte vectors per thread per tile
+    static_assert(NV >= 1 && STREAM_TILE % (NTHREADS * VW) == 0 && NSLOT <= 16, "tile geometry");
+    const int tid = threadIdx.x, lane = tid & 31;
+    const char *src = (const char *)a.logits + ((int64_t)row * a.row_stride + c0) * T::ESIZE;
+    const uint32_t rbase = (uint32_t)__cvta_generic_to_shared(ring);
+    const uint32_t bars = rbase + STREAM_RING;
+    const int ntiles = (n + STREAM_TILE - 1) / STREAM_TILE;
+    // tile t's whole 16-byte vectors come by bulk copy, a ragged end by plain loads
+    auto covered = [&](int t) { return (min(STREAM_TILE, n - t * STREAM_TILE) / VW) * VW; };
+    auto issue = [&](int t) {
+        const int slot = t % NSLOT;
+        const uint32_t bytes = (uint32_t)covered(t) * T::ESIZE;
+        const uint32_t bar = bars + 8 * slot;
+        if (bytes) {
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                             rbase + slot * SLOT),
+                         "l"(src + (int64_t)t * SLOT), "r"(bytes), "r"(bar)
+                         : "memory");
+        } else {
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+        }
+    };
+    if (tid == 0) {
+        for (int k = 0; k < NSLOT; k++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bars + 8 * k) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        sm.misc[3] = 0;
+    }
+    __syncthreads();
+    if (tid == 0)
+        for (int t = 0; t < NSLOT && t < ntiles; t++) issue(t);
+    const float qnan = __uint_as_float(0x7fc00000u);
+    uint32_t thr = 1;  // keys >= thr are candidates (key 0: not a candidate)
+    int cnt = 0;       // buffer fill, uniform (read after each tile's barrier)
+    bool timed_out = false;
+    for (int t = 0; t < ntiles; t++) {
+        const int slot = t % NSLOT, base = t * STREAM_TILE, cov = covered(t);
+        {
+            // bounded wait for the tile (on a timeout: the error flag, and the
+            // stale slot is read; every thread keeps the same control flow)
+            const uint32_t bar = bars + 8 * slot, par = (uint32_t)((t / NSLOT) & 1);
+            uint32_t ok = 0;
+            for (long k = 0; k < STREAM_WAIT_LIMIT && !ok; k++)
+                asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                             : "=r"(ok)
+                             : "r"(bar), "r"(par)
+                             : "memory");
+            timed_out |= !ok;
+        }
+        float x[NV * VW];
+#pragma unroll
+        for (int j = 0; j < NV; j++) {
+            const int e = j * (NTHREADS * VW) + tid * VW;  // within the tile
+            if (e + VW <= cov) {
+                T::unpack(*reinterpret_cast<const uint4 *>(ring + slot * SLOT + e * T::ESIZE), x + j * VW);
+            } else {
+#pragma unroll
+                for (int l = 0; l < VW; l++) {
+                    const int g = base + e + l;
+                    x[j * VW + l] = (g < n) ? T::load1(src, g) : qnan;
+                }
+            }
+        }
+        if (cnt > CAP2 - STREAM_TILE) {
+            cnt = stream_cut_to(cnt, K, CAP2 - STREAM_TILE, thr, sm);
+            if (tid == 0) sm.misc[3] = cnt;
+            __syncthreads();
+        }
+        uint32_t key[NV * VW];
+        int mine = 0;
+#pragma unroll
+        for (int i = 0; i < NV * VW; i++) {
+            key[i] = cand_key(x[i]);
+            mine += key[i] >= thr;
+        }
+        if (__any_sync(FULLMASK, mine)) {
+            const int inc = warp_incl_scan(mine);
+            int wbase = 0;
+            if (lane == 31) wbase = atomicAdd(&sm.misc[3], inc);
+            int o = __shfl_sync(FULLMASK, wbase, 31) + inc - mine;
+#pragma unroll
+            for (int i = 0; i < NV * VW; i++) {
+                if (key[i] >= thr) {
+                    const int e = base + (i / VW) * (NTHREADS * VW) + tid * VW + (i % VW);
+                    sm.L[o++] = composite(key[i], (uint32_t)(a.id_offset + c0 + e));
+                }
+            }
+        }
+        __syncthreads();  // every thread is done with the slot
+        cnt = sm.misc[3];
+        if (tid == 0 && t + NSLOT < ntiles) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic reads before the async refill
+            issue(t + NSLOT);
+        }
+    }
+    if (timed_out && a.err) atomicExch(a.err, 1);
+    // at most NTHREADS entries for the one-pass rank sort, then the first K
+    if (cnt > NTHREADS) cnt = stream_cut_to(cnt, K, NTHREADS, thr, sm);
+    sort_list_desc(sm, cnt);
+    return cnt < K ? cnt : K;
+}
+
+template <int DT>
+__global__ void __launch_bounds__(NTHREADS, 3) topk_stream_kernel(SampleArgs a)
+{
+    __shared__ TopkSmem sm;
+    extern __shared__ __align__(128) uint8_t stream_ring[];  // STREAM_DYN_SMEM: tile ring + mbarriers
+    const int row = blockIdx.y, chunk = blockIdx.x, tid = threadIdx.x;
+    const g4s_params p = a.params.get(row);
+    const int K = p.top_k;
+    if (!(K > 0 && K < a.vocab && K <= KMAX)) return;
+    const int64_t c0 = (int64_t)chunk * a.chunk;
+    const int n = (int)min((int64_t)a.chunk, (int64_t)a.vocab - c0);
+    const int m = chunk_select_stream<DT>(a, row, c0, n, K, sm, stream_ring);
+    uint64_t *out = a.cand + ((int64_t)row * a.nch + chunk) * KMAX;
+    for (int i = tid; i < m; i += NTHREADS) out[i] = sm.L[i];
+    if (tid == 0) a.cand_cnt[(int64_t)row * a.nch + chunk] = m;
+
+    // last-arriving CTA of the row merges (threadfence reduction pattern)
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) sm.misc[0] = atomicAdd(&a.counters_topk[row], 1u) == (unsigned)(a.nch - 1);
+    __syncthreads();
+    if (!sm.misc[0]) return;
+    __threadfence();
+    topk_merge(a, row, p, sm);
+}
+
 template <int DT, int EPT, bool VEC>
 __global__ void __launch_bounds__(NTHREADS) topk_chunk_kernel(SampleArgs a)
 {
@@ -767,6 +1004,52 @@ bool topk_cluster_available()
                     cluster_ok_t<G4S_BF16, true>() && cluster_ok_t<G4S_BF16, false>();
     cudaGetLastError();
     return ok;
+}
+
+template <int DT>
+static bool stream_setup_t()
+{
+    // the tile ring is dynamic shared memory; the whole shared memory of an SM
+    // for its CTAs (about 68 KiB each: three resident)
+    return cudaFuncSetAttribute(topk_stream_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, STREAM_DYN_SMEM) ==
+               cudaSuccess &&
+           cudaFuncSetAttribute(topk_stream_kernel<DT>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                (int)cudaSharedmemCarveoutMaxShared) == cudaSuccess;
+}
+
+template <int DT>
+static cudaError_t launch_stream_t(const SampleArgs &a, cudaStream_t s)
+{
+    static bool ready = false;
+    if (!ready) {
+        if (!stream_setup_t<DT>()) return cudaGetLastError();
+        ready = true;
+    }
+    dim3 grid(a.nch, a.rows);
+    topk_stream_kernel<DT><<<grid, NTHREADS, STREAM_DYN_SMEM, s>>>(a);
+    return cudaGetLastError();
+}
+
+// resident CTAs per SM of the streaming kernel (the grid is sized to one wave)
+int topk_stream_blocks_per_sm()
+{
+    static int nb = 0;
+    if (nb == 0) {
+        if (!stream_setup_t<G4S_F32>() ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, topk_stream_kernel<G4S_F32>, NTHREADS,
+                                                          STREAM_DYN_SMEM) != cudaSuccess ||
+            nb < 1)
+            nb = 1;
+        cudaGetLastError();
+    }
+    return nb;
+}
+
+// long chunks (a.chunk a multiple of STREAM_TILE, rows 16-byte aligned): the
+// running-threshold pass
+cudaError_t launch_topk_stream(const SampleArgs &a, cudaStream_t s)
+{
+    return a.dtype == G4S_F32 ? launch_stream_t<G4S_F32>(a, s) : launch_stream_t<G4S_BF16>(a, s);
 }
 
 cudaError_t launch_topk(const SampleArgs &a, int ept, bool vec, cudaStream_t s)
