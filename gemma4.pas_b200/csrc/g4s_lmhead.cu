@@ -69,7 +69,7 @@ __device__ __forceinline__ void dequant_word(uint32_t w, __half2 sc, uint32_t *h
 // vocab rows; one pipeline stage covers 64 hidden elements (two Q4 blocks):
 //   - the stage's nibbles and scales for the CTA's rows (8 KiB + 1 KiB, each
 //     contiguous in the grouped layout) arrive by 1-D bulk copies (TMA engine,
-//     no multicast) into a ring of TC_RS slots;
+//     single-CTA destination) into a ring of TC_RS slots;
 //   - the stage's activation tile (8 KiB, L2-resident, already in the
 //     canonical K-major core-matrix layout) arrives into a ring of TC_BS slots;
 //   - each dequant thread turns its row's 64 nibbles into fp16 and writes them
@@ -194,7 +194,7 @@ __device__ __forceinline__ void tc_expect(uint32_t bar, uint32_t bytes)
 {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
-// 1-D bulk copy global -> this CTA's shared memory (no multicast), completion
+// 1-D bulk copy global -> this CTA's shared memory only, completion
 // counted on `bar`; addresses 16-byte aligned, size a multiple of 16
 __device__ __forceinline__ void tc_bulk(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar)
 {

@@ -528,7 +528,7 @@ __device__ __forceinline__ int chunk_select(const SampleArgs &a, int row, int64_
 
 // Stage 1 for long chunks (tens of thousands of ids per CTA): one pass with a
 // running threshold.  The chunk streams through a 32 KiB shared-memory ring of
-// tiles filled by 1-D bulk copies (TMA engine, no multicast; completion counted
+// tiles filled by 1-D bulk copies (TMA engine, single-CTA destination; completion counted
 // on one mbarrier per slot), so each CTA keeps several tiles in flight without
 // holding them in registers.  Keys >= thr go to the shared candidate buffer
 // sm.L; when the next tile could overflow it, the buffer is compacted to the
