@@ -4,6 +4,7 @@ degenerate draws, softcap disabled, and argument errors."""
 import numpy as np
 import pytest
 
+import synth
 from gpu_util import BF16, F32, check_full_rows, check_topk_rows, run_gpu
 
 pytestmark = pytest.mark.gpu
@@ -181,3 +182,31 @@ def test_single_row_cluster_merge_paths(sampler, torch_cuda, oracle, g4, K):
     u = np.array([0.37, 0.81])
     for T in (1.0, 0.0):
         _both(sampler, torch_cuda, oracle, x, F32, g4.make_params(T, K, 0.9), CAP, u)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_streaming_topk_batches(sampler, torch_cuda, oracle, g4, dtype):
+    # batches of 64 rows or more with aligned rows take the streaming top-K pass
+    # (long chunks through a bulk-copy tile ring, a running bound, buffer cuts).
+    # Constant rows force the exact radix cut; NaNs, masked and almost empty
+    # rows, per-row K from 1 to 256, and a padded row stride with a vocabulary
+    # that is not a whole number of vectors (the ragged end of each row's last
+    # chunk comes through plain loads).
+    rows, V, stride = 80, 262141, 262144
+    rng = np.random.default_rng(21)
+    x = (rng.standard_normal((rows, V)) * 3).astype(np.float32)
+    x[0, :] = 1.5                                             # one value: ties everywhere
+    x[1, :] = rng.integers(0, 4, V).astype(np.float32)        # four values
+    x[2, rng.choice(V, 500, replace=False)] = np.nan
+    x[3, :] = -np.inf
+    x[3, [7, 131071, V - 1]] = [2.0, 1.0, 3.0]                # three candidates
+    x[4, -5:] = 40.0                                          # the top K in the ragged end
+    if dtype == "bf16":
+        xd, dt = synth.f32_to_bf16_rne(x), BF16
+    else:
+        xd, dt = x, F32
+    ks = [1, 40, 64, 256, 7]
+    prm = [(0.8 if r % 3 else 1.0, ks[r % len(ks)], 0.9) for r in range(rows)]
+    u = rng.random(rows)
+    res = run_gpu(sampler, torch_cuda, xd, dt, prm, CAP, u, cand_stride=256, row_stride=stride)
+    check_topk_rows(oracle, xd, dt, prm, CAP, u, res)
