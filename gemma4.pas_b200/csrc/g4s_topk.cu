@@ -4,23 +4,28 @@
 // DoSelectTopKIndices (src/Gemma4.Model.pas:2615-2689) replaced by an exact
 // parallel selection whose ties at the K-th place go to the lower vocab id.
 //
-// One CTA per (row, chunk of `chunk` ids):
-//   stage 1  the chunk is read once into registers (16-byte streaming loads),
-//            a lower bound t on the chunk's K-th largest key is taken from the
-//            per-thread maxima (each warp's ceil(K/8)-th largest thread max,
-//            minimum over the 8 warps: at least K elements lie at or above it),
-//            the elements >= t are compacted to shared memory, bitonic-sorted by
-//            (value desc, id asc) and the first K written to the workspace.
-//   stage 2  the last CTA of the row (atomic arrival counter) merges the
-//            per-chunk lists: with j = ceil(K / nch), the ceil(K/j)-th largest
-//            of the chunks' j-th entries is again a lower bound on the row's
-//            K-th largest; the entries above it are gathered, sorted, cut to K,
-//            re-sorted by id and handed to the tail.
-//   tail     one warp: softcap, temperature, max, exp, the reference's serial
-//            fp32 sum in ascending-id order, division, argmax, the serial
-//            cumulative draw -- the same fp32 operation sequence as the
-//            reference, so probabilities and tokens are bit-identical to the
-//            oracle's transcription.
+// Three ways to the K winners of a row, one tail:
+//   chunk kernel   (up to 63 rows) one CTA per chunk of `chunk` ids: the chunk
+//            is read once into registers (16-byte streaming loads), a lower
+//            bound t on its K-th largest key is taken from the per-thread
+//            maxima (each warp's ceil(K/8)-th largest thread max, minimum over
+//            the 8 warps: at least K elements lie at or above it), the elements
+//            >= t are compacted to shared memory, sorted by (value desc, id asc)
+//            and the first K written to the workspace; the last CTA of the row
+//            (atomic arrival counter) merges the chunk lists (with j = ceil(K /
+//            nch), the ceil(K/j)-th largest of the lists' j-th entries bounds
+//            the row's K-th largest from below).
+//   stream kernel  (64 rows and more) the same per-chunk lists and merge, each
+//            long chunk streamed through a bulk-copy tile ring with a running
+//            bound (chunk_select_stream).
+//   cluster kernel (up to 8 rows) one 16-CTA thread-block cluster per row,
+//            merged through distributed shared memory (topk_cluster_kernel).
+//   tail     on the whole CTA: the winners re-sorted by id, then per winner
+//            softcap, temperature, max, Exp, the reference's serial fp32 sum in
+//            ascending-id order, division, argmax, the serial cumulative draw
+//            -- the same fp32 operation sequence as the reference, so
+//            probabilities and tokens are bit-identical to the oracle's
+//            transcription.
 #include <cooperative_groups.h>
 
 #include "g4s_device.cuh"
@@ -926,10 +931,38 @@ __global__ void __launch_bounds__(NTHREADS, 1) topk_cluster_kernel(SampleArgs a)
     cluster.sync();  // every push has landed in CTA 0
     if (rank != 0) return;
     const int n2 = s_push;
-    for (int i = tid; i < n2; i += NTHREADS) sm.L[i] = s_w[i];
-    __syncthreads();
-    sort_list_desc(sm, n2);
-    finish_row(a, row, p, n2 < K ? n2 : K, sm);
+    const int kw = n2 < K ? n2 : K;
+    if (n2 <= NTHREADS) {
+        // each pushed entry's rank by value (composites are unique; tpe threads
+        // of adjacent lanes split the count); the K largest go straight to their
+        // rank slot, re-keyed by ascending vocabulary id, then one rank sort puts
+        // them in id order for the tail
+        int tpe = 1;
+        while (tpe < 8 && tpe * 2 * n2 <= NTHREADS) tpe *= 2;
+        const int i = tid / tpe, part = tid & (tpe - 1);
+        const uint64_t v = i < n2 ? s_w[i] : 0;
+        int r0 = 0, r1 = 0;
+        if (i < n2) {
+            const ulonglong2 *W2 = reinterpret_cast<const ulonglong2 *>(s_w);
+            for (int q = part; q < (n2 >> 1); q += tpe) {
+                const ulonglong2 x = W2[q];
+                r0 += x.x > v;
+                r1 += x.y > v;
+            }
+            if ((n2 & 1) && part == 0) r0 += s_w[n2 - 1] > v;
+        }
+        int r = r0 + r1;
+        for (int d = 1; d < tpe; d <<= 1) r += __shfl_xor_sync(FULLMASK, r, d);
+        if (i < n2 && part == 0 && r < K) sm.L[r] = ((uint64_t)comp_id(v) ^ 0xffffffffull) << 32 | comp_key(v);
+        __syncthreads();
+        sort_list_desc(sm, kw);
+        topk_tail(a, row, p, kw, sm);
+    } else {
+        for (int i = tid; i < n2; i += NTHREADS) sm.L[i] = s_w[i];
+        __syncthreads();
+        sort_list_desc(sm, n2);
+        finish_row(a, row, p, kw, sm);
+    }
 }
 
 // ---------------------------------------------------------------------------
