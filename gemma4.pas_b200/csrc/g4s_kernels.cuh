@@ -78,6 +78,19 @@ constexpr int TOPK_CLUSTER_KMAX = 128;  // largest top_k of the cluster kernel
 // Launchers (return the launch status; nothing is launched for rows of other kinds).
 cudaError_t launch_topk(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
 cudaError_t launch_topk_stream(const SampleArgs &a, cudaStream_t s);
+
+// Function attributes (dynamic shared memory limits, carve-outs) belong to
+// each device: set-up that is done once is done once per device.
+constexpr int MAX_DEVICES = 64;
+inline int current_device()
+{
+    int d = -1;
+    if (cudaGetDevice(&d) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    return d;
+}
 int topk_stream_blocks_per_sm();
 cudaError_t launch_full(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
 cudaError_t launch_full_probs(const SampleArgs &a, int ept, bool vec, cudaStream_t s);

@@ -463,11 +463,12 @@ cudaError_t launch_q4_repack(const uint8_t *blocks, int vocab, int hidden, uint8
 cudaError_t launch_lmhead(const float *hidden, int rows, int H, const float *norm_w, float eps, const uint8_t *nib,
                           const uint16_t *scales, int vocab, __half *xh, float *logits, int *err, cudaStream_t s)
 {
-    static bool attr = false;
-    if (!attr) {
+    static bool attr[MAX_DEVICES] = {};
+    const int dev = current_device();
+    if (dev < 0 || dev >= MAX_DEVICES || !attr[dev]) {
         cudaError_t e = cudaFuncSetAttribute(lmhead_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_LAUNCH);
         if (e != cudaSuccess) return e;
-        attr = true;
+        if (dev >= 0 && dev < MAX_DEVICES) attr[dev] = true;
     }
     lmhead_prep_tc_kernel<<<64, 256, 0, s>>>(hidden, rows, H, norm_w, eps, xh);
     cudaError_t e = cudaGetLastError();

@@ -1053,10 +1053,11 @@ static bool stream_setup_t()
 template <int DT>
 static cudaError_t launch_stream_t(const SampleArgs &a, cudaStream_t s)
 {
-    static bool ready = false;
-    if (!ready) {
+    static bool ready[MAX_DEVICES] = {};
+    const int dev = current_device();
+    if (dev < 0 || dev >= MAX_DEVICES || !ready[dev]) {
         if (!stream_setup_t<DT>()) return cudaGetLastError();
-        ready = true;
+        if (dev >= 0 && dev < MAX_DEVICES) ready[dev] = true;
     }
     dim3 grid(a.nch, a.rows);
     topk_stream_kernel<DT><<<grid, NTHREADS, STREAM_DYN_SMEM, s>>>(a);
@@ -1066,7 +1067,9 @@ static cudaError_t launch_stream_t(const SampleArgs &a, cudaStream_t s)
 // resident CTAs per SM of the streaming kernel (the grid is sized to one wave)
 int topk_stream_blocks_per_sm()
 {
-    static int nb = 0;
+    static int nbs[MAX_DEVICES] = {};
+    const int dev = current_device();
+    int nb = dev >= 0 && dev < MAX_DEVICES ? nbs[dev] : 0;
     if (nb == 0) {
         if (!stream_setup_t<G4S_F32>() ||
             cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, topk_stream_kernel<G4S_F32>, NTHREADS,
@@ -1074,6 +1077,7 @@ int topk_stream_blocks_per_sm()
             nb < 1)
             nb = 1;
         cudaGetLastError();
+        if (dev >= 0 && dev < MAX_DEVICES) nbs[dev] = nb;
     }
     return nb;
 }
