@@ -18,7 +18,6 @@
 namespace g4s {
 constexpr int KMAX_ = 256;
 constexpr int NCH_MAX_ = 1024;
-constexpr int STREAM_TILE_ = 2048;       // ids per tile of the streaming top-K pass
 constexpr int STREAM_MIN_CHUNK_ = 8192;  // shortest chunk given to it (four tiles)
 constexpr int STREAM_MIN_ROWS_ = 64;     // fewer rows: the chunk kernel's shorter chunks win (B = 32 measured)
 constexpr int LK_SLOTS = 16;
@@ -133,7 +132,7 @@ static TopkChunks choose_topk_chunks(const g4s_ctx *ctx, int rows, int vocab, bo
     if (ept == 32 && vec && vocab >= STREAM_MIN_CHUNK_ && rows >= STREAM_MIN_ROWS_) {
         const int64_t slots = (int64_t)topk_stream_blocks_per_sm() * ctx->sm_count;
         const int64_t splits = std::max<int64_t>(1, slots / rows);
-        int64_t chunk = ceil_div(ceil_div(vocab, splits), STREAM_TILE_) * STREAM_TILE_;
+        int64_t chunk = ceil_div(ceil_div(vocab, splits), STREAM_TILE) * STREAM_TILE;
         if (chunk < STREAM_MIN_CHUNK_) chunk = STREAM_MIN_CHUNK_;
         return {(int)chunk, (int)ceil_div(vocab, chunk), true};
     }

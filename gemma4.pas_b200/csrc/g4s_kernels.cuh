@@ -77,6 +77,7 @@ constexpr int TOPK_CLUSTER_KMAX = 128;  // largest top_k of the cluster kernel
 
 // Launchers (return the launch status; nothing is launched for rows of other kinds).
 cudaError_t launch_topk(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
+constexpr int STREAM_TILE = 2048;  // ids per tile of the streaming top-K pass; its chunks are whole tiles
 cudaError_t launch_topk_stream(const SampleArgs &a, cudaStream_t s);
 
 // Function attributes (dynamic shared memory limits, carve-outs) belong to

@@ -542,7 +542,6 @@ __device__ __forceinline__ int chunk_select(const SampleArgs &a, int row, int64_
 // chunk, so each logit costs a shared-memory read, a key and a compare.  Leaves the chunk's top min(K,
 // valid) composites sorted descending in sm.L[0..m) and returns m, as
 // chunk_select.
-constexpr int STREAM_TILE = 2048;          // ids per tile (per CTA iteration)
 constexpr int STREAM_RING = 32768;         // bytes of the tile ring per CTA
 constexpr int STREAM_DYN_SMEM = STREAM_RING + 16 * 8;  // ring + one mbarrier per slot
 constexpr long STREAM_WAIT_LIMIT = 1L << 22;
