@@ -67,3 +67,35 @@ def test_rmsnorm_restatement(oracle):
     xd = x.astype(np.float64)
     want = xd / np.sqrt(np.mean(xd * xd) + 1e-6) * w
     assert np.max(np.abs(got - want) / np.abs(want)) < 1e-5
+
+
+def test_lmhead_dequant_identities_exact():
+    # The LM head turns a Q4_0 nibble n (0..15) and the block's fp16 scale s into
+    # the fp16 weight (n - 8) * s rounded once, without an integer-to-float
+    # conversion: the even nibbles of a word are masked in place as the fp16
+    # value 1024 + n, the odd ones as 1024 + 16 n (both exact), then
+    #   even: ((1024 + n) - 1032) * s
+    #   odd:  fma(1024 + 16 n, 1/16, -72) * s
+    # The subtraction and the fused multiply-add give n - 8 exactly, so the
+    # product with s is the only rounding.  Checked for every nibble against a
+    # sweep of scales (normal, subnormal, large, both signs).
+    rng = np.random.default_rng(7)
+    scales = np.concatenate([
+        rng.standard_normal(20000).astype(np.float16),
+        (rng.random(2000) * 0.02).astype(np.float16),                       # the C4 weight scales
+        np.array([6.1e-5, 5.96e-8, -3e-6, 1e-7, 4094.0, -65504 / 16, 1.0, -1.0], dtype=np.float16),
+    ])
+    s32 = scales.astype(np.float32)
+    for n in range(16):
+        want = (np.float32(n - 8) * s32).astype(np.float16)                 # exact product, one rounding
+        even = np.float16(1024 + n) - np.float16(1032)                      # exact in fp16
+        odd = np.float16(np.float32(1024 + 16 * n) * np.float32(1 / 16) - np.float32(72))  # fma, exact
+        assert float(even) == n - 8 and float(odd) == n - 8
+        got_even = (np.float32(even) * s32).astype(np.float16)
+        got_odd = (np.float32(odd) * s32).astype(np.float16)
+        assert np.array_equal(got_even.view(np.uint16), want.view(np.uint16))
+        assert np.array_equal(got_odd.view(np.uint16), want.view(np.uint16))
+    # the masks: the bit patterns 0x6400 | n and 0x6400 | (n << 4) are those values
+    for n in range(16):
+        assert float(np.array([0x6400 | n], dtype=np.uint16).view(np.float16)[0]) == 1024 + n
+        assert float(np.array([0x6400 | (n << 4)], dtype=np.uint16).view(np.float16)[0]) == 1024 + 16 * n
