@@ -48,6 +48,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-c4", action="store_true", help="skip the config C4 (LM head) record")
+    ap.add_argument("--no-c5", action="store_true", help="skip the config C5 record")
     ap.add_argument("--only", choices=["c4"], default=None,
                     help="run config C4 alone and print its record (for profiling)")
     return ap.parse_args()
@@ -71,7 +72,7 @@ def load_peak():
 
 def profiled_traffic():
     """DRAM bytes per launch of the full-path streaming kernel from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "full_stream_kernel_c3.md")
+    path = os.path.join(ROOT, "profiles", "full_tab_kernel_c3.md")
     try:
         m = re.search(r"dram_bytes_per_launch:\s*([0-9]+)", open(path).read())
         return int(m.group(1)) if m else None
@@ -213,6 +214,17 @@ def allreduce_max(x, world):
     return float(t.item())
 
 
+def c3_config(world):
+    """The headline workload, described identically by both arms of the bench."""
+    return {"workload": "C3 full-vocab sampling, B=256 x V=262144 bf16 per GPU, top_k=0, T=1, top_p=0.95, softcap 30",
+            "global_batch": ROWS * world, "seq_len": VOCAB,
+            "parallelism": f"row-sharded x{world} (independent rows, no collective)",
+            "l2": "4 rotating input sets of 128 MiB (512 MiB > 126 MB L2)",
+            "timing": "K steps per timed window (CUDA graphs of up to 250 calls, each replayed once untimed); "
+                      "the window is repeated (15 times at K = 20) and its median reported; CUDA events, max over "
+                      "ranks"}
+
+
 def cpu_reference(rows_bf16, u, nthreads, min_cpu_s=10.0):
     """The reference algorithm (oracle port of DoSample, fp32 transcription) on host
     threads; repeats the sample until ~min_cpu_s of CPU work.  Returns rows/s."""
@@ -226,6 +238,39 @@ def cpu_reference(rows_bf16, u, nthreads, min_cpu_s=10.0):
         el = time.perf_counter() - t0
         if el * nthreads >= min_cpu_s:
             return done / el, done, el
+
+
+def one_core_us_per_row(rows_bf16, u):
+    """The reference algorithm on one host thread: microseconds per C3 row."""
+    from oracle import oracle as O
+
+    p = O.params(1.0, 0, 0.95)
+    O.sample_batch(rows_bf16[:1], O.DTYPE_BF16, p, SOFTCAP, u[:1], O.VARIANT_F32, O.TIE_HEAP, 1)
+    t0 = time.perf_counter()
+    O.sample_batch(rows_bf16, O.DTYPE_BF16, p, SOFTCAP, u, O.VARIANT_F32, O.TIE_HEAP, 1)
+    return (time.perf_counter() - t0) * 1e6 / rows_bf16.shape[0]
+
+
+def verify_c3(rows_bf16, u, got, nthreads):
+    """Tokens of one C3 step against the oracle: equal to the fp64 restatement
+    except draws within 1e-6 of a CDF boundary (counted); also how often the
+    reference's own fp32 arithmetic (serial sums) picks another token."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    p = O.params(1.0, 0, 0.95)
+    t64 = O.sample_batch(rows_bf16, O.DTYPE_BF16, p, SOFTCAP, u, O.VARIANT_F64, O.TIE_LOWER, nthreads)
+    t32 = O.sample_batch(rows_bf16, O.DTYPE_BF16, p, SOFTCAP, u, O.VARIANT_F32, O.TIE_LOWER, nthreads)
+    boundary, bad = 0, 0
+    for r in np.nonzero(got != t64)[0]:
+        _, tr, _, _ = O.sample(O.as_f32(rows_bf16[r]), p, SOFTCAP, u[r], O.VARIANT_F64)
+        if tr["boundary"] < 1e-6:
+            boundary += 1
+        else:
+            bad += 1
+    return {"rows": int(len(got)), "tokens_match_f64": int((got == t64).sum()), "boundary_rows": boundary,
+            "mismatch_outside_band": bad, "ref_f32_vs_f64_rows": int((t32 != t64).sum())}
 
 
 def run_reference(args, emit):
@@ -256,8 +301,7 @@ def run_reference(args, emit):
         "warmup": args.warmup, "ms_per_step": el * 1e3 / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": "C3 full-vocab sampling, B=256 x V=262144 bf16, top_k=0, T=1, top_p=0.95, softcap 30",
-                   "global_batch": ROWS, "seq_len": VOCAB, "parallelism": "host threads"},
+        "config": c3_config(args.gpus),
         "cpu_baseline": {"value": value, "unit": "rows/s", "cores": nthreads, "kind": "port",
                          "sample": f"all {ROWS} rows per step, {args.steps} steps; C oracle port of "
                                    "TModel.DoSample (the Delphi reference does not build here)"},
@@ -323,53 +367,132 @@ def run_c4(dev, peak, steps=20):
                       "20-call CUDA graph"}
 
 
-def run_c5_sharded(s_unused, rank, world, local, dev, peak, steps=200):
-    """Config C5 in the vocabulary-sharded mode: 1024 fp32 rows, each rank
-    holding a contiguous V/world slice of every row (per-row T, top-K, top-P);
-    per step: the slice's top-K lists, two NCCL all-gathers, the merge and the
-    draw.  Device time per step, max over ranks."""
+def run_c5(rank, world, local, dev, peak, steps=50):
+    """Config C5: 1024 fp32 rows x V=262144, per-row T, top-K, top-P.
+
+    N = 1: plain g4s_sample on the whole rows (the one-GPU line of this batch).
+    N > 1: the vocabulary-sharded mode: every rank holds a contiguous V/world
+    slice of every row; per step the slice's top-K lists, two NCCL
+    all-gathers, the merge and the draw (g4s_shard_sample).  The rows are the
+    same on every rank (one seeded generator), so rank 0 also samples the
+    whole rows unsharded on its own GPU and reports how many tokens agree
+    (the merge is exact: all of them must).  Phase times come from separate
+    timed runs of g4s_shard_lists and g4s_shard_merge on the same inputs;
+    the exchange is the step minus the two.  Device time per step, max over
+    ranks; two input buffers alternate (each slice >= 128 MiB at N <= 8)."""
     import numpy as np
     import torch
-    import torch.distributed as dist
 
     import g4sampler as g4
     import synth
 
     rows = 1024
-    lo, hi = g4.shard_slices(VOCAB, world)[rank]
-    n = hi - lo
-    sets = [torch.from_numpy(synth.c5_logits(rows, vocab=n, step=100 * rank + k)).to(dev) for k in range(2)]
-    prm = synth.c5_params(rows)
+    full = synth.c5_logits(rows)  # identical on every rank
+    prm = g4.params_array(synth.c5_params(rows))  # converted once, reused every step
     u = torch.from_numpy(synth.uniforms(rows, synth.SEEDS["c5"])).to(dev)
     out = torch.empty(rows, dtype=torch.int32, device=dev)
+    # a stream of our own: the events below are recorded on it, and its handle
+    # is non-zero (a NULL stream would mean the sampler context's own stream)
+    cs = torch.cuda.Stream(device=dev)
+    stream = cs.cuda_stream
+    torch.cuda.set_stream(cs)
+
+    def timed(fn, n):
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        barrier(world)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for i in range(n):
+            fn(i)
+        t1.record()
+        torch.cuda.synchronize()
+        return allreduce_max(t0.elapsed_time(t1), world) * 1e3 / n
+
+    rec = {"world": world, "rows": rows}
+    single = None
+    if rank == 0:
+        # the whole batch on one GPU (both N = 1 and the reference point at N > 1)
+        xa = torch.from_numpy(full).to(dev)
+        sets = [xa, xa.clone()]
+        s1 = g4.Sampler(local, rows, VOCAB)
+
+        def one(i):
+            s1.sample(sets[i % 2].data_ptr(), g4.F32, rows, VOCAB, VOCAB, prm, SOFTCAP, u.data_ptr(), out.data_ptr(),
+                      stream=stream)
+
+        for i in range(3):
+            one(i)
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for i in range(steps):
+            one(i)
+        t1.record()
+        torch.cuda.synchronize()
+        us = t0.elapsed_time(t1) * 1e3 / steps
+        one(0)
+        torch.cuda.synchronize()
+        single = out.cpu().numpy().copy()
+        s1.close()
+        del sets, xa
+        rec["single_gpu"] = {"us_per_step": us, "rows_per_s": rows / (us * 1e-6),
+                             "hbm_frac_of_peak": rows * VOCAB * 4 / (us * 1e-6) / 1e9 / peak}
+    barrier(world)
+    if world == 1:
+        rec.update(rec.pop("single_gpu"))
+        rec["config"] = ("C5 on one GPU: B=1024 x V=262144 fp32, per-row T~U[0.3,1.5], K in {1,20,64,200}, "
+                         f"P~U[0.5,1]; g4s_sample, {steps} steps, CUDA events")
+        return rec
+
+    lo, hi = g4.shard_slices(VOCAB, world)[rank]
+    n = hi - lo
+    xs = torch.from_numpy(np.ascontiguousarray(full[:, lo:hi])).to(dev)
+    del full
+    sets = [xs, xs.clone()]
     sh = g4.Sampler(local, rows, n)
     uid = torch.zeros(g4.SHARD_UID_BYTES, dtype=torch.uint8, device=dev)
     if rank == 0:
         uid.copy_(torch.frombuffer(bytearray(g4.shard_unique_id()), dtype=torch.uint8))
+    import torch.distributed as dist
+
     dist.broadcast(uid, 0)
     sh.shard_init(world, rank, VOCAB, bytes(uid.cpu().numpy().tobytes()))
-    stream = torch.cuda.current_stream(dev).cuda_stream
-    for i in range(5):
+
+    def step(i):
         sh.shard_sample(sets[i % 2].data_ptr(), g4.F32, rows, n, prm, SOFTCAP, u.data_ptr(), out.data_ptr(),
                         stream=stream)
+
+    step(0)
     torch.cuda.synchronize()
-    dist.barrier()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for i in range(steps):
-        sh.shard_sample(sets[i % 2].data_ptr(), g4.F32, rows, n, prm, SOFTCAP, u.data_ptr(), out.data_ptr(),
-                        stream=stream)
-    t1.record()
-    torch.cuda.synchronize()
-    ms = allreduce_max(t0.elapsed_time(t1), world)
+    got = out.clone()
+    allt = [torch.empty_like(got) for _ in range(world)]
+    dist.all_gather(allt, got)
+    ranks_agree = all(bool(torch.equal(allt[0], t)) for t in allt)
+    us = timed(step, steps)
+    # phases, each timed alone on the same inputs
+    lists = torch.zeros((world, rows, g4.SHARD_LIST), dtype=torch.int64, device=dev)
+    counts = torch.zeros((world, rows), dtype=torch.int32, device=dev)
+    us_lists = timed(lambda i: sh.shard_lists(sets[i % 2].data_ptr(), g4.F32, rows, n, n, lo, VOCAB, prm,
+                                              lists[rank].data_ptr(), counts[rank].data_ptr(), stream=stream), steps)
+    dist.all_gather_into_tensor(lists.view(-1), lists[rank].contiguous().view(-1))
+    dist.all_gather_into_tensor(counts.view(-1), counts[rank].contiguous().view(-1))
+    us_merge = timed(lambda i: sh.shard_merge(lists.data_ptr(), counts.data_ptr(), world, rows, VOCAB, prm, SOFTCAP,
+                                              u.data_ptr(), out.data_ptr(), stream=stream), steps)
     sh.close()
-    us = ms * 1e3 / steps
-    return {"rows_per_s": rows / (us * 1e-6), "us_per_step": us, "world": world,
-            "per_gpu_hbm_frac_of_peak": rows * n * 4 / (us * 1e-6) / 1e9 / peak,
-            "allgather_bytes_per_rank": rows * (g4.SHARD_LIST * 8 + 4),
-            "config": f"C5 sharded: B=1024 x V=262144 fp32, a {n}-id slice per rank; per-row T~U[0.3,1.5], "
-                      "K in {1,20,64,200}, P~U[0.5,1]; lists -> ncclAllGather x2 -> merge; "
-                      f"{steps} steps, host loop, CUDA events, max over ranks"}
+    if rank == 0:
+        rec["tokens_match"] = int((got.cpu().numpy() == single).sum())
+    rec["ranks_agree"] = ranks_agree
+    rec.update({"rows_per_s": rows / (us * 1e-6), "us_per_step": us,
+                "per_gpu_hbm_frac_of_peak": rows * n * 4 / (us * 1e-6) / 1e9 / peak,
+                "phases_us": {"lists": us_lists, "merge": us_merge, "exchange": max(0.0, us - us_lists - us_merge)},
+                "lists_hbm_frac_of_peak": rows * n * 4 / (us_lists * 1e-6) / 1e9 / peak,
+                "allgather_bytes_per_rank": rows * (g4.SHARD_LIST * 8 + 4),
+                "config": f"C5 sharded: B=1024 x V=262144 fp32, a {n}-id slice per rank; per-row T~U[0.3,1.5], "
+                          "K in {1,20,64,200}, P~U[0.5,1]; lists -> ncclAllGather x2 -> merge; "
+                          f"{steps} steps, host loop, CUDA events, max over ranks; phases timed alone"})
+    return rec
 
 
 def main():
@@ -437,33 +560,47 @@ def main():
         gr.replay()
         return gr
 
-    def timed(graphs, clocks=None):
-        torch.cuda.synchronize()
-        barrier(world)
+    def timed(graphs, clocks=None, reps=1):
+        """The K steps `graphs` hold, timed `reps` times (each time exactly K
+        steps between a barrier + synchronize on both sides, max over ranks);
+        returns the median over the repetitions."""
         if clocks:
             clocks.start()
-        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        t0.record()
-        for gr in graphs:
-            gr.replay()
-        t1.record()
-        torch.cuda.synchronize()
+        runs = []
+        for _ in range(reps):
+            torch.cuda.synchronize()
+            barrier(world)
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record()
+            for gr in graphs:
+                gr.replay()
+            t1.record()
+            torch.cuda.synchronize()
+            barrier(world)
+            runs.append(allreduce_max(t0.elapsed_time(t1), world))
         clk = clocks.stop() if clocks else None
-        barrier(world)
-        return t0.elapsed_time(t1), clk
+        return statistics.median(runs), clk, runs
 
     g_main = capture(G)
     g_rest = capture(K % G) if K % G else None
     plan = [g_main] * (K // G) + ([g_rest] if g_rest else [])
-    total_ms, clk = timed(plan, Clocks(local))
-    total_ms_max = allreduce_max(total_ms, world)
+    # short K (the driver's K = 20 is ~1 ms of work): repeat the K-step window
+    # and take the median, so one scheduling hiccup or rank skew does not decide
+    reps = max(1, min(15, int(20000 // max(K, 1))))
+    total_ms_max, clk, rep_ms = timed(plan, Clocks(local), reps)
     value = world * ROWS * K / (total_ms_max / 1e3)
     tokens_ok = bool(((out >= 0) & (out < VOCAB)).all().item())
+    # one step of the timed workload, checked against the oracle (rank 0)
+    check = None
+    if rank == 0:
+        s.sample(sets[0].data_ptr(), g4.BF16, ROWS, VOCAB, VOCAB, p, SOFTCAP, u_all[0].data_ptr(), out.data_ptr())
+        torch.cuda.synchronize()
+        check = verify_c3(base, u_all[0].cpu().numpy(), out.cpu().numpy(), host_threads())
     # the dominant kernel alone: the same steps with only the streaming pass
     # (G4S_PHASE_FULL_STREAM_ONLY), for the roofline's achieved bandwidth
     gs_main = capture(G, 1)
     gs_rest = capture(K % G, 1) if K % G else None
-    stream_ms, _ = timed([gs_main] * (K // G) + ([gs_rest] if gs_rest else []))
+    stream_ms, _, _ = timed([gs_main] * (K // G) + ([gs_rest] if gs_rest else []), None, reps)
     stream_us = stream_ms / K * 1e3
     achieved = ROWS * BYTES_PER_ROW / (stream_us * 1e-6) / 1e9
     del plan, g_main, g_rest, gs_main, gs_rest
@@ -510,13 +647,37 @@ def main():
         with torch.cuda.graph(g1, stream=cap):
             call1(0, cap.cuda_stream)
         ls = replay_times(g1, 200)
-        lat = {"p50_us": lt[len(lt) // 2], "p90_us": lt[int(len(lt) * 0.9)],
+        # After a producer, as in a decode step: each call samples a row that a
+        # kernel just wrote (a 1 MiB device copy standing in for the LM head),
+        # so consecutive sampler calls cannot overlap each other.  The step's
+        # latency is the graph [copy -> sample] x 20 minus the graph [copy] x 20.
+        work = torch.empty(VOCAB, dtype=torch.float32, device=dev)
+
+        def call_w(i, st):
+            s.sample(work.data_ptr(), g4.F32, 1, VOCAB, VOCAB, p1, SOFTCAP, u1[i:].data_ptr(), o1[i:].data_ptr(),
+                     stream=st)
+
+        gp = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gp, stream=cap):
+            for i in range(n1):
+                work.copy_(c1[i])
+                call_w(i, cap.cuda_stream)
+        gq = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gq, stream=cap):
+            for i in range(n1):
+                work.copy_(c1[i])
+        tq = statistics.median(replay_times(gq, 200)) / n1
+        tp = sorted(t / n1 - tq for t in replay_times(gp, 200))
+        lat = {"p50_us": tp[len(tp) // 2], "p90_us": tp[int(len(tp) * 0.9)],
+               "pipelined_p50_us": lt[len(lt) // 2], "pipelined_p90_us": lt[int(len(lt) * 0.9)],
                "single_graph_p50_us": ls[len(ls) // 2], "single_graph_p90_us": ls[int(len(ls) * 0.9)],
-               "steps": 200 * n1,
-               "config": "C1: B=1 x V=262144 fp32 (fresh row per call), top_k 64, T=1, top_p 0.95; p50_us: device "
-                         "time per call inside a CUDA graph of 20 consecutive calls; single_graph: one call per "
-                         "graph replay"}
-        del gl, g1
+               "producer_us": tq, "steps": 200 * n1,
+               "config": "C1: B=1 x V=262144 fp32 (fresh row per call), top_k 64, T=1, top_p 0.95.  p50_us: one "
+                         "step after a producer -- graph of 20 x [1 MiB copy writing the row -> g4s_sample] minus "
+                         "graph of 20 x [copy], per step, p50/p90 over 200 replays; pipelined: 20 consecutive calls "
+                         "in one graph (call i+1's launch overlaps call i); single_graph: one call per graph replay "
+                         "(includes the graph launch)"}
+        del gl, g1, gp, gq
 
         # ---- config C2: B=32 fp32 rows, T=0.7, top_k 40, top_p 0.9 (HBM-bound top-K) ----
         nset, k2 = 8, 200
@@ -533,7 +694,18 @@ def main():
                 s.sample(c2sets[i % nset].data_ptr(), g4.F32, 32, VOCAB, VOCAB, p2, SOFTCAP, u2.data_ptr(),
                          o2.data_ptr(), stream=cap.cuda_stream)
         t2 = statistics.median(replay_times(g2, 5)) / k2
+        s.sample(c2sets[0].data_ptr(), g4.F32, 32, VOCAB, VOCAB, p2, SOFTCAP, u2.data_ptr(), o2.data_ptr())
+        torch.cuda.synchronize()
+        from oracle import oracle as O
+
+        x2 = synth.c2_logits(32, step=0)
+        u2h = u2.cpu().numpy()
+        want2 = O.sample_batch(x2, O.DTYPE_F32, O.params(0.7, 40, 0.9), SOFTCAP, u2h, O.VARIANT_F32, O.TIE_LOWER,
+                               host_threads())
+        ties2 = sum(int(not np.array_equal(np.sort(O.topk(x2[r], 40, O.TIE_HEAP)), np.sort(O.topk(x2[r], 40, O.TIE_LOWER))))
+                    for r in range(32))
         c2 = {"rows_per_s": 32 / (t2 * 1e-6), "us_per_step": t2,
+              "tokens_match_oracle": int((o2.cpu().numpy() == want2).sum()), "heap_tie_rows": ties2,
               "hbm_frac_of_peak": 32 * VOCAB * 4 / (t2 * 1e-6) / 1e9 / peak,
               "config": "C2: B=32 x V=262144 fp32, T=0.7, top_k 40, top_p 0.9; 8 rotating input sets "
                         "(256 MiB > L2); 200 calls per CUDA graph, median of 5 replays"}
@@ -565,27 +737,28 @@ def main():
         nt = host_threads()
         sample = base[:64]
         rps, done, el = cpu_reference(sample, synth.uniforms(64, 3), nt)
+        us1 = one_core_us_per_row(base[:8], synth.uniforms(8, 4))
         cpu = {"value": rps, "unit": "rows/s", "cores": nt, "kind": "port",
+               "us_per_row_1core": us1,
                "sample": f"{done} C3 rows ({64}-row sample repeated, {el:.1f} s wall on {nt} threads); "
-                         "C oracle port of TModel.DoSample, fp32 transcription"}
+                         "C oracle port of TModel.DoSample, fp32 transcription; us_per_row_1core: 8 rows on one "
+                         "thread, as the reference's single-threaded DoSample"}
 
     s.close()
-    c5 = run_c5_sharded(None, rank, world, local, dev, peak) if world > 1 else None
+    c5 = run_c5(rank, world, local, dev, peak) if not args.no_c5 else None
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": total_ms_max / K, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "C3 full-vocab sampling, B=256 x V=262144 bf16 per GPU, top_k=0, T=1, "
-                                   "top_p=0.95, softcap 30",
-                       "global_batch": ROWS * world, "seq_len": VOCAB,
-                       "parallelism": f"row-sharded x{world} (independent rows, no collective)",
-                       "l2": "4 rotating input sets of 128 MiB (512 MiB > 126 MB L2)",
-                       "timing": f"K steps from CUDA graphs of {G} calls, each graph replayed once "
-                                 "untimed; K steps timed with CUDA events"},
+            "config": c3_config(world),
+            "timed_windows_ms": rep_ms,
             "hbm_frac_of_peak": ROWS * BYTES_PER_ROW / (total_ms_max / K * 1e-3) / 1e9 / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": profiled_traffic(),
+                         "traffic_source": "static: dram__bytes_read + dram__bytes_write of one launch in the "
+                                           "committed ncu capture (profiles/full_tab_kernel_c3.md), not measured "
+                                           "in this run",
                          "kernel": "full_stream_kernel<bf16>, timed alone (phase_mask = stream only), "
                                    "CUDA events over K launches",
                          "kernel_mean_us": stream_us,
@@ -596,12 +769,13 @@ def main():
             "latency_b1": lat,
             "c2": c2,
             "c4": c4,
-            "c5_sharded": c5,
+            "c5": c5,
             "e2e": e2e,
             "cpu_baseline": cpu,
             "gpu_launches": 2 * K,
             "clocks": clk,
             "tokens_in_range": tokens_ok,
+            "parity_c3": check,
         }
         emit(line)
     if world > 1:

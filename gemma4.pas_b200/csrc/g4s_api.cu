@@ -43,6 +43,9 @@ struct g4s_ctx {
     uint32_t *counters_topk = nullptr;
     float4 *istat = nullptr;
     int persist[2][2] = {{0, 0}, {0, 0}};  // full-path streaming CTAs per SM [dtype][vec]
+    int persist_tab = 0;                   // the same for the bf16 softcap-table variant
+    float *sc_tab = nullptr;               // bf16 softcap table (workspace), built for sc_tab_cap
+    float sc_tab_cap = 0.0f;               // softcap the table holds (0: not built)
     RowStat *rowstat = nullptr;
     int32_t *lk_idx = nullptr;
     float *lk_val = nullptr;
@@ -62,6 +65,7 @@ struct g4s_ctx {
     float *lm_logits = nullptr;
     void *lm_xh = nullptr;
     int *dev_err = nullptr;  // device error flag in the workspace (a bounded wait that ran out), read by g4s_device_status
+    int64_t wait_limit = 0;  // g4s_set_wait_limit (test hook; 0 = the kernels' own limits)
     size_t lm_logits_n = 0, lm_xh_n = 0;
     // g4s_sample_host staging
     void *h_logits = nullptr;
@@ -361,6 +365,7 @@ int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t
     const size_t o_lv = off; off = align(off + (size_t)LK_SLOTS * max_vocab * sizeof(float));
     const size_t o_pd = off; off = align(off + (size_t)PSLOTS * max_rows * (sizeof(g4s_params) + sizeof(float)));
     const size_t o_err = off; off = align(off + sizeof(int));
+    const size_t o_tab = off; off = align(off + (size_t)SC_TABLE_BYTES);
     ctx->ws_bytes = off;
     if (cudaMalloc(&ctx->ws, off) != cudaSuccess) {
         cudaGetLastError();
@@ -377,6 +382,7 @@ int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t
     ctx->lk_val = (float *)(base + o_lv);
     ctx->params_dev = (g4s_params *)(base + o_pd);
     ctx->dev_err = (int *)(base + o_err);
+    ctx->sc_tab = (float *)(base + o_tab);
     if (cudaMemset(ctx->ws, 0, off) != cudaSuccess ||
         cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaHostAlloc((void **)&ctx->params_pinned, (size_t)PSLOTS * max_rows * (sizeof(g4s_params) + sizeof(float)),
@@ -457,6 +463,10 @@ int32_t g4s_sample_ex(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t r
     if ((ex.cand_ids || ex.cand_probs) && any_topk && ex.cand_stride < max_k_small)
         return fail(ctx, G4S_ERR_ARG, "g4s_sample: cand_stride %d < largest top_k %d", ex.cand_stride, max_k_small);
 
+    // the context's device is current before the chunk choice: its occupancy
+    // query and launch attributes are per device
+    DeviceGuard guard(ctx->device);
+    if (!guard.ok) return fail(ctx, G4S_ERR_CUDA, "g4s_sample: cannot select device %d", ctx->device);
     const int esize = dtype == G4S_F32 ? 4 : 2;
     const bool vec = ((uintptr_t)logits % 16u == 0) && (((int64_t)row_stride * esize) % 16 == 0);
     const int ept = choose_ept(ctx, rows, vocab);
@@ -465,9 +475,6 @@ int32_t g4s_sample_ex(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t r
     const int nch = tc.nch;
     if (nch > NCH_MAX_ || (int64_t)rows * nch > ctx->lists_cap)
         return fail(ctx, G4S_ERR_CAPACITY, "g4s_sample: %d rows x %d chunks exceed the workspace", rows, nch);
-
-    DeviceGuard guard(ctx->device);
-    if (!guard.ok) return fail(ctx, G4S_ERR_CUDA, "g4s_sample: cannot select device %d", ctx->device);
     cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
 
     SampleArgs a;
@@ -495,10 +502,28 @@ int32_t g4s_sample_ex(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t r
     a.cand_cnt = ctx->cand_cnt;
     a.counters_topk = ctx->counters_topk;
     a.err = ctx->dev_err;
+    a.wait_limit = ctx->wait_limit;
     a.istat = ctx->istat;
+    // bf16 full-path rows take the softcap from a table built once per softcap
+    // value.  Outside stream capture the build is waited for, so calls on any
+    // stream may use it afterwards; a captured build is part of the graph and
+    // is not remembered (the next call outside the graph builds again).
+    const bool use_tab = any_full && dtype == G4S_BF16 && vec && softcap > 0.0f && softcap <= SC_TABLE_MAX_CAP;
+    if (use_tab && ctx->sc_tab_cap != softcap) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(s, &cs) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(ctx, G4S_ERR_CUDA, "g4s_sample: cannot query the stream's capture state");
+        }
+        cudaError_t te = launch_softcap_table(softcap, a.invcap, ctx->sc_tab, s);
+        if (te == cudaSuccess && cs == cudaStreamCaptureStatusNone) te = cudaStreamSynchronize(s);
+        if (te != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "g4s_sample: softcap table: %s", cudaGetErrorString(te));
+        if (cs == cudaStreamCaptureStatusNone) ctx->sc_tab_cap = softcap;
+    }
+    a.sc_table = use_tab ? ctx->sc_tab : nullptr;
     if (any_full) {
-        int &bps = ctx->persist[dtype][vec ? 1 : 0];
-        if (bps == 0) bps = full_stream_blocks_per_sm(dtype, vec);
+        int &bps = use_tab ? ctx->persist_tab : ctx->persist[dtype][vec ? 1 : 0];
+        if (bps == 0) bps = full_stream_blocks_per_sm(dtype, vec, use_tab);
         a.persist_blocks = bps * ctx->sm_count;
     }
     a.rowstat = ctx->rowstat;
@@ -627,6 +652,14 @@ int32_t g4s_lmhead_sample(g4s_ctx *ctx, const float *hidden, int32_t rows, int32
                          extra, s);
 }
 
+int32_t g4s_set_wait_limit(g4s_ctx *ctx, int64_t polls)
+{
+    if (!ctx) return fail(nullptr, G4S_ERR_ARG, "g4s_set_wait_limit: ctx is NULL");
+    if (polls < 0) return fail(ctx, G4S_ERR_ARG, "g4s_set_wait_limit: polls %lld < 0", (long long)polls);
+    ctx->wait_limit = polls;
+    return G4S_OK;
+}
+
 int32_t g4s_device_status(g4s_ctx *ctx)
 {
     if (!ctx) return fail(nullptr, G4S_ERR_ARG, "g4s_device_status: ctx is NULL");
@@ -648,9 +681,12 @@ int32_t g4s_device_status(g4s_ctx *ctx)
 // ---------------------------------------------------------------------------
 // vocabulary-sharded mode
 // ---------------------------------------------------------------------------
-int32_t g4s_shard_lists(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t rows, int32_t slice_vocab,
-                        int64_t row_stride, int32_t id_offset, int32_t vocab_total, const g4s_params *params,
-                        int32_t params_stride, uint64_t *out_lists, int32_t *out_counts, void *stream)
+// The two phases of the sharded mode; `staged` (nullable) is the call's per-row
+// params already on the device (g4s_shard_sample stages them once for both).
+static int32_t shard_lists_core(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t rows, int32_t slice_vocab,
+                                int64_t row_stride, int32_t id_offset, int32_t vocab_total, const g4s_params *params,
+                                int32_t params_stride, uint64_t *out_lists, int32_t *out_counts, void *stream,
+                                const RowParams *staged)
 {
     static const char *who = "g4s_shard_lists";
     if (!ctx) return fail(nullptr, G4S_ERR_ARG, "%s: ctx is NULL", who);
@@ -669,6 +705,8 @@ int32_t g4s_shard_lists(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t
     bool any_draw;
     int32_t rc = check_shard_rows(ctx, who, params, params_stride, rows, slice_vocab, vocab_total, &any_draw);
     if (rc != G4S_OK) return rc;
+    DeviceGuard guard(ctx->device);
+    if (!guard.ok) return fail(ctx, G4S_ERR_CUDA, "%s: cannot select device %d", who, ctx->device);
     const int esize = dtype == G4S_F32 ? 4 : 2;
     const bool vec = ((uintptr_t)logits % 16u == 0) && (((int64_t)row_stride * esize) % 16 == 0);
     const int ept = choose_ept(ctx, rows, slice_vocab);
@@ -676,8 +714,6 @@ int32_t g4s_shard_lists(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t
     const int nch = tc.nch;
     if (nch > NCH_MAX_ || (int64_t)rows * nch > ctx->lists_cap)
         return fail(ctx, G4S_ERR_CAPACITY, "%s: %d rows x %d chunks exceed the workspace", who, rows, nch);
-    DeviceGuard guard(ctx->device);
-    if (!guard.ok) return fail(ctx, G4S_ERR_CUDA, "%s: cannot select device %d", who, ctx->device);
     cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
     SampleArgs a;
     memset(&a, 0, sizeof(a));
@@ -692,19 +728,21 @@ int32_t g4s_shard_lists(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t
     a.cand_cnt = ctx->cand_cnt;
     a.counters_topk = ctx->counters_topk;
     a.err = ctx->dev_err;
+    a.wait_limit = ctx->wait_limit;
     a.id_offset = id_offset;
     a.list_out = out_lists;
     a.list_cnt = out_counts;
-    rc = stage_params(ctx, who, params, params_stride, rows, s, a.params);
-    if (rc != G4S_OK) return rc;
+    if (staged) a.params = *staged;
+    else if ((rc = stage_params(ctx, who, params, params_stride, rows, s, a.params)) != G4S_OK) return rc;
     cudaError_t e = tc.stream ? launch_topk_stream(a, s) : launch_topk(a, ept, vec, s);
     if (e != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "%s: launch failed: %s", who, cudaGetErrorString(e));
     return G4S_OK;
 }
 
-int32_t g4s_shard_merge(g4s_ctx *ctx, const uint64_t *lists, const int32_t *counts, int32_t world, int32_t rows,
-                        int32_t vocab_total, const g4s_params *params, int32_t params_stride, float softcap,
-                        const double *u, int32_t *out_tokens, const g4s_outputs *extra, void *stream)
+static int32_t shard_merge_core(g4s_ctx *ctx, const uint64_t *lists, const int32_t *counts, int32_t world,
+                                int32_t rows, int32_t vocab_total, const g4s_params *params, int32_t params_stride,
+                                float softcap, const double *u, int32_t *out_tokens, const g4s_outputs *extra,
+                                void *stream, const RowParams *staged)
 {
     static const char *who = "g4s_shard_merge";
     if (!ctx) return fail(nullptr, G4S_ERR_ARG, "%s: ctx is NULL", who);
@@ -744,11 +782,27 @@ int32_t g4s_shard_merge(g4s_ctx *ctx, const uint64_t *lists, const int32_t *coun
     a.glists = lists;
     a.gcnts = counts;
     a.gworld = world;
-    rc = stage_params(ctx, who, params, params_stride, rows, s, a.params);
-    if (rc != G4S_OK) return rc;
+    if (staged) a.params = *staged;
+    else if ((rc = stage_params(ctx, who, params, params_stride, rows, s, a.params)) != G4S_OK) return rc;
     cudaError_t e = launch_shard_merge(a, s);
     if (e != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "%s: launch failed: %s", who, cudaGetErrorString(e));
     return G4S_OK;
+}
+
+int32_t g4s_shard_lists(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t rows, int32_t slice_vocab,
+                        int64_t row_stride, int32_t id_offset, int32_t vocab_total, const g4s_params *params,
+                        int32_t params_stride, uint64_t *out_lists, int32_t *out_counts, void *stream)
+{
+    return shard_lists_core(ctx, logits, dtype, rows, slice_vocab, row_stride, id_offset, vocab_total, params,
+                            params_stride, out_lists, out_counts, stream, nullptr);
+}
+
+int32_t g4s_shard_merge(g4s_ctx *ctx, const uint64_t *lists, const int32_t *counts, int32_t world, int32_t rows,
+                        int32_t vocab_total, const g4s_params *params, int32_t params_stride, float softcap,
+                        const double *u, int32_t *out_tokens, const g4s_outputs *extra, void *stream)
+{
+    return shard_merge_core(ctx, lists, counts, world, rows, vocab_total, params, params_stride, softcap, u, out_tokens,
+                            extra, stream, nullptr);
 }
 
 int32_t g4s_shard_unique_id(uint8_t *uid)
@@ -815,10 +869,20 @@ int32_t g4s_shard_sample(g4s_ctx *ctx, const void *logits_slice, int32_t dtype, 
     int32_t *send_cnt = (int32_t *)(ctx->sh_send + (size_t)ctx->max_rows * KMAX_);
     uint64_t *recv = ctx->sh_recv;
     int32_t *recv_cnt = (int32_t *)(ctx->sh_recv + (size_t)W * ctx->max_rows * KMAX_);
-    int32_t rc = g4s_shard_lists(ctx, logits_slice, dtype, rows, n, row_stride, off, ctx->shard_vocab, params,
-                                 params_stride, send, send_cnt, s);
+    if (!params || (params_stride != 0 && params_stride != 1))
+        return fail(ctx, G4S_ERR_ARG, "%s: params must be non-NULL, params_stride 0 or 1", who);
+    bool any_draw;
+    int32_t rc = check_shard_rows(ctx, who, params, params_stride, rows, n, ctx->shard_vocab, &any_draw);
     if (rc != G4S_OK) return rc;
     DeviceGuard guard(ctx->device);
+    if (!guard.ok) return fail(ctx, G4S_ERR_CUDA, "%s: cannot select device %d", who, ctx->device);
+    // per-row params go to the device once for both phases
+    RowParams rp;
+    memset(&rp, 0, sizeof(rp));
+    if ((rc = stage_params(ctx, who, params, params_stride, rows, s, rp)) != G4S_OK) return rc;
+    rc = shard_lists_core(ctx, logits_slice, dtype, rows, n, row_stride, off, ctx->shard_vocab, params, params_stride,
+                          send, send_cnt, s, &rp);
+    if (rc != G4S_OK) return rc;
     ncclComm_t comm = (ncclComm_t)ctx->nccl_comm;
     ncclResult_t r = g_nccl.GroupStart();
     if (r == ncclSuccess) r = g_nccl.AllGather(send, recv, (size_t)rows * KMAX_, ncclUint64, comm, s);
@@ -827,8 +891,8 @@ int32_t g4s_shard_sample(g4s_ctx *ctx, const void *logits_slice, int32_t dtype, 
     if (r == ncclSuccess) r = r2;
     if (r != ncclSuccess) return fail(ctx, G4S_ERR_NCCL, "%s: all-gather: %s", who, g_nccl.GetErrorString(r));
     // the merge reads list w of row i at recv + w * rows * KMAX + i * KMAX
-    return g4s_shard_merge(ctx, recv, recv_cnt, W, rows, ctx->shard_vocab, params, params_stride, softcap, u,
-                           out_tokens, extra, s);
+    return shard_merge_core(ctx, recv, recv_cnt, W, rows, ctx->shard_vocab, params, params_stride, softcap, u,
+                            out_tokens, extra, s, &rp);
 }
 
 }  // extern "C"

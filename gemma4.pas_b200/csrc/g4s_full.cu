@@ -266,6 +266,56 @@ __device__ __forceinline__ float fast_exp_sum_any(Vec vec, const SParams &sp, fl
     return sp.use_t ? fast_exp_sum<DT, false, true, ROLLED>(vec, sp, cc) : fast_exp_sum<DT, false, false, ROLLED>(vec, sp, cc);
 }
 
+// ---------------------------------------------------------------------------
+// bf16 softcap table.  For bf16 logits the softcapped value s = fl32(tanh(
+// fl32(v * (1/cap))) * cap) depends only on the 16-bit input, and it is odd
+// (every step of the fp32 sequence is), so one fp32 entry per magnitude code
+// gives s exactly: tab[c - TAB_LOW] = s(bits c << 16) for the magnitude codes
+// c = TAB_LOW .. TAB_TOP (2^-16 <= |v| <= 512), built on the device with the
+// same g4_tanhf as every other path.  Above 512, s is cap itself for cap <=
+// SC_TABLE_MAX_CAP (tanh(q) rounds to 1 beyond q = 9.02), so larger
+// magnitudes, infinities included, clamp to the last entry.  Items holding a
+// NaN or a magnitude below 2^-16 (zero included) are flagged for the exact
+// general path instead.  A lookup replaces the 13 fp32 FMA-pipe operations of
+// the polynomial with integer work and one shared-memory load.
+// ---------------------------------------------------------------------------
+constexpr uint32_t TAB_LOW = 0x3780u;  // 2^-16
+constexpr uint32_t TAB_TOP = 0x4400u;  // 512
+constexpr int SC_TAB_N = (int)(TAB_TOP - TAB_LOW) + 1;
+constexpr int SC_TAB_BYTES = (SC_TAB_N * 4 + 15) / 16 * 16;
+static_assert(SC_TAB_BYTES == SC_TABLE_BYTES, "table size in the launch interface");
+static_assert(SC_TABLE_MAX_CAP * 9.1f <= 512.0f, "s saturates to cap within the table");
+
+__global__ void softcap_table_kernel(float cap, float invcap, float *tab)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < SC_TAB_N)
+        tab[i] = __fmul_rn(g4_tanhf(__fmul_rn(__uint_as_float((TAB_LOW + (uint32_t)i) << 16), invcap)), cap);
+}
+
+__device__ __forceinline__ uint32_t min_u16x2(uint32_t a, uint32_t b)
+{
+    uint32_t r;
+    asm("min.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b)
+{
+    uint32_t r;
+    asm("max.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+// s of both bf16 logits of a 32-bit word (low half first).  tab0 points
+// TAB_LOW entries before the table, so a clamped magnitude code indexes it.
+__device__ __forceinline__ float2 tab_s2(uint32_t w, const float *tab0)
+{
+    const uint32_t m = min_u16x2(max_u16x2(w & 0x7fff7fffu, (TAB_LOW << 16) | TAB_LOW), (TAB_TOP << 16) | TAB_TOP);
+    const uint32_t lo = __float_as_uint(tab0[m & 0xffffu]) ^ ((w << 16) & 0x80000000u);
+    const uint32_t hi = __float_as_uint(tab0[m >> 16]) ^ (w & 0x80000000u);
+    return make_float2(__uint_as_float(lo), __uint_as_float(hi));
+}
+
 // One item of the streaming pass; vec(j) returns this lane's vector j.  The
 // fast path runs without waiting for the warp's verdict on it; the vote comes
 // after the exponent sum.  Items that must be redone on the general path (a
@@ -405,6 +455,184 @@ __global__ void __launch_bounds__(STREAM_THREADS) full_stream_kernel(SampleArgs 
         }
         cp_async_wait<0>();
     }
+}
+
+// ---------------------------------------------------------------------------
+// full_tab_kernel: the streaming pass for aligned bf16 rows with a softcap in
+// (0, SC_TABLE_MAX_CAP].  Same items, ring and statistics as
+// full_stream_kernel, and the same per-element values and accumulation order
+// (so the item sums are bit-identical), but each lane's first TAB_NT vectors
+// of an item take s from the shared-memory table and the others from the
+// polynomial: the lookups load the shared-memory pipe, the polynomial the
+// fp32 FMA pipe, and the two run side by side.  An item is flagged for the
+// combine when it holds a NaN, a magnitude below 2^-16 in a table vector, an
+// |v * (1/cap)| > 1 in a polynomial vector, or is a ragged last item.  CTAs of
+// TAB_THREADS, two per SM; dynamic shared memory = ring + table.
+// ---------------------------------------------------------------------------
+#ifndef G4S_TAB_THREADS
+#define G4S_TAB_THREADS 512
+#endif
+#ifndef G4S_TAB_NT
+#define G4S_TAB_NT 4
+#endif
+#ifndef G4S_TAB_CPS
+#define G4S_TAB_CPS 2
+#endif
+constexpr int TAB_THREADS = G4S_TAB_THREADS;
+constexpr int TAB_NT = G4S_TAB_NT;  // vectors per lane and item looked up in the table (of NVEC)
+constexpr int TAB_RING_BYTES = (TAB_THREADS / 32) * STAGES * NVEC * 32 * 16;
+constexpr int TAB_DYN_SMEM = TAB_RING_BYTES + SC_TAB_BYTES;
+static_assert(TAB_NT >= 0 && TAB_NT <= NVEC, "table vectors");
+
+__device__ __forceinline__ uint32_t bmax4(uint4 v) { return bmax2_nan(bmax2_nan(v.x, v.y), bmax2_nan(v.z, v.w)); }
+__device__ __forceinline__ uint32_t bmin4(uint4 v) { return bmin2_nan(bmin2_nan(v.x, v.y), bmin2_nan(v.z, v.w)); }
+__device__ __forceinline__ uint32_t magmin4(uint4 v)
+{
+    return min_u16x2(min_u16x2(v.x & 0x7fff7fffu, v.y & 0x7fff7fffu), min_u16x2(v.z & 0x7fff7fffu, v.w & 0x7fff7fffu));
+}
+__device__ __forceinline__ float bf16x2_max_f(uint32_t m) { return fmax_nan(__uint_as_float(m << 16), __uint_as_float(m & 0xffff0000u)); }
+__device__ __forceinline__ float bf16x2_min_f(uint32_t m) { return fmin_nan(__uint_as_float(m << 16), __uint_as_float(m & 0xffff0000u)); }
+
+template <bool TEMP>
+__device__ __forceinline__ void tab_item(const SampleArgs &a, int64_t it, int row, int sub, const uint4 *rv,
+                                         const float *tab0, const g4s_params &p)
+{
+    const float NEG_INF = -__uint_as_float(0x7f800000u);
+    const float invT = TEMP ? a.params.inv_t(row) : 1.0f;
+    const int n = item_len<G4S_BF16>(a.vocab, sub);
+    bool ok = n == Geo<G4S_BF16>::ITEM;
+    // lane extremes: NaN-propagating maxima of all vectors; the magnitude
+    // minimum of the table vectors; the minimum of the polynomial vectors
+    uint32_t mx2 = bmax4(rv[0]);
+#pragma unroll
+    for (int j = 1; j < NVEC; j++) mx2 = bmax2_nan(mx2, bmax4(rv[j]));
+    const float lmx = bf16x2_max_f(mx2);
+    ok &= lmx == lmx;
+    if constexpr (TAB_NT > 0) {
+        uint32_t mg = magmin4(rv[0]);
+#pragma unroll
+        for (int j = 1; j < TAB_NT; j++) mg = min_u16x2(mg, magmin4(rv[j]));
+        ok &= min(mg & 0xffffu, mg >> 16) >= TAB_LOW;
+    }
+    if constexpr (TAB_NT < NVEC) {
+        uint32_t pmx = bmax4(rv[TAB_NT]), pmn = bmin4(rv[TAB_NT]);
+#pragma unroll
+        for (int j = TAB_NT + 1; j < NVEC; j++) {
+            pmx = bmax2_nan(pmx, bmax4(rv[j]));
+            pmn = bmin2_nan(pmn, bmin4(rv[j]));
+        }
+        ok &= (fabsf(__fmul_rn(bf16x2_max_f(pmx), a.invcap)) <= 1.0f) & (fabsf(__fmul_rn(bf16x2_min_f(pmn), a.invcap)) <= 1.0f);
+    }
+    // item maximum s(max v) from the table (softcap and temperature are monotone)
+    const float vmax = warp_max_redux(lmx == lmx ? lmx : 0.0f);
+    float m = tab_s2(__float_as_uint(vmax), tab0).y;
+    if (TEMP) m = __fmul_rn(m, invT);
+    float cc = 0.0f, S = 0.0f;
+    if (p.temperature > 0.0f) {
+        cc = __fmul_rn(m, G4_L2E);
+        const float2 t2 = make_float2(invT, invT), l2 = make_float2(G4_L2E, G4_L2E), nc = make_float2(-cc, -cc);
+        const float2 ic = make_float2(a.invcap, a.invcap), c2 = make_float2(a.softcap, a.softcap);
+        float2 acc0 = make_float2(0.0f, 0.0f), acc1 = acc0;
+        auto pair = [&](uint32_t w, float2 &acc, bool table) {
+            float2 v;
+            if (table) {
+                v = tab_s2(w, tab0);
+            } else {
+                v = make_float2(__uint_as_float(__byte_perm(w, 0u, 0x1044)), __uint_as_float(w & 0xffff0000u));
+                v = __fmul2_rn(tanh_poly2(__fmul2_rn(v, ic)), c2);
+            }
+            if (TEMP) v = __fmul2_rn(v, t2);
+            const float2 y = __ffma2_rn(v, l2, nc);
+            acc = __fadd2_rn(acc, make_float2(ex2_approx(y.x), ex2_approx(y.y)));
+        };
+#pragma unroll
+        for (int j = 0; j < NVEC; j++) {
+            const bool table = j < TAB_NT;
+            pair(rv[j].x, acc0, table);
+            pair(rv[j].y, acc1, table);
+            pair(rv[j].z, acc0, table);
+            pair(rv[j].w, acc1, table);
+        }
+        acc0 = __fadd2_rn(acc0, acc1);
+        S = acc0.x + acc0.y;
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) S += __shfl_xor_sync(FULLMASK, S, d);
+    }
+    const bool redo = !__all_sync(FULLMASK, ok);
+    if ((threadIdx.x & 31) == 0) a.istat[it] = make_float4(redo ? NEG_INF : m, cc, S, redo ? 1.0f : 0.0f);
+}
+
+__global__ void __launch_bounds__(TAB_THREADS, G4S_TAB_CPS) full_tab_kernel(SampleArgs a)
+{
+    constexpr int ITEM = Geo<G4S_BF16>::ITEM;
+    constexpr int WPB = TAB_THREADS / 32;
+    extern __shared__ __align__(16) uint4 dsm[];  // ring, then the table
+    {
+        uint4 *dst = dsm + TAB_RING_BYTES / 16;
+        const uint4 *src = reinterpret_cast<const uint4 *>(a.sc_table);
+        for (int i = threadIdx.x; i < SC_TAB_BYTES / 16; i += TAB_THREADS) dst[i] = __ldcg(src + i);
+    }
+    const float *tab0 = reinterpret_cast<const float *>(dsm + TAB_RING_BYTES / 16) - TAB_LOW;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int ipr = (a.vocab + ITEM - 1) / ITEM;
+    const int64_t nitems = (int64_t)a.rows * ipr;
+    const int64_t nw = (int64_t)gridDim.x * WPB;
+    const int64_t it0 = (int64_t)blockIdx.x * WPB + wib;
+    const int step_row = (int)(nw / ipr), step_sub = (int)(nw % ipr);
+    struct Cursor {
+        int row, sub;
+    };
+    auto advance = [&](Cursor &c) {
+        c.sub += step_sub;
+        c.row += step_row;
+        if (c.sub >= ipr) {
+            c.sub -= ipr;
+            c.row++;
+        }
+    };
+    uint4 *wring = dsm + wib * STAGES * NVEC * 32;
+    auto issue = [&](int64_t i, const Cursor &c, int stage) {
+        if (i >= nitems) return;
+        const int n = item_len<G4S_BF16>(a.vocab, c.sub);
+        const char *src = (const char *)a.logits + ((int64_t)c.row * a.row_stride + (int64_t)c.sub * ITEM) * 2;
+        uint4 *dst = wring + stage * NVEC * 32;
+#pragma unroll
+        for (int j = 0; j < NVEC; j++) {
+            const int e0 = item_pos<G4S_BF16>(j, 0, lane);
+            if (e0 + 8 <= n) cp_async16(dst + j * 32 + lane, src + (int64_t)e0 * 2);
+        }
+    };
+    Cursor cur{(int)(it0 / ipr), (int)(it0 % ipr)};
+    Cursor nxt = cur;
+#pragma unroll
+    for (int st = 0; st < STAGES - 1; st++) {
+        issue(it0 + st * nw, nxt, st);
+        cp_async_commit();
+        advance(nxt);
+    }
+    __syncthreads();  // the table is in shared memory
+    int stage = 0;
+    for (int64_t it = it0; it < nitems; it += nw) {
+        issue(it + (STAGES - 1) * nw, nxt, stage == 0 ? STAGES - 1 : stage - 1);
+        cp_async_commit();
+        advance(nxt);
+        cp_async_wait<STAGES - 1>();  // this lane's copies of item `it` have landed
+        const uint4 *src = wring + stage * NVEC * 32;
+        uint4 rv[NVEC];
+#pragma unroll
+        for (int j = 0; j < NVEC; j++) rv[j] = src[j * 32 + lane];
+        const g4s_params p = a.params.get(cur.row);
+        if (p.top_k <= 0 || p.top_k >= a.vocab) {
+            if (p.temperature > 0.0f && p.temperature != 1.0f)
+                tab_item<true>(a, it, cur.row, cur.sub, rv, tab0, p);
+            else
+                tab_item<false>(a, it, cur.row, cur.sub, rv, tab0, p);
+        }
+        advance(cur);
+        stage = stage + 1 == STAGES ? 0 : stage + 1;
+    }
+    cp_async_wait<0>();
 }
 
 // 2^d for a double d <= ~0: 2^round(d) * ex2(d - round(d)) (|f| <= 1/2, so the
@@ -832,6 +1060,24 @@ __global__ void __launch_bounds__(NTHREADS) full_probs_kernel(SampleArgs a)
     }
 }
 
+// Per-device set-up of the table kernel: its dynamic shared memory (ring + table).
+static bool tab_setup()
+{
+    static bool ready[MAX_DEVICES] = {};
+    const int dev = current_device();
+    if (dev >= 0 && dev < MAX_DEVICES && ready[dev]) return true;
+    if (cudaFuncSetAttribute(full_tab_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TAB_DYN_SMEM) != cudaSuccess)
+        return false;
+    if (dev >= 0 && dev < MAX_DEVICES) ready[dev] = true;
+    return true;
+}
+
+cudaError_t launch_softcap_table(float cap, float invcap, float *tab, cudaStream_t s)
+{
+    softcap_table_kernel<<<(SC_TAB_N + 255) / 256, 256, 0, s>>>(cap, invcap, tab);
+    return cudaGetLastError();
+}
+
 template <int DT, bool VEC>
 static cudaError_t launch_full_t(const SampleArgs &a, cudaStream_t s, bool probs)
 {
@@ -839,11 +1085,27 @@ static cudaError_t launch_full_t(const SampleArgs &a, cudaStream_t s, bool probs
     const int ipr = (a.vocab + ITEM - 1) / ITEM;
     const int64_t nitems = (int64_t)a.rows * ipr;
     if (!probs) {
-        constexpr int wpb = STREAM_THREADS / 32;
-        int64_t blocks = (nitems + wpb - 1) / wpb;
-        if (a.persist_blocks > 0 && blocks > a.persist_blocks) blocks = a.persist_blocks;
-        full_stream_kernel<DT, VEC><<<(unsigned)blocks, STREAM_THREADS, 0, s>>>(a);
-        cudaError_t e = cudaGetLastError();
+        cudaError_t e;
+        if constexpr (DT == G4S_BF16 && VEC) {
+            if (a.sc_table) {
+                if (!tab_setup()) return cudaGetLastError();
+                constexpr int wpb = TAB_THREADS / 32;
+                int64_t blocks = (nitems + wpb - 1) / wpb;
+                if (a.persist_blocks > 0 && blocks > a.persist_blocks) blocks = a.persist_blocks;
+                full_tab_kernel<<<(unsigned)blocks, TAB_THREADS, TAB_DYN_SMEM, s>>>(a);
+            } else {
+                constexpr int wpb = STREAM_THREADS / 32;
+                int64_t blocks = (nitems + wpb - 1) / wpb;
+                if (a.persist_blocks > 0 && blocks > a.persist_blocks) blocks = a.persist_blocks;
+                full_stream_kernel<DT, VEC><<<(unsigned)blocks, STREAM_THREADS, 0, s>>>(a);
+            }
+        } else {
+            constexpr int wpb = STREAM_THREADS / 32;
+            int64_t blocks = (nitems + wpb - 1) / wpb;
+            if (a.persist_blocks > 0 && blocks > a.persist_blocks) blocks = a.persist_blocks;
+            full_stream_kernel<DT, VEC><<<(unsigned)blocks, STREAM_THREADS, 0, s>>>(a);
+        }
+        e = cudaGetLastError();
         if (e != cudaSuccess || a.stream_only) return e;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)a.rows);
@@ -870,11 +1132,14 @@ static cudaError_t launch_full_dt(const SampleArgs &a, bool vec, cudaStream_t s,
 
 int full_item_logits(int dtype) { return dtype == G4S_F32 ? Geo<G4S_F32>::ITEM : Geo<G4S_BF16>::ITEM; }
 
-int full_stream_blocks_per_sm(int dtype, bool vec)
+int full_stream_blocks_per_sm(int dtype, bool vec, bool tab)
 {
     int n = 0;
     cudaError_t e;
-    if (dtype == G4S_F32)
+    if (tab && dtype == G4S_BF16 && vec)
+        e = tab_setup() ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, full_tab_kernel, TAB_THREADS, TAB_DYN_SMEM)
+                        : cudaGetLastError();
+    else if (dtype == G4S_F32)
         e = vec ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, full_stream_kernel<G4S_F32, true>, STREAM_THREADS, 0)
                 : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, full_stream_kernel<G4S_F32, false>, STREAM_THREADS, 0);
     else

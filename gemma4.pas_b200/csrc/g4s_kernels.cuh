@@ -66,6 +66,9 @@ struct SampleArgs {
     const int32_t *gcnts;      //   and their lengths [gworld][rows]
     int32_t gworld;
     int *err;                  // device error flag: a bounded wait ran out (nullable)
+    const float *sc_table;     // full path, bf16 rows: the softcap table of `softcap` (nullable)
+    int64_t wait_limit;        // 0: the kernels' own poll limits; > 0: test hook, every
+                               //   bounded wait gives up after this many non-blocking polls
 };
 
 // Single-row latency path of the top-K selection: one cluster of TOPK_CLUSTER
@@ -115,7 +118,14 @@ cudaError_t launch_shard_merge(const SampleArgs &a, cudaStream_t s);
 bool topk_cluster_available();
 // Logits per item of the full-path streaming kernel (one float4 of statistics each).
 int full_item_logits(int dtype);
-// Resident CTAs per SM of the full-path streaming kernel (for its persistent grid).
-int full_stream_blocks_per_sm(int dtype, bool vec);
+// Resident CTAs per SM of the full-path streaming kernel (for its persistent
+// grid); tab: the variant with the bf16 softcap table.
+int full_stream_blocks_per_sm(int dtype, bool vec, bool tab);
+// The bf16 softcap table (full path): SC_TABLE_BYTES of device memory, built
+// for one softcap value by launch_softcap_table; usable for softcaps in
+// (0, SC_TABLE_MAX_CAP].
+constexpr int SC_TABLE_BYTES = 12816;
+constexpr float SC_TABLE_MAX_CAP = 55.0f;
+cudaError_t launch_softcap_table(float cap, float invcap, float *tab, cudaStream_t s);
 
 }  // namespace g4s

@@ -14,7 +14,10 @@
 // cannot use the array's name as a device address (in host code it names a
 // host-side stand-in), so the first call on each device, with that device
 // current, looks its device address up with cudaGetSymbolAddress and caches
-// it.  Make that first call before any stream capture.
+// it.  Make that first call before any stream capture.  The cached address
+// belongs to the device's context at that time; cudaDeviceReset ends that
+// context and leaves the cache stale, so a process that resets a device must
+// not call this entry point on that device again.
 //
 // All calls share the one array and it keeps the last call's contents: each
 // call clears the per-row arrival counters it relies on, and calls that
@@ -88,7 +91,7 @@ extern "C" int32_t g4s_sample_topk_noalloc(const void *logits, int32_t dtype, in
     }
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int64_t nbig = (vocab + 8191) / 8192, nsmall = (vocab + 2047) / 2048;
+    const int64_t nbig = ((int64_t)vocab + 8191) / 8192, nsmall = ((int64_t)vocab + 2047) / 2048;
     int ept = ((int64_t)rows * nbig < 2LL * sms && nsmall <= 1024) ? 8 : 32;
     if (ept == 8 && (int64_t)rows * nsmall > NA_MAX_LISTS) ept = 32;
     const int64_t nch = ept == 8 ? nsmall : nbig;

@@ -363,10 +363,25 @@ __device__ int merge_lists(int K, TopkSmem &sm, const uint64_t *C, int64_t lstri
     int total;
     int off = block_excl_scan(cnt, &total, sm.scan);
     if (total <= CAP2 / 2) {
+        // every thread copies: entry i comes from the last list whose prefix
+        // starts at or before i (list start offsets in the upper half of sm.L,
+        // which the copy does not reach)
+        int *loff = reinterpret_cast<int *>(sm.L + CAP2 / 2);
 #pragma unroll
         for (int r = 0; r < CPT; r++) {
-            const uint64_t *list = C + (tid * CPT + r) * lstride;
-            for (int i = 0; i < pc[r]; i++) sm.L[off++] = __ldcg(&list[i]);
+            const int c = tid * CPT + r;
+            if (c < nch) loff[c] = off;
+            off += pc[r];
+        }
+        __syncthreads();
+        for (int i = tid; i < total; i += NTHREADS) {
+            int lo = 0, hi = nch - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (loff[mid] <= i) lo = mid;
+                else hi = mid - 1;
+            }
+            sm.L[i] = __ldcg(&C[lo * lstride + (i - loff[lo])]);
         }
         __syncthreads();
         sort_list_desc(sm, total);
@@ -415,6 +430,20 @@ __device__ void topk_merge(const SampleArgs &a, int row, const g4s_params &p, To
         finish_row(a, row, p, kw, sm);
     }
     if (tid == 0) a.counters_topk[row] = 0;  // ready for the next call
+}
+
+// A row in one chunk: the chunk's sorted top min(K, valid) list in sm.L is the
+// row's, so it is published or sampled without the workspace round trip.
+__device__ __forceinline__ void finish_single_chunk(const SampleArgs &a, int row, const g4s_params &p, int m,
+                                                    TopkSmem &sm)
+{
+    const int tid = threadIdx.x;
+    if (a.list_out) {
+        for (int i = tid; i < m; i += NTHREADS) a.list_out[(int64_t)row * KMAX + i] = sm.L[i];
+        if (tid == 0) a.list_cnt[row] = m;
+    } else {
+        finish_row(a, row, p, m, sm);
+    }
 }
 
 // Vocabulary-sharded mode, after the all-gather: one CTA per row merges the
@@ -673,19 +702,29 @@ __device__ __forceinline__ int chunk_select_stream(const SampleArgs &a, int row,
     const float qnan = __uint_as_float(0x7fc00000u);
     uint32_t thr = 1;  // keys >= thr are candidates (key 0: not a candidate)
     int cnt = 0;       // buffer fill, uniform (read after each tile's barrier)
-    bool timed_out = false;
+    bool timed_out = false;  // this thread's wait for a tile ran out
+    bool broken = false;     // block-uniform: some thread's wait ran out
+    int issued = min(NSLOT, ntiles);  // tiles [0, issued) have been issued
     for (int t = 0; t < ntiles; t++) {
         const int slot = t % NSLOT, base = t * STREAM_TILE, cov = covered(t);
-        {
+        if (!broken) {
             // bounded wait for the tile (on a timeout: the error flag, and the
             // stale slot is read; every thread keeps the same control flow)
             const uint32_t bar = bars + 8 * slot, par = (uint32_t)((t / NSLOT) & 1);
             uint32_t ok = 0;
-            for (long k = 0; k < STREAM_WAIT_LIMIT && !ok; k++)
-                asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-                             : "=r"(ok)
-                             : "r"(bar), "r"(par)
-                             : "memory");
+            if (a.wait_limit > 0) {
+                for (int64_t k = 0; k < a.wait_limit && !ok; k++)
+                    asm volatile("{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                                 : "=r"(ok)
+                                 : "r"(bar), "r"(par)
+                                 : "memory");
+            } else {
+                for (long k = 0; k < STREAM_WAIT_LIMIT && !ok; k++)
+                    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                                 : "=r"(ok)
+                                 : "r"(bar), "r"(par)
+                                 : "memory");
+            }
             timed_out |= !ok;
         }
         float x[NV * VW];
@@ -727,14 +766,36 @@ __device__ __forceinline__ int chunk_select_stream(const SampleArgs &a, int row,
                 }
             }
         }
-        __syncthreads();  // every thread is done with the slot
+        // every thread is done with the slot; after a wait ran out no tile is
+        // issued any more (a refill could arrive on a phase still pending)
+        broken = __syncthreads_or(timed_out);
         cnt = sm.misc[3];
-        if (tid == 0 && t + NSLOT < ntiles) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic reads before the async refill
-            issue(t + NSLOT);
+        if (!broken && t + NSLOT < ntiles) {
+            if (tid == 0) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic reads before the async refill
+                issue(t + NSLOT);
+            }
+            issued = t + NSLOT + 1;
         }
     }
-    if (timed_out && a.err) atomicExch(a.err, 1);
+    if (broken) {
+        // drain: no bulk copy may still be writing this CTA's shared memory when
+        // it exits.  The last tile issued to each slot is waited for with the
+        // normal limit (its phase completes after every earlier one of the slot).
+        if (tid == 0) {
+            for (int t = max(0, issued - NSLOT); t < issued; t++) {
+                const uint32_t bar = bars + 8 * (t % NSLOT), par = (uint32_t)((t / NSLOT) & 1);
+                uint32_t ok = 0;
+                for (long k = 0; k < STREAM_WAIT_LIMIT && !ok; k++)
+                    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                                 : "=r"(ok)
+                                 : "r"(bar), "r"(par)
+                                 : "memory");
+            }
+            if (a.err) atomicExch(a.err, 1);
+        }
+        __syncthreads();
+    }
     // at most NTHREADS entries for the one-pass rank sort, then the first K
     if (cnt > NTHREADS) cnt = stream_cut_to(cnt, K, NTHREADS, thr, sm);
     sort_list_desc(sm, cnt);
@@ -753,6 +814,10 @@ __global__ void __launch_bounds__(NTHREADS, 3) topk_stream_kernel(SampleArgs a)
     const int64_t c0 = (int64_t)chunk * a.chunk;
     const int n = (int)min((int64_t)a.chunk, (int64_t)a.vocab - c0);
     const int m = chunk_select_stream<DT>(a, row, c0, n, K, sm, stream_ring);
+    if (a.nch == 1) {
+        finish_single_chunk(a, row, p, m, sm);
+        return;
+    }
     uint64_t *out = a.cand + ((int64_t)row * a.nch + chunk) * KMAX;
     for (int i = tid; i < m; i += NTHREADS) out[i] = sm.L[i];
     if (tid == 0) a.cand_cnt[(int64_t)row * a.nch + chunk] = m;
@@ -778,6 +843,10 @@ __global__ void __launch_bounds__(NTHREADS) topk_chunk_kernel(SampleArgs a)
     const int64_t c0 = (int64_t)chunk * a.chunk;
     const int n = (int)min((int64_t)a.chunk, (int64_t)a.vocab - c0);
     const int m = chunk_select<DT, EPT, VEC>(a, row, c0, n, K, sm);
+    if (a.nch == 1) {
+        finish_single_chunk(a, row, p, m, sm);
+        return;
+    }
     uint64_t *out = a.cand + ((int64_t)row * a.nch + chunk) * KMAX;
     for (int i = tid; i < m; i += NTHREADS) out[i] = sm.L[i];
     if (tid == 0) a.cand_cnt[(int64_t)row * a.nch + chunk] = m;

@@ -58,6 +58,7 @@ SIGNATURES = {
     "g4s_sample_topk_noalloc": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_int64, POINTER(Params),
                                           c_float, c_void_p, c_void_p, c_void_p]),
     "g4s_device_status": (c_int32, [c_void_p]),
+    "g4s_set_wait_limit": (c_int32, [c_void_p, c_int64]),
     "g4s_q4_repack": (c_int32, [c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
     "g4s_lmhead_sample": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_float, c_void_p, c_void_p,
                                     c_int32, POINTER(Params), c_int32, c_float, c_void_p, c_void_p,
@@ -129,7 +130,11 @@ def make_params(temperature=1.0, top_k=64, top_p=0.95, repetition_penalty=1.0) -
 
 
 def params_array(rows):
-    """ctypes array of Params from a sequence of (T, K, P) or Params."""
+    """ctypes array of Params from a sequence of (T, K, P) or Params.  An array
+    this function made is passed through unchanged, so a caller that samples
+    the same per-row settings every step converts them once."""
+    if isinstance(rows, ctypes.Array) and rows._type_ is Params:
+        return rows
     arr = (Params * len(rows))()
     for i, r in enumerate(rows):
         arr[i] = r if isinstance(r, Params) else make_params(*r)

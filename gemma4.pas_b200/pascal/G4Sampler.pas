@@ -105,6 +105,11 @@ function g4s_sample_topk_noalloc(Logits: Pointer; DType, Rows, Vocab: Int32;
 { G4S_ERR_TIMEOUT when a kernel gave up a bounded wait since the last check. }
 function g4s_device_status(Ctx: PG4SCtx): Int32; cdecl; external G4SLib;
 
+{ Test hook: Polls > 0 makes the streaming top-K pass's bounded waits give up
+  after that many polls (0 = normal limits). }
+function g4s_set_wait_limit(Ctx: PG4SCtx; Polls: Int64): Int32; cdecl;
+  external G4SLib;
+
 { LM head (CpuMatVecQ4, src/Gemma4.Tensors.pas:546-590) + DoSample: TQ4Block
   weights repacked once on the device, then one call per step. }
 function g4s_q4_repack(Blocks: Pointer; Vocab, Hidden: Int32; Nibbles: Pointer;

@@ -104,7 +104,8 @@ int32_t g4s_version(void);
 void g4s_params_defaults(g4s_params *p);
 
 /* Creates a sampler on CUDA device `device` able to take up to max_rows rows of
-   up to max_vocab logits per call.  flags: reserved, pass 0.
+   up to max_vocab logits per call.  flags: 0, or G4S_FLAG_HOST_STAGING to
+   allocate g4s_sample_host's device staging here rather than on its first call.
    Replaces the sampler state TModel keeps implicitly (FLogits buffer and the
    temporary arrays DoSample allocates per call, src/Gemma4.Model.pas:2740-2752). */
 int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t flags,
@@ -181,8 +182,12 @@ int32_t g4s_sample_host(g4s_ctx *ctx, const void *host_logits, int32_t dtype, in
  * Scratch comes from one fixed array inside the library (held on every GPU
  * that loads it until exit).  The first call on a device, with that device
  * current, looks up the array's device address (cudaGetSymbolAddress): make
- * that first call before any stream capture.  All calls share the array, so
- * calls that overlap on the GPU race; issue them one after another.
+ * that first call before any stream capture.  The cached address belongs to
+ * the device's CUDA context as it was then: after cudaDeviceReset it is stale
+ * and a later call on that device would hand the kernel a dead address, so a
+ * process that resets a device must not call this entry point on it again.
+ * All calls share the array, so calls that overlap on the GPU race; issue
+ * them one after another.
  * Sizes above G4S_NOALLOC_MAX_ROWS rows or G4S_NOALLOC_MAX_LISTS lists return
  * G4S_ERR_CAPACITY; errors are read with g4s_last_error(NULL).
  */
@@ -215,6 +220,14 @@ int32_t g4s_sample_topk_noalloc(const void *logits, int32_t dtype, int32_t rows,
 /* Waits for the device, then reports whether a kernel of this context gave up
    a bounded wait (G4S_ERR_TIMEOUT; the flag is cleared) since the last check. */
 int32_t g4s_device_status(g4s_ctx *ctx);
+
+/* Test hook, no counterpart in the reference: with polls > 0 every bounded
+   wait of the streaming top-K pass (rows >= 64) gives up after `polls`
+   non-blocking polls instead of its own limit, so a test can make one run
+   out: the kernel then stops refilling, drains the copies it issued, sets the
+   flag g4s_device_status reports and returns (its tokens are invalid).
+   0 restores the normal limits. */
+int32_t g4s_set_wait_limit(g4s_ctx *ctx, int64_t polls);
 
 int32_t g4s_q4_repack(const uint8_t *blocks, int32_t vocab, int32_t hidden, uint8_t *nibbles, uint16_t *scales,
                       void *stream);

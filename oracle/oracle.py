@@ -82,6 +82,12 @@ def load():
     lib.ref_matvec_q4.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int32]
     lib.ref_matvec_q4_f64.restype = None
     lib.ref_matvec_q4_f64.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int32]
+    lib.ref_matvec_q4_mt.restype = None
+    lib.ref_matvec_q4_mt.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32]
+    lib.ref_quantize_q8_1.restype = None
+    lib.ref_quantize_q8_1.argtypes = [c_void_p, c_int32, c_void_p, c_void_p]
+    lib.ref_matvec_q4q8.restype = None
+    lib.ref_matvec_q4q8.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32]
     _lib = lib
     return lib
 
@@ -153,6 +159,38 @@ def matvec_q4(blocks: np.ndarray, vec: np.ndarray, rows: int, cols: int, f64=Fal
     blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
     out = np.empty(rows, dtype=np.float64 if f64 else np.float32)
     (lib.ref_matvec_q4_f64 if f64 else lib.ref_matvec_q4)(_ptr(blocks), _ptr(vec), _ptr(out), rows, cols)
+    return out
+
+
+def matvec_q4_mt(blocks: np.ndarray, vec: np.ndarray, rows: int, cols: int, nthreads: int = 1):
+    """CpuMatVecQ4 (src/Gemma4.Tensors.pas:546-590) on `nthreads` threads
+    (same per-row arithmetic as matvec_q4)."""
+    lib = load()
+    vec = np.ascontiguousarray(vec, dtype=np.float32)
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    out = np.empty(rows, dtype=np.float32)
+    lib.ref_matvec_q4_mt(_ptr(blocks), _ptr(vec), _ptr(out), rows, cols, nthreads)
+    return out
+
+
+def quantize_q8_1(x: np.ndarray):
+    """gemma4_quantize_q8.comp: (int8 qs [n], fp16 bits ds [n/32, 2] = (d, d*sum(q)))."""
+    lib = load()
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    qs = np.empty(x.shape[0], dtype=np.int8)
+    ds = np.empty((x.shape[0] // 32, 2), dtype=np.uint16)
+    lib.ref_quantize_q8_1(_ptr(x), x.shape[0], _ptr(qs), _ptr(ds))
+    return qs, ds
+
+
+def matvec_q4q8(blocks: np.ndarray, vec: np.ndarray, rows: int, cols: int, nthreads: int = 1):
+    """The reference's GPU LM head: Q8_1 activations and the DP4A matvec
+    (gemma4_quantize_q8.comp, gemma4_matvec_q4q8.comp)."""
+    lib = load()
+    qs, ds = quantize_q8_1(vec)
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    out = np.empty(rows, dtype=np.float32)
+    lib.ref_matvec_q4q8(_ptr(blocks), _ptr(qs), _ptr(ds), _ptr(out), rows, cols, nthreads)
     return out
 
 

@@ -630,3 +630,167 @@ void ref_rmsnorm(const float *x, const float *w, float *out, int32_t n, float ep
     const float scale = 1.0f / rms;
     for (int32_t i = 0; i < n; i++) out[i] = (x[i] * scale) * w[i];
 }
+
+/* ------------------------------------------------------------------------ */
+/* Threaded driver of ref_matvec_q4: vocabulary rows split among threads,    */
+/* each row's serial fp32 sum unchanged (results identical to one thread).   */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+    const uint8_t *blocks;
+    const float *vec;
+    float *dst;
+    int32_t r0, r1, cols;
+    const int8_t *qs;
+    const uint16_t *ds;
+} mv_job;
+
+static void *mv_q4_worker(void *arg)
+{
+    mv_job *j = (mv_job *)arg;
+    size_t bpr = (size_t)(j->cols / 32);
+    ref_matvec_q4(j->blocks + (size_t)j->r0 * bpr * 18u, j->vec, j->dst + j->r0, j->r1 - j->r0, j->cols);
+    return NULL;
+}
+
+static void run_mv(mv_job *base, int32_t rows, int32_t nthreads, void *(*fn)(void *))
+{
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > rows) nthreads = rows > 0 ? rows : 1;
+    mv_job *jobs = (mv_job *)calloc((size_t)nthreads, sizeof(mv_job));
+    pthread_t *th = (pthread_t *)calloc((size_t)nthreads, sizeof(pthread_t));
+    for (int32_t t = 0; t < nthreads; t++) {
+        jobs[t] = *base;
+        jobs[t].r0 = (int32_t)((int64_t)rows * t / nthreads);
+        jobs[t].r1 = (int32_t)((int64_t)rows * (t + 1) / nthreads);
+    }
+    for (int32_t t = 1; t < nthreads; t++) pthread_create(&th[t], NULL, fn, &jobs[t]);
+    fn(&jobs[0]);
+    for (int32_t t = 1; t < nthreads; t++) pthread_join(th[t], NULL);
+    free(jobs);
+    free(th);
+}
+
+void ref_matvec_q4_mt(const uint8_t *blocks, const float *vec, float *dst, int32_t rows, int32_t cols,
+                      int32_t nthreads)
+{
+    mv_job b = {blocks, vec, dst, 0, rows, cols, NULL, NULL};
+    run_mv(&b, rows, nthreads, mv_q4_worker);
+}
+
+/* ------------------------------------------------------------------------ */
+/* The reference's GPU LM head (RecordMatVecQ4 takes it whenever the device  */
+/* has integer dot products, src/Gemma4.Compute.pas:1037-1044):              */
+/*   Q8_1 activations, shaders/src/gemma4_quantize_q8.comp:30-68 -- per      */
+/*   32-value block d = amax / 127, q = clamp(round(v * (1/d)), -127, 127),  */
+/*   stored d and s = d * sum(q) as fp16 (packHalf2x16);                     */
+/*   the DP4A matvec, shaders/src/gemma4_matvec_q4q8.comp:58-126 -- per      */
+/*   block idot = sum(nibble * q) over the 32 values (exact integer), then   */
+/*   d4 * (d8 * idot - 8 * s8); lane l of a 32-lane row group sums blocks    */
+/*   l, l + 32 (pairs per iteration), then the group is reduced.             */
+/* GLSL leaves the rounding of round() at exact halves, of packHalf2x16 and  */
+/* the order of subgroupClusteredAdd to the implementation; this            */
+/* restatement rounds halves away from zero, packs with round-to-nearest-    */
+/* even and reduces as a butterfly (offsets 16, 8, 4, 2, 1), with no FMA     */
+/* contraction.                                                              */
+/* ------------------------------------------------------------------------ */
+
+/* fp32 -> fp16 bits, round to nearest even (finite inputs; overflow to inf). */
+static uint16_t f32_to_f16_rne(float f)
+{
+    uint32_t b = f32_bits(f), sign = (b >> 16) & 0x8000u;
+    uint32_t ab = b & 0x7FFFFFFFu;
+    if (ab >= 0x477FF000u) return (uint16_t)(sign | 0x7C00u); /* rounds to >= 65520: inf */
+    if (ab < 0x33000001u) return (uint16_t)sign;             /* below half the smallest subnormal */
+    int32_t e = (int32_t)(ab >> 23) - 127;
+    uint32_t man = (ab & 0x7FFFFFu) | 0x800000u;
+    int32_t shift = e >= -14 ? 13 : 13 + (-14 - e);          /* subnormal results shift further */
+    uint32_t keep = man >> shift, rem = man & ((1u << shift) - 1u), half = 1u << (shift - 1);
+    if (rem > half || (rem == half && (keep & 1u))) keep++;
+    uint32_t out;
+    if (e >= -14) out = (uint32_t)((e + 15) << 10) + (keep - 0x400u); /* carry may bump the exponent */
+    else out = keep;
+    return (uint16_t)(sign | out);
+}
+
+static float f16_to_f32_exact(uint16_t h)
+{
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16, ex = (h >> 10) & 0x1Fu, man = h & 0x3FFu;
+    if (ex == 0) {
+        float v = (float)man * 5.9604644775390625e-08f; /* man * 2^-24, exact */
+        return sign ? -v : v;
+    }
+    if (ex == 0x1F) return bits_f32(sign | 0x7F800000u | (man << 13));
+    return bits_f32(sign | ((ex + 112u) << 23) | (man << 13));
+}
+
+void ref_quantize_q8_1(const float *x, int32_t n, int8_t *qs, uint16_t *ds)
+{
+    for (int32_t b = 0; b < n / 32; b++) {
+        const float *v = x + (size_t)b * 32u;
+        float amax = 0.0f;
+        for (int32_t i = 0; i < 32; i++) {
+            float a = fabsf(v[i]);
+            if (a > amax) amax = a;
+        }
+        float d = amax / 127.0f;
+        float id = d != 0.0f ? 1.0f / d : 0.0f;
+        int32_t qsum = 0;
+        for (int32_t i = 0; i < 32; i++) {
+            float t = v[i] * id;
+            int32_t q = (int32_t)roundf(t);
+            if (q < -127) q = -127;
+            if (q > 127) q = 127;
+            qs[(size_t)b * 32u + (size_t)i] = (int8_t)q;
+            qsum += q;
+        }
+        ds[2 * b] = f32_to_f16_rne(d);
+        ds[2 * b + 1] = f32_to_f16_rne(d * (float)qsum);
+    }
+}
+
+static float q4q8_block(const uint8_t *blk, const int8_t *q8, const uint16_t *ds8)
+{
+    /* interleaved reference block: byte j = value 2j (low nibble), 2j+1 (high) */
+    int32_t idot = 0;
+    for (int32_t j = 0; j < 16; j++) {
+        idot += (int32_t)(blk[2 + j] & 0x0F) * (int32_t)q8[2 * j];
+        idot += (int32_t)(blk[2 + j] >> 4) * (int32_t)q8[2 * j + 1];
+    }
+    float d4 = f16_to_f32_exact((uint16_t)(blk[0] | (blk[1] << 8)));
+    float d8 = f16_to_f32_exact(ds8[0]), s8 = f16_to_f32_exact(ds8[1]);
+    float a = d8 * (float)idot;
+    float c = 8.0f * s8;
+    return d4 * (a - c);
+}
+
+static void *mv_q4q8_worker(void *arg)
+{
+    mv_job *j = (mv_job *)arg;
+    int32_t bpr = j->cols / 32;
+    for (int32_t r = j->r0; r < j->r1; r++) {
+        const uint8_t *rs = j->blocks + (size_t)r * (size_t)bpr * 18u;
+        float lane[32];
+        for (int32_t l = 0; l < 32; l++) {
+            float sum = 0.0f;
+            int32_t b = l;
+            for (; b + 32 < bpr; b += 64) {
+                sum += q4q8_block(rs + (size_t)b * 18u, j->qs + (size_t)b * 32u, j->ds + 2 * b);
+                sum += q4q8_block(rs + (size_t)(b + 32) * 18u, j->qs + (size_t)(b + 32) * 32u, j->ds + 2 * (b + 32));
+            }
+            if (b < bpr) sum += q4q8_block(rs + (size_t)b * 18u, j->qs + (size_t)b * 32u, j->ds + 2 * b);
+            lane[l] = sum;
+        }
+        for (int32_t off = 16; off > 0; off >>= 1)
+            for (int32_t l = 0; l < off; l++) lane[l] = lane[l] + lane[l + off];
+        j->dst[r] = lane[0];
+    }
+    return NULL;
+}
+
+void ref_matvec_q4q8(const uint8_t *blocks, const int8_t *qs, const uint16_t *ds, float *dst, int32_t rows,
+                     int32_t cols, int32_t nthreads)
+{
+    mv_job b = {blocks, NULL, dst, 0, rows, cols, qs, ds};
+    run_mv(&b, rows, nthreads, mv_q4q8_worker);
+}
+

@@ -128,6 +128,20 @@ void ref_matvec_q4(const uint8_t *blocks, const float *vec, float *dst, int32_t 
 void ref_matvec_q4_f64(const uint8_t *blocks, const float *vec, double *dst, int32_t rows,
                        int32_t cols);
 
+/* ref_matvec_q4 with the vocabulary rows split among nthreads threads
+   (every row's arithmetic unchanged). */
+void ref_matvec_q4_mt(const uint8_t *blocks, const float *vec, float *dst, int32_t rows,
+                      int32_t cols, int32_t nthreads);
+
+/* The reference's GPU LM head (the DP4A path RecordMatVecQ4 takes on devices
+   with integer dot products, src/Gemma4.Compute.pas:1037-1044):
+   ref_quantize_q8_1 restates shaders/src/gemma4_quantize_q8.comp (per 32
+   values: int8 qs and fp16 (d, s) in ds[2 * block]); ref_matvec_q4q8 restates
+   shaders/src/gemma4_matvec_q4q8.comp on the interleaved blocks. */
+void ref_quantize_q8_1(const float *x, int32_t n, int8_t *qs, uint16_t *ds);
+void ref_matvec_q4q8(const uint8_t *blocks, const int8_t *qs, const uint16_t *ds, float *dst,
+                     int32_t rows, int32_t cols, int32_t nthreads);
+
 /* Final RMSNorm (src/Gemma4.Layers.pas:142-175), the LM head's input. */
 void ref_rmsnorm(const float *x, const float *w, float *out, int32_t n, float eps);
 

@@ -61,6 +61,7 @@ def test_null_context_calls_fail_cleanly(g4):
     assert lib.g4s_destroy(None) == g4.OK
     assert lib.g4s_last_error(None) is not None
     assert lib.g4s_workspace_bytes(None) == 0
+    assert lib.g4s_set_wait_limit(None, 1) == g4.ERR_ARG
 
 
 def test_create_without_gpu_reports_unavailable(g4):

@@ -123,3 +123,50 @@ def test_lmhead_with_fused_final_norm(g4, torch_cuda, oracle):
     bound = 2.0 ** -9 * (np.abs(xn) @ np.abs(W).T) + 1e-5
     assert (np.abs(lg - want) <= bound).all()
     check_topk_rows(oracle, lg, F32, prm, CAP, u, {"tokens": tok})
+
+
+def test_lmhead_agreement_with_reference_paths(g4, torch_cuda, oracle):
+    # The same C4 inputs through the reference's own LM-head arithmetic -- the
+    # serial fp32 CpuMatVecQ4 (src/Gemma4.Tensors.pas:546-590) and the Q8_1 +
+    # DP4A shaders its GPU path uses (gemma4_quantize_q8.comp,
+    # gemma4_matvec_q4q8.comp) -- then the oracle's DoSample on those logits.
+    # The three arithmetics round differently (fp16 operands here, fp32 and
+    # int8 activations there), so survivor sets and tokens are compared as
+    # agreement counts; the fp32 path must agree on nearly every survivor.
+    import os
+
+    torch = torch_cuda
+    rows, hidden, vocab = 64, 2560, 262144
+    h, blocks = synth.c4_inputs(rows, hidden, vocab)
+    u = synth.uniforms(rows, 0xC4, 2)
+    prm = g4.make_params(1.0, 64, 0.95)
+    bd = torch.from_numpy(blocks).cuda()
+    nib = torch.empty(vocab * hidden // 2, dtype=torch.uint8, device="cuda")
+    sc = torch.empty(vocab * hidden // 32, dtype=torch.int16, device="cuda")
+    g4.q4_repack(bd.data_ptr(), vocab, hidden, nib.data_ptr(), sc.data_ptr())
+    hd, ud = torch.from_numpy(h).cuda(), torch.from_numpy(u).cuda()
+    out = torch.full((rows,), -5, dtype=torch.int32, device="cuda")
+    cid = torch.full((rows, 64), -9, dtype=torch.int32, device="cuda")
+    o = g4.Outputs()
+    o.cand_ids, o.cand_stride = cid.data_ptr(), 64
+    s = g4.Sampler(0, 64, vocab)
+    try:
+        s.lmhead_sample(hd.data_ptr(), rows, hidden, nib.data_ptr(), sc.data_ptr(), vocab, prm, CAP, ud.data_ptr(),
+                        out.data_ptr(), outputs=o)
+        torch.cuda.synchronize()
+    finally:
+        s.close()
+    tok, ids = out.cpu().numpy(), cid.cpu().numpy()
+    nt = max(1, min(32, os.cpu_count() or 1))
+    stats = {"rows": 0, "tok_f32": 0, "tok_q8": 0, "ids_f32": 0.0, "ids_q8": 0.0}
+    for r in range(0, rows, 16):
+        for name, lg in (("f32", oracle.matvec_q4_mt(blocks, h[r], vocab, hidden, nt)),
+                         ("q8", oracle.matvec_q4q8(blocks, h[r], vocab, hidden, nt))):
+            t, _, rid, _ = oracle.sample(lg, oracle.params(1.0, 64, 0.95), CAP, u[r], oracle.VARIANT_F32,
+                                         oracle.TIE_LOWER)
+            stats["tok_" + name] += int(t == tok[r])
+            stats["ids_" + name] += len(set(rid.tolist()) & set(ids[r].tolist())) / 64.0
+        stats["rows"] += 1
+    print("C4 agreement with the reference's LM-head arithmetic:", stats)
+    assert stats["ids_f32"] >= 0.95 * stats["rows"], stats
+    assert stats["ids_q8"] >= 0.5 * stats["rows"], stats

@@ -25,7 +25,7 @@ def test_c1_batched_1000_steps(sampler, torch_cuda, oracle, g4, c1_rows):
 
 
 def test_c1_single_row_steps(sampler, torch_cuda, oracle, g4, c1_rows):
-    # one call per decode step, as TModel.Generate does (B = 1: small-chunk kernel)
+    # one call per decode step, as TModel.Generate does (B = 1: the cluster kernel)
     x, u = c1_rows
     p = g4.make_params(1.0, 64, 0.95)
     tot = {"boundary": 0}
