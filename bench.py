@@ -356,12 +356,34 @@ def run_c4(dev, peak, steps=20):
         b.synchronize()
         ts.append(a.elapsed_time(b) * 1e3 / steps)
     del g
+    # agreement with the reference's own LM-head arithmetic on a few rows: the
+    # fp32 CpuMatVecQ4 and the Q8_1 + DP4A path of its GPU shaders, each
+    # followed by the oracle's DoSample
+    from oracle import oracle as O
+
+    cid = torch.full((rows, 64), -1, dtype=torch.int32, device=dev)
+    o = g4.Outputs()
+    o.cand_ids, o.cand_stride = cid.data_ptr(), 64
+    s.lmhead_sample(hd.data_ptr(), rows, H, nib.data_ptr(), sc.data_ptr(), VOCAB, p, SOFTCAP, u.data_ptr(),
+                    out.data_ptr(), outputs=o)
+    torch.cuda.synchronize()
     s.close()
+    tok, ids = out.cpu().numpy(), cid.cpu().numpy()
+    uh = u.cpu().numpy()
+    agree = {"rows": 0, "tokens_vs_f32": 0, "tokens_vs_q8": 0, "survivors_vs_f32": 0.0, "survivors_vs_q8": 0.0}
+    for r in range(0, rows, 16):
+        for name, lg in (("f32", O.matvec_q4_mt(blocks, h[r], VOCAB, H, host_threads())),
+                         ("q8", O.matvec_q4q8(blocks, h[r], VOCAB, H, host_threads()))):
+            t, _, rid, _ = O.sample(lg, O.params(1.0, 64, 0.95), SOFTCAP, uh[r], O.VARIANT_F32, O.TIE_LOWER)
+            agree["tokens_vs_" + name] += int(t == tok[r])
+            agree["survivors_vs_" + name] += len(set(rid.tolist()) & set(ids[r].tolist())) / 64.0
+        agree["rows"] += 1
     us = statistics.median(ts)
     wbytes = VOCAB * (H // 32) * 18
     return {"us_per_step": us, "rows_per_s": rows / (us * 1e-6), "weight_gbs": wbytes / (us * 1e-6) / 1e9,
             "hbm_frac_of_peak": wbytes / (us * 1e-6) / 1e9 / peak,
             "tflops": 2.0 * rows * VOCAB * H / (us * 1e-6) / 1e12,
+            "agreement_with_reference_lmhead": agree,
             "config": "C4: hidden 64 x 2560 fp32 -> LM head 262144 x 2560 Q4_0 (tcgen05 fp16 MMA, dequantized "
                       "weights in TMEM, fp32 accumulate) -> top_k 64, T=1, top_p 0.95; median of 5 replays of a "
                       "20-call CUDA graph"}

@@ -46,6 +46,9 @@ struct g4s_ctx {
     int persist_tab = 0;                   // the same for the bf16 softcap-table variant
     float *sc_tab = nullptr;               // bf16 softcap table (workspace), built for sc_tab_cap
     float sc_tab_cap = 0.0f;               // softcap the table holds (0: not built)
+    float *e_tab = nullptr;                // bf16 weight table of one (softcap, 1/T) (workspace)
+    float e_tab_cap = 0.0f, e_tab_invt = 0.0f;  // what it holds (cap 0: not built)
+    int persist_etab = 0;                  // CTAs per SM of the weight-table kernel
     RowStat *rowstat = nullptr;
     int32_t *lk_idx = nullptr;
     float *lk_val = nullptr;
@@ -366,6 +369,7 @@ int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t
     const size_t o_pd = off; off = align(off + (size_t)PSLOTS * max_rows * (sizeof(g4s_params) + sizeof(float)));
     const size_t o_err = off; off = align(off + sizeof(int));
     const size_t o_tab = off; off = align(off + (size_t)SC_TABLE_BYTES);
+    const size_t o_etab = off; off = align(off + (size_t)ETAB_TABLE_BYTES);
     ctx->ws_bytes = off;
     if (cudaMalloc(&ctx->ws, off) != cudaSuccess) {
         cudaGetLastError();
@@ -383,6 +387,7 @@ int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t
     ctx->params_dev = (g4s_params *)(base + o_pd);
     ctx->dev_err = (int *)(base + o_err);
     ctx->sc_tab = (float *)(base + o_tab);
+    ctx->e_tab = (float *)(base + o_etab);
     if (cudaMemset(ctx->ws, 0, off) != cudaSuccess ||
         cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaHostAlloc((void **)&ctx->params_pinned, (size_t)PSLOTS * max_rows * (sizeof(g4s_params) + sizeof(float)),
@@ -521,8 +526,29 @@ int32_t g4s_sample_ex(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t r
         if (cs == cudaStreamCaptureStatusNone) ctx->sc_tab_cap = softcap;
     }
     a.sc_table = use_tab ? ctx->sc_tab : nullptr;
+    // one temperature for every row that draws: the per-logit weight itself
+    // comes from a table (built once per (softcap, temperature), like the above)
+    const float T0 = params[0].temperature;
+    const float invt0 = (T0 > 0.0f && T0 != 1.0f) ? 1.0f / T0 : 1.0f;
+    const bool use_etab = use_tab && params_stride == 0 && T0 > 0.0f && softcap * invt0 <= ETAB_MAX_CAP_OVER_T &&
+                          (ctx->persist_etab > 0 || (ctx->persist_etab = full_etab_blocks_per_sm()) > 0);
+    if (use_etab && (ctx->e_tab_cap != softcap || ctx->e_tab_invt != invt0)) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(s, &cs) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(ctx, G4S_ERR_CUDA, "g4s_sample: cannot query the stream's capture state");
+        }
+        cudaError_t te = launch_etable(softcap, a.invcap, invt0, T0 != 1.0f, ctx->e_tab, nullptr, s);
+        if (te == cudaSuccess && cs == cudaStreamCaptureStatusNone) te = cudaStreamSynchronize(s);
+        if (te != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "g4s_sample: weight table: %s", cudaGetErrorString(te));
+        if (cs == cudaStreamCaptureStatusNone) {
+            ctx->e_tab_cap = softcap;
+            ctx->e_tab_invt = invt0;
+        }
+    }
+    a.e_table = use_etab ? ctx->e_tab : nullptr;
     if (any_full) {
-        int &bps = use_tab ? ctx->persist_tab : ctx->persist[dtype][vec ? 1 : 0];
+        int &bps = use_etab ? ctx->persist_etab : use_tab ? ctx->persist_tab : ctx->persist[dtype][vec ? 1 : 0];
         if (bps == 0) bps = full_stream_blocks_per_sm(dtype, vec, use_tab);
         a.persist_blocks = bps * ctx->sm_count;
     }

@@ -635,6 +635,266 @@ __global__ void __launch_bounds__(TAB_THREADS, G4S_TAB_CPS) full_tab_kernel(Samp
     cp_async_wait<0>();
 }
 
+// ---------------------------------------------------------------------------
+// full_etab_kernel: broadcast-params draw rows of aligned bf16 logits with a
+// softcap (the C3 workload).  One temperature for the whole call makes the
+// per-logit weight itself a function of the 16-bit input, so a table holds
+// E(c) = 2^(s(c) * L2E - C) rounded once to fp32 for every bf16 code c from
+// ETAB_LO up (s the exact softcapped and tempered value; C = fl32(s(+inf) *
+// L2E), so every E lies in [2^-2C, 1]): the positive codes from 2^-16 up and
+// every negative code.  A logit then costs its code, one shared-memory load
+// and an add -- no exponent, no sign fix-up, no clamp from above.  Positive
+// magnitudes below 2^-16 (zero included) are clamped up to ETAB_LO and flag
+// their item for the exact general path, as do NaNs (their entries are 0).
+// The table (200 KiB) fills the CTA's shared memory; every lane loads the
+// vectors of its next item straight into registers.
+// The item statistics keep the other kernels' definition: cc = fl32(m * L2E)
+// with m = s(max v) exact, and S = sum 2^(s * L2E - cc), obtained as
+// (sum E) / E(max v) * 2^r with r = m * L2E - cc (exact in fp64, |r| below
+// half an ulp of cc, so 2^r = 1 + r ln2 to 1e-11).
+// ---------------------------------------------------------------------------
+#ifndef G4S_ETAB_THREADS
+#define G4S_ETAB_THREADS 1024
+#endif
+constexpr int ETAB_THREADS = G4S_ETAB_THREADS;
+constexpr uint32_t ETAB_LO = TAB_LOW;                    // first code in the table (2^-16)
+constexpr int ETAB_N = (int)(0x10000u - ETAB_LO);         // codes ETAB_LO .. 0xffff
+constexpr int ETAB_BYTES = ETAB_N * 4;
+static_assert(ETAB_BYTES % 16 == 0, "bulk copies move 16-byte multiples");
+static_assert(ETAB_BYTES == ETAB_TABLE_BYTES, "E table size in the launch interface");
+constexpr int ETAB_SMEM_LAUNCH = ETAB_BYTES + 16;        // + the table's mbarrier
+constexpr long ETAB_WAIT_LIMIT = 1L << 21;
+
+__global__ void etable_kernel(float cap, float invcap, float invT, int use_t, float C, float *tab)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= ETAB_N) return;
+    const uint32_t code = ETAB_LO + (uint32_t)i;
+    const float v = __uint_as_float(code << 16);
+    float e = 0.0f;
+    if (v == v) {
+        float sv = __fmul_rn(g4_tanhf(__fmul_rn(v, invcap)), cap);
+        if (use_t) sv = __fmul_rn(sv, invT);
+        e = (float)exp2((double)sv * (double)G4_L2E - (double)C);
+    }
+    tab[i] = e;
+}
+
+#ifndef G4S_ETAB_NPOLY
+#define G4S_ETAB_NPOLY 0
+#endif
+// Vectors per lane and item whose weights the polynomial computes instead of
+// the table (the FMA and MUFU pipes then carry part of the work the
+// shared-memory pipe would).
+constexpr int ETAB_NPOLY = G4S_ETAB_NPOLY;
+static_assert(ETAB_NPOLY >= 0 && ETAB_NPOLY < NVEC, "at least one table vector");
+
+// A 4-byte load from this CTA's shared memory at byte address `addr` (no side
+// effects: the compiler may schedule it freely; the table it reads is complete
+// before any item is processed).
+__device__ __forceinline__ float lds_f32(uint32_t addr)
+{
+    float v;
+    asm("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+    return v;
+}
+
+// One item from this lane's four vectors `rv`; writes the item statistics (lane 0).
+__device__ __forceinline__ void etab_item(const SampleArgs &a, int64_t it, int sub, const uint4 *rv, uint32_t tbase,
+                                          const SParams &sp)
+{
+    constexpr int ITEM = Geo<G4S_BF16>::ITEM;
+    constexpr int NTV = NVEC - ETAB_NPOLY;  // table vectors
+    const float NEG_INF = -__uint_as_float(0x7f800000u);
+    const int lane = threadIdx.x & 31;
+    const int n = item_len<G4S_BF16>(a.vocab, sub);
+    const uint32_t LO2 = (ETAB_LO << 16) | ETAB_LO;
+    uint32_t mx2 = bmax4(rv[0]);
+    uint32_t mn2 = min_u16x2(min_u16x2(rv[0].x, rv[0].y), min_u16x2(rv[0].z, rv[0].w));
+    if constexpr (ETAB_NPOLY > 0) {
+#pragma unroll
+        for (int j = 1; j < NTV; j++) {
+            mx2 = bmax2_nan(mx2, bmax4(rv[j]));
+            mn2 = min_u16x2(mn2, min_u16x2(min_u16x2(rv[j].x, rv[j].y), min_u16x2(rv[j].z, rv[j].w)));
+        }
+    }
+    bool ok = n == ITEM;
+    float2 pacc = make_float2(0.0f, 0.0f);
+    float cc = 0.0f, m = NEG_INF;
+    if constexpr (ETAB_NPOLY > 0) {
+        // the polynomial vectors need the item's exponent origin first
+        uint32_t pmx = bmax4(rv[NTV]), pmn = bmin4(rv[NTV]);
+#pragma unroll
+        for (int j = NTV + 1; j < NVEC; j++) {
+            pmx = bmax2_nan(pmx, bmax4(rv[j]));
+            pmn = bmin2_nan(pmn, bmin4(rv[j]));
+        }
+        mx2 = bmax2_nan(mx2, pmx);
+        ok &= (fabsf(__fmul_rn(bf16x2_max_f(pmx), sp.invcap)) <= 1.0f) &
+              (fabsf(__fmul_rn(bf16x2_min_f(pmn), sp.invcap)) <= 1.0f);
+    }
+    float vmax = 0.0f;
+    if constexpr (ETAB_NPOLY > 0) {
+        const float lmx = bf16x2_max_f(mx2);
+        ok &= (lmx == lmx) & (min(mn2 & 0xffffu, mn2 >> 16) >= ETAB_LO);
+        vmax = warp_max_redux(lmx == lmx ? lmx : 0.0f);
+        m = s_of(vmax, sp);
+        cc = __fmul_rn(m, G4_L2E);
+        const float2 ic = make_float2(sp.invcap, sp.invcap), c2 = make_float2(sp.cap, sp.cap);
+        const float2 t2 = make_float2(sp.invT, sp.invT), l2 = make_float2(G4_L2E, G4_L2E), nc = make_float2(-cc, -cc);
+#pragma unroll
+        for (int j = NTV; j < NVEC; j++) {
+            const uint32_t wv[4] = {rv[j].x, rv[j].y, rv[j].z, rv[j].w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                float2 v = make_float2(__uint_as_float(__byte_perm(wv[k], 0u, 0x1044)), __uint_as_float(wv[k] & 0xffff0000u));
+                v = __fmul2_rn(tanh_poly2(__fmul2_rn(v, ic)), c2);
+                if (sp.use_t) v = __fmul2_rn(v, t2);
+                const float2 y = __ffma2_rn(v, l2, nc);
+                pacc = __fadd2_rn(pacc, make_float2(ex2_approx(y.x), ex2_approx(y.y)));
+            }
+        }
+    }
+    float2 acc0 = make_float2(0.0f, 0.0f), acc1 = acc0;
+#pragma unroll
+    for (int j = 0; j < NTV; j++) {
+        if (ETAB_NPOLY == 0 && j) {
+            mx2 = bmax2_nan(mx2, bmax4(rv[j]));
+            mn2 = min_u16x2(mn2, min_u16x2(min_u16x2(rv[j].x, rv[j].y), min_u16x2(rv[j].z, rv[j].w)));
+        }
+        const uint32_t wv[4] = {rv[j].x, rv[j].y, rv[j].z, rv[j].w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint32_t c = max_u16x2(wv[k], LO2);  // positive codes below the table: flagged above
+            const float2 e = make_float2(lds_f32(tbase + ((c & 0xffffu) << 2)), lds_f32(tbase + ((c >> 16) << 2)));
+            if (k & 1) acc1 = __fadd2_rn(acc1, e);
+            else acc0 = __fadd2_rn(acc0, e);
+        }
+    }
+    acc0 = __fadd2_rn(acc0, acc1);
+    float S = acc0.x + acc0.y;
+    if constexpr (ETAB_NPOLY > 0) {
+        // the table sums to the item origin cc, per lane, then the polynomial's
+        const float em = lds_f32(tbase + ((__float_as_uint(vmax) >> 16) << 2));
+        const double r = (double)m * (double)G4_L2E - (double)cc;
+        const float scale = (float)((1.0 + r * 0.6931471805599453) / (double)em);
+        S = __fmaf_rn(S, scale, pacc.x + pacc.y);
+    }
+    if constexpr (ETAB_NPOLY == 0) {
+        const float lmx = bf16x2_max_f(mx2);
+        // no NaN, no positive code below the table (negative codes are >= 0x8000)
+        ok &= (lmx == lmx) & (min(mn2 & 0xffffu, mn2 >> 16) >= ETAB_LO);
+        vmax = warp_max_redux(lmx == lmx ? lmx : 0.0f);
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) S += __shfl_xor_sync(FULLMASK, S, d);
+    const bool redo = !__all_sync(FULLMASK, ok);
+    if (lane == 0) {
+        if constexpr (ETAB_NPOLY == 0) {
+            if (!redo) {
+                m = s_of(vmax, sp);
+                cc = __fmul_rn(m, G4_L2E);
+                const float em = lds_f32(tbase + ((__float_as_uint(vmax) >> 16) << 2));
+                const double r = (double)m * (double)G4_L2E - (double)cc;
+                S = (float)((double)__fdiv_rn(S, em) * (1.0 + r * 0.6931471805599453));
+            }
+        }
+        a.istat[it] = redo ? make_float4(NEG_INF, 0.0f, 0.0f, 1.0f) : make_float4(m, cc, S, 0.0f);
+    }
+}
+
+__global__ void __launch_bounds__(ETAB_THREADS, 1) full_etab_kernel(SampleArgs a)
+{
+    constexpr int ITEM = Geo<G4S_BF16>::ITEM;
+    constexpr int WPB = ETAB_THREADS / 32;
+    extern __shared__ __align__(16) uint4 dsm[];  // the table, then its mbarrier
+    const uint32_t tsh = (uint32_t)__cvta_generic_to_shared(dsm);
+    const uint32_t bar = tsh + ETAB_BYTES;
+    // the table arrives by bulk copies (one thread issues them) while every lane
+    // already loads its first item
+    if (threadIdx.x == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(ETAB_BYTES) : "memory");
+        constexpr int PIECE = 32768;
+        for (int o = 0; o < ETAB_BYTES; o += PIECE) {
+            const int bytes = ETAB_BYTES - o < PIECE ? ETAB_BYTES - o : PIECE;
+            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                             tsh + o),
+                         "l"((const char *)a.e_table + o), "r"(bytes), "r"(bar)
+                         : "memory");
+        }
+    }
+    const uint32_t tbase = tsh - ETAB_LO * 4u;  // address of code c: tbase + 4 c
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int ipr = (a.vocab + ITEM - 1) / ITEM;
+    const int64_t nitems = (int64_t)a.rows * ipr;
+    const int64_t nw = (int64_t)gridDim.x * WPB;
+    const int64_t it0 = (int64_t)blockIdx.x * WPB + wib;
+    const int step_row = (int)(nw / ipr), step_sub = (int)(nw % ipr);
+    const SParams sp = make_sparams(a, a.params.p0, 0);
+    struct Cursor {
+        int row, sub;
+    };
+    auto advance = [&](Cursor &c) {
+        c.sub += step_sub;
+        c.row += step_row;
+        if (c.sub >= ipr) {
+            c.sub -= ipr;
+            c.row++;
+        }
+    };
+    const int64_t lane_off = (int64_t)lane * 16;
+    // vectors of a partial last item past its end read as zero (the item is redone)
+    auto load = [&](const Cursor &c, uint4 *r) {
+        const int n = item_len<G4S_BF16>(a.vocab, c.sub);
+        const char *src = (const char *)a.logits + ((int64_t)c.row * a.row_stride + (int64_t)c.sub * ITEM) * 2 + lane_off;
+#pragma unroll
+        for (int j = 0; j < NVEC; j++)
+            r[j] = item_pos<G4S_BF16>(j, 0, lane) + 8 <= n ? ld_stream_v4(src + j * 512) : make_uint4(0u, 0u, 0u, 0u);
+    };
+    Cursor cur{(int)(it0 / ipr), (int)(it0 % ipr)};
+    uint4 nxt[NVEC];
+    Cursor cn = cur;
+    if (it0 < nitems) load(cn, nxt);
+    advance(cn);
+    __syncthreads();  // the mbarrier is initialised
+    {
+        // bounded wait for the table (on a timeout: the error flag, and this
+        // CTA's items are flagged for the general path)
+        uint32_t ok = 0;
+        for (long k = 0; k < ETAB_WAIT_LIMIT && !ok; k++)
+            asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0, 1000; selp.u32 %0, 1, 0, p; }"
+                         : "=r"(ok)
+                         : "r"(bar)
+                         : "memory");
+        if (!__syncthreads_and(ok)) {
+            if (threadIdx.x == 0) {
+                if (a.err) atomicExch(a.err, 1);
+                // drain: the copies land before the CTA leaves (bounded)
+                for (long k = 0; k < ETAB_WAIT_LIMIT && !ok; k++)
+                    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0, 1000; selp.u32 %0, 1, 0, p; }"
+                                 : "=r"(ok)
+                                 : "r"(bar)
+                                 : "memory");
+            }
+            for (int64_t it = it0; it < nitems; it += nw)
+                if (lane == 0) a.istat[it] = make_float4(-__uint_as_float(0x7f800000u), 0.0f, 0.0f, 1.0f);
+            return;
+        }
+    }
+    for (int64_t it = it0; it < nitems; it += nw) {
+        uint4 rv[NVEC];
+#pragma unroll
+        for (int j = 0; j < NVEC; j++) rv[j] = nxt[j];
+        if (it + nw < nitems) load(cn, nxt);
+        advance(cn);
+        etab_item(a, it, cur.sub, rv, tbase, sp);
+        advance(cur);
+    }
+}
+
 // 2^d for a double d <= ~0: 2^round(d) * ex2(d - round(d)) (|f| <= 1/2, so the
 // fp32 ex2 is accurate to a few units in 1e-7 relative); 0 below 2^-1000.
 __device__ __forceinline__ double pow2_split(double d)
@@ -1072,6 +1332,40 @@ static bool tab_setup()
     return true;
 }
 
+static bool etab_setup()
+{
+    static bool ready[MAX_DEVICES] = {};
+    const int dev = current_device();
+    if (dev >= 0 && dev < MAX_DEVICES && ready[dev]) return true;
+    if (cudaFuncSetAttribute(full_etab_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ETAB_SMEM_LAUNCH) !=
+        cudaSuccess)
+        return false;
+    if (dev >= 0 && dev < MAX_DEVICES) ready[dev] = true;
+    return true;
+}
+
+int full_etab_blocks_per_sm()
+{
+    int n = 0;
+    if (!etab_setup() ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, full_etab_kernel, ETAB_THREADS, ETAB_SMEM_LAUNCH) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+cudaError_t launch_etable(float cap, float invcap, float invT, bool use_t, float *tab, float *C_out, cudaStream_t s)
+{
+    // origin: the largest possible weight exponent, fl32(s(+inf) * L2E); s(+inf)
+    // is cap (times 1/T) because tanh rounds to 1 well inside the table
+    const float stop = use_t ? cap * invT : cap;
+    const float C = stop * G4_L2E;
+    if (C_out) *C_out = C;
+    etable_kernel<<<(ETAB_N + 255) / 256, 256, 0, s>>>(cap, invcap, invT, use_t ? 1 : 0, C, tab);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_softcap_table(float cap, float invcap, float *tab, cudaStream_t s)
 {
     softcap_table_kernel<<<(SC_TAB_N + 255) / 256, 256, 0, s>>>(cap, invcap, tab);
@@ -1087,7 +1381,12 @@ static cudaError_t launch_full_t(const SampleArgs &a, cudaStream_t s, bool probs
     if (!probs) {
         cudaError_t e;
         if constexpr (DT == G4S_BF16 && VEC) {
-            if (a.sc_table) {
+            if (a.e_table) {
+                if (!etab_setup()) return cudaGetLastError();
+                int64_t blocks = (nitems + ETAB_THREADS / 32 - 1) / (ETAB_THREADS / 32);
+                if (a.persist_blocks > 0 && blocks > a.persist_blocks) blocks = a.persist_blocks;
+                full_etab_kernel<<<(unsigned)blocks, ETAB_THREADS, ETAB_SMEM_LAUNCH, s>>>(a);
+            } else if (a.sc_table) {
                 if (!tab_setup()) return cudaGetLastError();
                 constexpr int wpb = TAB_THREADS / 32;
                 int64_t blocks = (nitems + wpb - 1) / wpb;

@@ -67,6 +67,7 @@ struct SampleArgs {
     int32_t gworld;
     int *err;                  // device error flag: a bounded wait ran out (nullable)
     const float *sc_table;     // full path, bf16 rows: the softcap table of `softcap` (nullable)
+    const float *e_table;      // full path, bf16 rows, one temperature: the E table (nullable; see full_etab_kernel)
     int64_t wait_limit;        // 0: the kernels' own poll limits; > 0: test hook, every
                                //   bounded wait gives up after this many non-blocking polls
 };
@@ -127,5 +128,13 @@ int full_stream_blocks_per_sm(int dtype, bool vec, bool tab);
 constexpr int SC_TABLE_BYTES = 12816;
 constexpr float SC_TABLE_MAX_CAP = 55.0f;
 cudaError_t launch_softcap_table(float cap, float invcap, float *tab, cudaStream_t s);
+// The E table of the broadcast-params draw path (ETAB_TABLE_BYTES; see
+// full_etab_kernel): built for one (softcap, temperature); C is its exponent origin.
+constexpr int ETAB_TABLE_BYTES = 205312;
+// E values span [2^-2C, 1]: usable while 2 * C stays inside the normal fp32 range.
+constexpr float ETAB_MAX_CAP_OVER_T = 43.0f;
+cudaError_t launch_etable(float cap, float invcap, float invT, bool use_t, float *tab, float *C_out, cudaStream_t s);
+// Whether a call's full-path rows may take the E-table kernel, and its grid size per SM.
+int full_etab_blocks_per_sm();
 
 }  // namespace g4s

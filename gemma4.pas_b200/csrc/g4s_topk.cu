@@ -33,6 +33,8 @@
 
 namespace g4s {
 
+constexpr int HB = 2048;  // bins of one hist_level (11 bits of the keys), kept in sm.L
+
 struct TopkSmem {
     alignas(16) uint64_t L[CAP2];
     alignas(16) float tv[KMAX];
@@ -95,6 +97,94 @@ __device__ uint64_t radix_kth(ForEach for_each, int K, TopkSmem &sm)
         __syncthreads();
     }
     return prefix;
+}
+
+// One level of a histogram selection over the keys a visitor enumerates (key
+// 0: not a candidate): among the keys whose bits from `shift + bits` up equal
+// those of `prefix`, the bins of bits shift .. shift + bits - 1 (bits <= 11;
+// the bits below `shift` ignored).  Finds the bin holding the k-th largest of those keys.
+// Returns true when it exists (*bin, and *above = how many of them lie in
+// higher bins, *inbin = how many in the bin); false when fewer than k keys
+// match.  The bins overlay sm.L, whose contents the caller no longer needs;
+// for_each(fn) must call fn(key) for each of this thread's keys (registers).
+template <class ForEach>
+__device__ bool hist_level(ForEach for_each, uint32_t prefix, int shift, int bits, int k, TopkSmem &sm,
+                           uint32_t *bin, int *above, int *inbin)
+{
+    constexpr int PER = HB / NTHREADS;
+    static_assert(HB * 4 <= CAP2 * 8, "the bins fit in sm.L");
+    uint32_t *hb = reinterpret_cast<uint32_t *>(sm.L);
+    const int tid = threadIdx.x;
+    const int top = shift + bits;
+    const uint32_t hmask = top >= 32 ? 0u : ~0u << top;
+    __syncthreads();  // earlier reads of sm.L are over
+#pragma unroll
+    for (int r = 0; r < PER; r++) hb[tid + r * NTHREADS] = 0;
+    __syncthreads();
+    for_each([&](uint32_t key) {
+        if (key && (key & hmask) == (prefix & hmask)) atomicAdd(&hb[(key >> shift) & ((1u << bits) - 1u)], 1u);
+    });
+    __syncthreads();
+    // thread t owns bins HB-1-PER*t down to HB-PER*(t+1), in descending order
+    uint32_t c[PER];
+    int sum = 0;
+#pragma unroll
+    for (int r = 0; r < PER; r++) {
+        c[r] = hb[HB - 1 - PER * tid - r];
+        sum += (int)c[r];
+    }
+    int total;
+    const int excl = block_excl_scan(sum, &total, sm.scan);
+    if (total >= k && excl < k && excl + sum >= k) {
+        int cum = excl;
+#pragma unroll
+        for (int r = 0; r < PER; r++) {
+            if (cum + (int)c[r] >= k) {
+                sm.misc[1] = HB - 1 - PER * tid - r;
+                sm.misc[2] = cum;
+                sm.misc[0] = (int)c[r];
+                break;
+            }
+            cum += (int)c[r];
+        }
+    }
+    __syncthreads();
+    const bool found = total >= k;
+    if (found) {
+        *bin = (uint32_t)sm.misc[1];
+        *above = sm.misc[2];
+        *inbin = sm.misc[0];
+    }
+    __syncthreads();
+    return found;
+}
+
+// A threshold t on the keys a visitor enumerates with at least K keys >= t
+// (1 when fewer than K are valid): the lower edge of the 11-bit histogram bin
+// holding the K-th largest, refined by up to two more levels (bits 20..10,
+// then 9..0, the last one exact) while more than `limit` keys would remain.
+template <class ForEach>
+__device__ uint32_t hist_select(ForEach for_each, int K, int limit, TopkSmem &sm)
+{
+    uint32_t bin;
+    int above, inbin;
+    if (!hist_level(for_each, 0u, 21, 11, K, sm, &bin, &above, &inbin)) return 1u;
+    uint32_t t = bin << 21;
+    if (above + inbin > limit) {
+        const int k2 = K - above;
+        int a2, i2;
+        uint32_t b2;
+        if (hist_level(for_each, t, 10, 11, k2, sm, &b2, &a2, &i2)) {
+            t |= b2 << 10;
+            if (above + a2 + i2 > limit) {
+                const int k3 = k2 - a2;
+                int a3, i3;
+                uint32_t b3;
+                if (hist_level(for_each, t, 0, 10, k3, sm, &b3, &a3, &i3)) t |= b3;
+            }
+        }
+    }
+    return t ? t : 1u;
 }
 
 // The tail of the top-K path on the kw winners, sorted by ascending vocab id
@@ -308,6 +398,21 @@ __device__ __forceinline__ void finish_row(const SampleArgs &a, int row, const g
     topk_tail(a, row, p, kw, sm);
 }
 
+__device__ int stream_cut_to(int cnt, int K, int limit, uint32_t &thr, TopkSmem &sm);
+
+// The K largest of the candidates in sm.L[0..cnt) (cnt <= CAP2), sorted
+// descending in sm.L[0..min(K, cnt)): above NTHREADS candidates a histogram cut
+// (an exact radix cut under heavy ties) first, then the one-pass rank sort.
+__device__ int top_sorted(TopkSmem &sm, int cnt, int K)
+{
+    if (cnt > NTHREADS) {
+        uint32_t thr = 1;
+        cnt = stream_cut_to(cnt, K, NTHREADS, thr, sm);
+    }
+    sort_list_desc(sm, cnt);
+    return cnt < K ? cnt : K;
+}
+
 // Merge of nch descending candidate lists (list c: C + c * lstride, length
 // CC[c * cstride]) into the top min(K, entries) composites, sorted descending in
 // sm.L[0..kw).  With j = ceil(K / nch), the ceil(K/j)-th largest of the lists'
@@ -317,6 +422,31 @@ __device__ int merge_lists(int K, TopkSmem &sm, const uint64_t *C, int64_t lstri
                            int64_t cstride, int nch)
 {
     const int tid = threadIdx.x;
+    if (nch < 256 && nch <= NTHREADS) {
+        // few entries in all (the usual case): every list read whole into sm.L
+        // with coalesced loads, then one selection there -- no chains of
+        // dependent global loads
+        int *loff = reinterpret_cast<int *>(sm.hist);  // list start offsets (nch + 1 <= 256 ints)
+        const int cc = tid < nch ? __ldcg(&CC[tid * cstride]) : 0;
+        int total;
+        const int off = block_excl_scan(cc, &total, sm.scan);
+        if (total <= CAP2) {
+            if (tid < nch) loff[tid] = off;
+            if (tid == 0) loff[nch] = total;
+            __syncthreads();
+            for (int i = tid; i < total; i += NTHREADS) {
+                int lo = 0, hi = nch - 1;
+                while (lo < hi) {
+                    const int mid = (lo + hi + 1) >> 1;
+                    if (loff[mid] <= i) lo = mid;
+                    else hi = mid - 1;
+                }
+                sm.L[i] = __ldcg(&C[lo * lstride + (i - loff[lo])]);
+            }
+            __syncthreads();
+            return top_sorted(sm, total, K);
+        }
+    }
     const int j = (K + nch - 1) / nch;
     const int mm = (K + j - 1) / j;
     // lower bound t2: the mm-th largest of the lists' j-th entries
@@ -384,8 +514,7 @@ __device__ int merge_lists(int K, TopkSmem &sm, const uint64_t *C, int64_t lstri
             sm.L[i] = __ldcg(&C[lo * lstride + (i - loff[lo])]);
         }
         __syncthreads();
-        sort_list_desc(sm, total);
-        return total < K ? total : K;
+        return top_sorted(sm, total, K);
     }
     // heavy ties: exact radix selection over all list entries
     const uint64_t kth = radix_kth(
@@ -573,7 +702,8 @@ __device__ __forceinline__ int chunk_select(const SampleArgs &a, int row, int64_
 // chunk_select.
 constexpr int STREAM_RING = 32768;         // bytes of the tile ring per CTA
 constexpr int STREAM_DYN_SMEM = STREAM_RING + 16 * 8;  // ring + one mbarrier per slot
-constexpr long STREAM_WAIT_LIMIT = 1L << 22;
+constexpr long STREAM_WAIT_LIMIT = 1L << 21;  // tries of a tile wait (each suspends at most the hint below)
+constexpr int STREAM_WAIT_HINT_NS = 1000;
 static_assert(STREAM_TILE * 2 <= CAP2 && KMAX <= STREAM_TILE, "candidate buffer holds two tiles");
 
 // cut the candidate buffer sm.L[0..cnt) (cnt > K) to its K largest composites; returns their smallest
@@ -606,31 +736,24 @@ __device__ uint64_t stream_cut(int cnt, int K, TopkSmem &sm)
     return kth;
 }
 
-// Compacts the candidate buffer sm.L[0..cnt) to its entries with key >= t',
-// t' = the smallest over warps of each warp's ceil(K / NWARPS)-th largest lane
-// maximum (each warp has that many lanes holding an entry at or above it, so
-// at least K entries survive; on random logits a few times K do).  Raises thr
-// to t'.  Returns the new count.
-__device__ int stream_bound_cut(int cnt, int K, uint32_t &thr, TopkSmem &sm)
+// Compacts the candidate buffer sm.L[0..cnt) to its entries with key >= the
+// histogram bound of their keys (at least K survive) and raises thr to it.
+__device__ int stream_hist_cut(int cnt, int K, int limit, uint32_t &thr, TopkSmem &sm)
 {
     constexpr int PER = CAP2 / NTHREADS;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x;
     uint64_t keep[PER];
-    uint32_t mx = 0;
 #pragma unroll
     for (int j = 0; j < PER; j++) {
         const int i = tid + j * NTHREADS;
         keep[j] = i < cnt ? sm.L[i] : 0;
-        const uint32_t k = comp_key(keep[j]);
-        mx = k > mx ? k : mx;
     }
-    const uint32_t srt = warp_sort_desc_u32(mx);
-    const uint32_t wthr = __shfl_sync(FULLMASK, srt, (K + NWARPS - 1) / NWARPS - 1);
-    if (lane == 0) sm.wthr[warp] = wthr;
-    __syncthreads();
-    uint32_t t = sm.wthr[0];
+    uint32_t t = hist_select(
+        [&](auto fn) {
 #pragma unroll
-    for (int w = 1; w < NWARPS; w++) t = sm.wthr[w] < t ? sm.wthr[w] : t;
+            for (int j = 0; j < PER; j++) fn(comp_key(keep[j]));
+        },
+        K, limit, sm);
     if (t < thr) t = thr;
     int c = 0;
 #pragma unroll
@@ -645,11 +768,11 @@ __device__ int stream_bound_cut(int cnt, int K, uint32_t &thr, TopkSmem &sm)
     return total;
 }
 
-// Cut for the streaming pass: the bound compaction, and the exact radix cut
-// when ties keep the buffer above `limit` entries.
+// Cut for the streaming pass: the histogram-bound compaction, and the exact
+// radix cut when ties keep the buffer above `limit` entries.
 __device__ int stream_cut_to(int cnt, int K, int limit, uint32_t &thr, TopkSmem &sm)
 {
-    cnt = stream_bound_cut(cnt, K, thr, sm);
+    cnt = stream_hist_cut(cnt, K, limit, thr, sm);
     if (cnt > limit) {
         const uint64_t kth = stream_cut(cnt, K, sm);
         const uint32_t k = comp_key(kth);
@@ -719,10 +842,12 @@ __device__ __forceinline__ int chunk_select_stream(const SampleArgs &a, int row,
                                  : "r"(bar), "r"(par)
                                  : "memory");
             } else {
+                // each try may suspend the thread up to STREAM_WAIT_HINT_NS instead
+                // of spinning (the waiting warps leave the issue slots to the others)
                 for (long k = 0; k < STREAM_WAIT_LIMIT && !ok; k++)
-                    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
                                  : "=r"(ok)
-                                 : "r"(bar), "r"(par)
+                                 : "r"(bar), "r"(par), "n"(STREAM_WAIT_HINT_NS)
                                  : "memory");
             }
             timed_out |= !ok;
@@ -747,23 +872,32 @@ __device__ __forceinline__ int chunk_select_stream(const SampleArgs &a, int row,
             __syncthreads();
         }
         uint32_t key[NV * VW];
+#pragma unroll
+        for (int i = 0; i < NV * VW; i++) key[i] = cand_key(x[i]);
+        if (t == 0) {
+            // the first tile's histogram bound: at least K of its keys, so of
+            // the chunk's, lie at or above it (1 when the tile has fewer)
+            thr = hist_select(
+                [&](auto fn) {
+#pragma unroll
+                    for (int i = 0; i < NV * VW; i++) fn(key[i]);
+                },
+                K, 4 * K, sm);
+        }
         int mine = 0;
 #pragma unroll
-        for (int i = 0; i < NV * VW; i++) {
-            key[i] = cand_key(x[i]);
-            mine += key[i] >= thr;
-        }
+        for (int i = 0; i < NV * VW; i++) mine += key[i] >= thr;
         if (__any_sync(FULLMASK, mine)) {
             const int inc = warp_incl_scan(mine);
             int wbase = 0;
             if (lane == 31) wbase = atomicAdd(&sm.misc[3], inc);
             int o = __shfl_sync(FULLMASK, wbase, 31) + inc - mine;
+            const uint32_t id0 = (uint32_t)(a.id_offset + c0 + base + tid * VW);
 #pragma unroll
             for (int i = 0; i < NV * VW; i++) {
-                if (key[i] >= thr) {
-                    const int e = base + (i / VW) * (NTHREADS * VW) + tid * VW + (i % VW);
-                    sm.L[o++] = composite(key[i], (uint32_t)(a.id_offset + c0 + e));
-                }
+                const bool p = key[i] >= thr;
+                if (p) sm.L[o] = composite(key[i], id0 + (uint32_t)((i / VW) * (NTHREADS * VW) + (i % VW)));
+                o += p;
             }
         }
         // every thread is done with the slot; after a wait ran out no tile is

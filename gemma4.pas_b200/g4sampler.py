@@ -33,6 +33,21 @@ class Params(ctypes.Structure):
                 f"rp={self.repetition_penalty})")
 
 
+class TensorInfo(ctypes.Structure):
+    """g4s_tensor_info: TTensorInfo (src/Gemma4.Types.pas:119-129)."""
+
+    _fields_ = [("name", ctypes.c_char * 256), ("source_dtype", c_int32), ("output_dtype", c_int32),
+                ("offset", ctypes.c_uint64), ("size", ctypes.c_uint64), ("ndim", c_int32),
+                ("shape", c_int64 * 8)]
+
+    @property
+    def dims(self):
+        return tuple(self.shape[i] for i in range(self.ndim))
+
+
+DT_UNKNOWN, DT_BF16, DT_F16, DT_F32, DT_Q4_0 = 0, 1, 2, 3, 4
+
+
 class Outputs(ctypes.Structure):
     _fields_ = [("token_prob", c_void_p), ("row_flags", c_void_p), ("cand_ids", c_void_p),
                 ("cand_probs", c_void_p), ("cand_stride", c_int32), ("phase_mask", c_int32),
@@ -71,6 +86,15 @@ SIGNATURES = {
     "g4s_shard_init": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_void_p]),
     "g4s_shard_sample": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int64, POINTER(Params), c_int32,
                                    c_float, c_void_p, c_void_p, POINTER(Outputs), c_void_p]),
+    "g4s_vpk_open": (c_int32, [c_char_p, c_char_p, c_char_p, POINTER(c_void_p)]),
+    "g4s_vpk_close": (c_int32, [c_void_p]),
+    "g4s_vpk_tensor_count": (c_int32, [c_void_p]),
+    "g4s_vpk_tensor_at": (c_int32, [c_void_p, c_int32, POINTER(TensorInfo)]),
+    "g4s_vpk_find": (c_int32, [c_void_p, c_char_p, POINTER(TensorInfo)]),
+    "g4s_vpk_data": (c_void_p, [c_void_p, POINTER(TensorInfo)]),
+    "g4s_vpk_verify": (c_int32, [c_void_p, c_char_p]),
+    "g4s_vpk_load_lmhead": (c_int32, [c_void_p, c_int32, c_void_p, c_void_p, c_int32, POINTER(c_int32),
+                                      POINTER(c_int32), c_void_p]),
 }
 SHARD_LIST = 256       # G4S_SHARD_LIST
 SHARD_UID_BYTES = 128  # G4S_SHARD_UID_BYTES
@@ -271,3 +295,57 @@ class Sampler:
                                       c_void_p(out.ctypes.data))
         self._check(rc)
         return out
+
+
+class Vpk:
+    """A VPK weight archive opened through g4s_vpk_open (TWeightStore)."""
+
+    def __init__(self, path: str, manifest: str | None = None, weights: str | None = None):
+        self.lib = load()
+        h = c_void_p()
+        enc = lambda x: x.encode() if x is not None else None
+        rc = self.lib.g4s_vpk_open(path.encode(), enc(manifest), enc(weights), ctypes.byref(h))
+        if rc != OK:
+            raise G4SError(rc, self.lib.g4s_last_error(None).decode())
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.g4s_vpk_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __len__(self):
+        return self.lib.g4s_vpk_tensor_count(self.h)
+
+    def find(self, name: str) -> TensorInfo:
+        ti = TensorInfo()
+        rc = self.lib.g4s_vpk_find(self.h, name.encode(), ctypes.byref(ti))
+        if rc != OK:
+            raise G4SError(rc, self.lib.g4s_last_error(None).decode())
+        return ti
+
+    def tensor(self, name: str):
+        """The tensor's bytes (a read-only view of the mapping, copied to numpy)."""
+        import numpy as np
+
+        ti = self.find(name)
+        ptr = self.lib.g4s_vpk_data(self.h, ctypes.byref(ti))
+        return np.ctypeslib.as_array((ctypes.c_uint8 * ti.size).from_address(ptr)).copy(), ti
+
+    def verify(self, entry: str) -> int:
+        return self.lib.g4s_vpk_verify(self.h, entry.encode())
+
+    def load_lmhead(self, device: int, nib_ptr: int, scales_ptr: int, max_vocab: int, stream: int | None = None):
+        v, hdim = c_int32(), c_int32()
+        rc = self.lib.g4s_vpk_load_lmhead(self.h, device, c_void_p(nib_ptr), c_void_p(scales_ptr), max_vocab,
+                                          ctypes.byref(v), ctypes.byref(hdim), c_void_p(stream) if stream else None)
+        if rc != OK:
+            raise G4SError(rc, self.lib.g4s_last_error(None).decode())
+        return v.value, hdim.value
+

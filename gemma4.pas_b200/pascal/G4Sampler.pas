@@ -73,6 +73,19 @@ type
 
   PG4SCtx = Pointer;
 
+  { TTensorInfo (src/Gemma4.Types.pas:119-129) as g4s_tensor_info. }
+  TG4STensorInfo = record
+    Name: array[0..255] of AnsiChar;
+    SourceDtype: Int32;
+    OutputDtype: Int32;
+    Offset: UInt64;
+    Size: UInt64;
+    NDim: Int32;
+    Shape: array[0..7] of Int64;
+  end;
+  PG4STensorInfo = ^TG4STensorInfo;
+  PG4SVpk = Pointer;
+
 function g4s_version(): Int32; cdecl; external G4SLib;
 procedure g4s_params_defaults(P: PG4SParams); cdecl; external G4SLib;
 function g4s_create(Device, MaxRows, MaxVocab: Int32; Flags: UInt32;
@@ -136,6 +149,23 @@ function g4s_shard_init(Ctx: PG4SCtx; World, Rank, VocabTotal: Int32;
 function g4s_shard_sample(Ctx: PG4SCtx; LogitsSlice: Pointer; DType, Rows: Int32;
   RowStride: Int64; Params: PG4SParams; ParamsStride: Int32; Softcap: Single;
   U: PDouble; OutTokens: PInt32; Extra: PG4SOutputs;
+  Stream: Pointer): Int32; cdecl; external G4SLib;
+
+{ The VPK weight archive (TWeightStore): open, look up, read, load the LM head. }
+function g4s_vpk_open(Path, ManifestPath, WeightsPath: PAnsiChar;
+  out Vpk: PG4SVpk): Int32; cdecl; external G4SLib;
+function g4s_vpk_close(Vpk: PG4SVpk): Int32; cdecl; external G4SLib;
+function g4s_vpk_tensor_count(Vpk: PG4SVpk): Int32; cdecl; external G4SLib;
+function g4s_vpk_tensor_at(Vpk: PG4SVpk; Index: Int32;
+  Info: PG4STensorInfo): Int32; cdecl; external G4SLib;
+function g4s_vpk_find(Vpk: PG4SVpk; Name: PAnsiChar;
+  Info: PG4STensorInfo): Int32; cdecl; external G4SLib;
+function g4s_vpk_data(Vpk: PG4SVpk; Info: PG4STensorInfo): Pointer; cdecl;
+  external G4SLib;
+function g4s_vpk_verify(Vpk: PG4SVpk; EntryPath: PAnsiChar): Int32; cdecl;
+  external G4SLib;
+function g4s_vpk_load_lmhead(Vpk: PG4SVpk; Device: Int32; Nibbles: Pointer;
+  Scales: Pointer; MaxVocab: Int32; out Vocab, Hidden: Int32;
   Stream: Pointer): Int32; cdecl; external G4SLib;
 
 implementation

@@ -284,6 +284,54 @@ int32_t g4s_shard_sample(g4s_ctx *ctx, const void *logits_slice, int32_t dtype, 
                          const g4s_params *params, int32_t params_stride, float softcap, const double *u,
                          int32_t *out_tokens, const g4s_outputs *extra, void *stream);
 
+/*
+ * Weight archive (the reference's VPK, read by TWeightStore,
+ * src/Gemma4.Tensors.pas:100-130, 299-520, over StdApp's TVFS,
+ * src/vendor/StdApp/StdApp.VFS.pas): the archive is mapped read-only, its
+ * manifest parsed, tensors looked up by name.  Errors are read with
+ * g4s_last_error(NULL).
+ */
+typedef struct g4s_vpk g4s_vpk;
+
+enum g4s_weight_dtype {   /* TDtypeKind (src/Gemma4.Types.pas:505-517) */
+    G4S_DT_UNKNOWN = 0, G4S_DT_BF16 = 1, G4S_DT_F16 = 2, G4S_DT_F32 = 3, G4S_DT_Q4_0 = 4
+};
+#define G4S_MAX_DIMS 8
+
+/* TTensorInfo (src/Gemma4.Types.pas:119-129); offset is within weights.bin. */
+typedef struct g4s_tensor_info {
+    char     name[256];
+    int32_t  source_dtype;
+    int32_t  output_dtype;
+    uint64_t offset;
+    uint64_t size;
+    int32_t  ndim;
+    int64_t  shape[G4S_MAX_DIMS];
+} g4s_tensor_info;
+
+/* TWeightStore.Open: path of the .vpk, then the manifest and weights entries
+   inside it (NULL: the reference's defaults E4B/manifest.json, E4B/weights.bin,
+   src/Gemma4.Types.pas:79, 85). */
+int32_t g4s_vpk_open(const char *path, const char *manifest_path, const char *weights_path, g4s_vpk **out);
+int32_t g4s_vpk_close(g4s_vpk *vpk);
+/* TWeightStore.TensorCount / GetTensorInfo / FindTensor. */
+int32_t g4s_vpk_tensor_count(const g4s_vpk *vpk);
+int32_t g4s_vpk_tensor_at(const g4s_vpk *vpk, int32_t index, g4s_tensor_info *info);
+int32_t g4s_vpk_find(const g4s_vpk *vpk, const char *name, g4s_tensor_info *info);
+/* TWeightStore.GetRawPointer: host address of the tensor's bytes in the mapping. */
+const void *g4s_vpk_data(const g4s_vpk *vpk, const g4s_tensor_info *info);
+/* CRC-32 of one archive entry against its directory record (G4S_ERR_STATE on
+   a mismatch); the reference writes it when packing (TVFS.PackDirectory). */
+int32_t g4s_vpk_verify(const g4s_vpk *vpk, const char *entry_path);
+/* The LM head of the archive -- model.language_model.lm_head.weight, else the
+   tied model.language_model.embed_tokens.weight, as DoRecordFinalGpu picks
+   (src/Gemma4.Model.pas:1293-1299) -- uploaded to `device` and repacked into
+   nibbles [hidden/64][vocab][2][16] and scales [hidden/64][vocab][2] for
+   g4s_lmhead_sample (the reference repacks its GPU copy at load time too,
+   src/Gemma4.Model.pas:494-650).  Waits for the device; vocab <= max_vocab. */
+int32_t g4s_vpk_load_lmhead(const g4s_vpk *vpk, int32_t device, uint8_t *nibbles, uint16_t *scales, int32_t max_vocab,
+                            int32_t *out_vocab, int32_t *out_hidden, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
