@@ -496,7 +496,7 @@ def run_c5(rank, world, local, dev, peak, steps=50):
     # phases, each timed alone on the same inputs
     lists = torch.zeros((world, rows, g4.SHARD_LIST), dtype=torch.int64, device=dev)
     counts = torch.zeros((world, rows), dtype=torch.int32, device=dev)
-    us_lists = timed(lambda i: sh.shard_lists(sets[i % 2].data_ptr(), g4.F32, rows, n, n, lo, VOCAB, prm,
+    us_lists = timed(lambda i: sh.shard_lists(sets[i % 2].data_ptr(), g4.F32, rows, n, n, lo, VOCAB, prm, SOFTCAP,
                                               lists[rank].data_ptr(), counts[rank].data_ptr(), stream=stream), steps)
     dist.all_gather_into_tensor(lists.view(-1), lists[rank].contiguous().view(-1))
     dist.all_gather_into_tensor(counts.view(-1), counts[rank].contiguous().view(-1))

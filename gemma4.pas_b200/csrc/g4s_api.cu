@@ -49,6 +49,7 @@ struct g4s_ctx {
     float *e_tab = nullptr;                // bf16 weight table of one (softcap, 1/T) (workspace)
     float e_tab_cap = 0.0f, e_tab_invt = 0.0f;  // what it holds (cap 0: not built)
     int persist_etab = 0;                  // CTAs per SM of the weight-table kernel
+    ShardTarget *shard_tgt = nullptr;      // [max_rows] sharded full-vocabulary draws (workspace)
     RowStat *rowstat = nullptr;
     int32_t *lk_idx = nullptr;
     float *lk_val = nullptr;
@@ -157,6 +158,7 @@ struct NcclApi {
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
     ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
     ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*AllReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*GroupStart)() = nullptr;
     ncclResult_t (*GroupEnd)() = nullptr;
     const char *(*GetErrorString)(ncclResult_t) = nullptr;
@@ -183,6 +185,7 @@ static bool nccl_load()
     sym(g_nccl.CommDestroy, "ncclCommDestroy");
     sym(g_nccl.CommAbort, "ncclCommAbort");
     sym(g_nccl.AllGather, "ncclAllGather");
+    sym(g_nccl.AllReduce, "ncclAllReduce");
     sym(g_nccl.GroupStart, "ncclGroupStart");
     sym(g_nccl.GroupEnd, "ncclGroupEnd");
     sym(g_nccl.GetErrorString, "ncclGetErrorString");
@@ -247,24 +250,81 @@ static int32_t stage_params(g4s_ctx *ctx, const char *who, const g4s_params *par
     return G4S_OK;
 }
 
-// Checks that every row is a top-K row of the sharded path: 0 < top_k <= 256,
-// top_k below both the slice and the full vocabulary.
+// Checks the rows of a sharded call: top-K rows need 0 < top_k <= 256 below
+// both the slice and the vocabulary; rows with top_k <= 0 or >= the
+// vocabulary take the full-vocabulary path.  Reports what the call holds.
+struct ShardRows {
+    bool any_draw = false, any_full = false, any_full_draw = false, any_topk = false;
+};
 static int32_t check_shard_rows(g4s_ctx *ctx, const char *who, const g4s_params *params, int32_t params_stride,
-                                int rows, int slice_vocab, int vocab_total, bool *any_draw)
+                                int rows, int slice_vocab, int vocab_total, ShardRows *sr)
 {
     const int nparam = params_stride ? rows : 1;
-    *any_draw = false;
+    *sr = ShardRows();
     for (int r = 0; r < nparam; r++) {
         const g4s_params &p = params[r];
         if (p.temperature != p.temperature || p.top_p != p.top_p)
             return fail(ctx, G4S_ERR_ARG, "%s: NaN temperature/top_p in params[%d]", who, r);
-        if (p.top_k <= 0 || p.top_k > KMAX_ || p.top_k >= vocab_total || (slice_vocab > 0 && p.top_k >= slice_vocab))
+        const bool draw = p.temperature > 0.0f;
+        sr->any_draw |= draw;
+        if (p.top_k <= 0 || p.top_k >= vocab_total) {
+            sr->any_full = true;
+            sr->any_full_draw |= draw;
+            continue;
+        }
+        if (p.top_k > KMAX_ || (slice_vocab > 0 && p.top_k >= slice_vocab))
             return fail(ctx, G4S_ERR_ARG,
-                        "%s: params[%d].top_k = %d; the sharded path takes 0 < top_k <= %d below the slice (%d) "
-                        "and the vocabulary (%d); sample full-vocabulary rows with a row split",
+                        "%s: params[%d].top_k = %d; the sharded path takes top-K rows with top_k <= %d below the "
+                        "slice (%d), or full-vocabulary rows (top_k <= 0 or >= %d)",
                         who, r, p.top_k, KMAX_, slice_vocab, vocab_total);
-        if (p.temperature > 0.0f) *any_draw = true;
+        sr->any_topk = true;
     }
+    return G4S_OK;
+}
+
+// Set-up of a call's full-vocabulary rows: the softcap and weight tables the
+// bf16 streaming kernels read (built once per softcap, resp. per (softcap,
+// temperature)), the streaming grid and the item statistics.  Outside stream
+// capture a table build is waited for, so calls on any stream may use it
+// afterwards; a captured build is part of the graph and is not remembered
+// (the next call outside the graph builds again).
+static int32_t prepare_full_path(g4s_ctx *ctx, const char *who, SampleArgs &a, int dtype, bool vec, float softcap,
+                                 const g4s_params *params, int32_t params_stride, cudaStream_t s)
+{
+    a.istat = ctx->istat;
+    a.rowstat = ctx->rowstat;
+    const bool use_tab = dtype == G4S_BF16 && vec && softcap > 0.0f && softcap <= SC_TABLE_MAX_CAP;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (use_tab && cudaStreamIsCapturing(s, &cs) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(ctx, G4S_ERR_CUDA, "%s: cannot query the stream's capture state", who);
+    }
+    if (use_tab && ctx->sc_tab_cap != softcap) {
+        cudaError_t te = launch_softcap_table(softcap, a.invcap, ctx->sc_tab, s);
+        if (te == cudaSuccess && cs == cudaStreamCaptureStatusNone) te = cudaStreamSynchronize(s);
+        if (te != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "%s: softcap table: %s", who, cudaGetErrorString(te));
+        if (cs == cudaStreamCaptureStatusNone) ctx->sc_tab_cap = softcap;
+    }
+    a.sc_table = use_tab ? ctx->sc_tab : nullptr;
+    // one temperature for every row that draws: the per-logit weight itself
+    // comes from a table
+    const float T0 = params[0].temperature;
+    const float invt0 = (T0 > 0.0f && T0 != 1.0f) ? 1.0f / T0 : 1.0f;
+    const bool use_etab = use_tab && params_stride == 0 && T0 > 0.0f && softcap * invt0 <= ETAB_MAX_CAP_OVER_T &&
+                          (ctx->persist_etab > 0 || (ctx->persist_etab = full_etab_blocks_per_sm()) > 0);
+    if (use_etab && (ctx->e_tab_cap != softcap || ctx->e_tab_invt != invt0)) {
+        cudaError_t te = launch_etable(softcap, a.invcap, invt0, T0 != 1.0f, ctx->e_tab, nullptr, s);
+        if (te == cudaSuccess && cs == cudaStreamCaptureStatusNone) te = cudaStreamSynchronize(s);
+        if (te != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "%s: weight table: %s", who, cudaGetErrorString(te));
+        if (cs == cudaStreamCaptureStatusNone) {
+            ctx->e_tab_cap = softcap;
+            ctx->e_tab_invt = invt0;
+        }
+    }
+    a.e_table = use_etab ? ctx->e_tab : nullptr;
+    int &bps = use_etab ? ctx->persist_etab : use_tab ? ctx->persist_tab : ctx->persist[dtype][vec ? 1 : 0];
+    if (bps == 0) bps = full_stream_blocks_per_sm(dtype, vec, use_tab);
+    a.persist_blocks = bps * ctx->sm_count;
     return G4S_OK;
 }
 
@@ -370,6 +430,7 @@ int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t
     const size_t o_err = off; off = align(off + sizeof(int));
     const size_t o_tab = off; off = align(off + (size_t)SC_TABLE_BYTES);
     const size_t o_etab = off; off = align(off + (size_t)ETAB_TABLE_BYTES);
+    const size_t o_stg = off; off = align(off + (size_t)max_rows * sizeof(ShardTarget));
     ctx->ws_bytes = off;
     if (cudaMalloc(&ctx->ws, off) != cudaSuccess) {
         cudaGetLastError();
@@ -388,6 +449,7 @@ int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t
     ctx->dev_err = (int *)(base + o_err);
     ctx->sc_tab = (float *)(base + o_tab);
     ctx->e_tab = (float *)(base + o_etab);
+    ctx->shard_tgt = (ShardTarget *)(base + o_stg);
     if (cudaMemset(ctx->ws, 0, off) != cudaSuccess ||
         cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaHostAlloc((void **)&ctx->params_pinned, (size_t)PSLOTS * max_rows * (sizeof(g4s_params) + sizeof(float)),
@@ -509,48 +571,9 @@ int32_t g4s_sample_ex(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t r
     a.err = ctx->dev_err;
     a.wait_limit = ctx->wait_limit;
     a.istat = ctx->istat;
-    // bf16 full-path rows take the softcap from a table built once per softcap
-    // value.  Outside stream capture the build is waited for, so calls on any
-    // stream may use it afterwards; a captured build is part of the graph and
-    // is not remembered (the next call outside the graph builds again).
-    const bool use_tab = any_full && dtype == G4S_BF16 && vec && softcap > 0.0f && softcap <= SC_TABLE_MAX_CAP;
-    if (use_tab && ctx->sc_tab_cap != softcap) {
-        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-        if (cudaStreamIsCapturing(s, &cs) != cudaSuccess) {
-            cudaGetLastError();
-            return fail(ctx, G4S_ERR_CUDA, "g4s_sample: cannot query the stream's capture state");
-        }
-        cudaError_t te = launch_softcap_table(softcap, a.invcap, ctx->sc_tab, s);
-        if (te == cudaSuccess && cs == cudaStreamCaptureStatusNone) te = cudaStreamSynchronize(s);
-        if (te != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "g4s_sample: softcap table: %s", cudaGetErrorString(te));
-        if (cs == cudaStreamCaptureStatusNone) ctx->sc_tab_cap = softcap;
-    }
-    a.sc_table = use_tab ? ctx->sc_tab : nullptr;
-    // one temperature for every row that draws: the per-logit weight itself
-    // comes from a table (built once per (softcap, temperature), like the above)
-    const float T0 = params[0].temperature;
-    const float invt0 = (T0 > 0.0f && T0 != 1.0f) ? 1.0f / T0 : 1.0f;
-    const bool use_etab = use_tab && params_stride == 0 && T0 > 0.0f && softcap * invt0 <= ETAB_MAX_CAP_OVER_T &&
-                          (ctx->persist_etab > 0 || (ctx->persist_etab = full_etab_blocks_per_sm()) > 0);
-    if (use_etab && (ctx->e_tab_cap != softcap || ctx->e_tab_invt != invt0)) {
-        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-        if (cudaStreamIsCapturing(s, &cs) != cudaSuccess) {
-            cudaGetLastError();
-            return fail(ctx, G4S_ERR_CUDA, "g4s_sample: cannot query the stream's capture state");
-        }
-        cudaError_t te = launch_etable(softcap, a.invcap, invt0, T0 != 1.0f, ctx->e_tab, nullptr, s);
-        if (te == cudaSuccess && cs == cudaStreamCaptureStatusNone) te = cudaStreamSynchronize(s);
-        if (te != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "g4s_sample: weight table: %s", cudaGetErrorString(te));
-        if (cs == cudaStreamCaptureStatusNone) {
-            ctx->e_tab_cap = softcap;
-            ctx->e_tab_invt = invt0;
-        }
-    }
-    a.e_table = use_etab ? ctx->e_tab : nullptr;
     if (any_full) {
-        int &bps = use_etab ? ctx->persist_etab : use_tab ? ctx->persist_tab : ctx->persist[dtype][vec ? 1 : 0];
-        if (bps == 0) bps = full_stream_blocks_per_sm(dtype, vec, use_tab);
-        a.persist_blocks = bps * ctx->sm_count;
+        const int32_t rc = prepare_full_path(ctx, "g4s_sample", a, dtype, vec, softcap, params, params_stride, s);
+        if (rc != G4S_OK) return rc;
     }
     a.rowstat = ctx->rowstat;
     a.lk_idx = ctx->lk_idx;
@@ -711,8 +734,8 @@ int32_t g4s_device_status(g4s_ctx *ctx)
 // params already on the device (g4s_shard_sample stages them once for both).
 static int32_t shard_lists_core(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t rows, int32_t slice_vocab,
                                 int64_t row_stride, int32_t id_offset, int32_t vocab_total, const g4s_params *params,
-                                int32_t params_stride, uint64_t *out_lists, int32_t *out_counts, void *stream,
-                                const RowParams *staged)
+                                int32_t params_stride, float softcap, uint64_t *out_lists, int32_t *out_counts,
+                                void *stream, const RowParams *staged)
 {
     static const char *who = "g4s_shard_lists";
     if (!ctx) return fail(nullptr, G4S_ERR_ARG, "%s: ctx is NULL", who);
@@ -728,8 +751,8 @@ static int32_t shard_lists_core(g4s_ctx *ctx, const void *logits, int32_t dtype,
                     (long long)id_offset + slice_vocab, vocab_total);
     if (params_stride != 0 && params_stride != 1)
         return fail(ctx, G4S_ERR_ARG, "%s: params_stride must be 0 or 1", who);
-    bool any_draw;
-    int32_t rc = check_shard_rows(ctx, who, params, params_stride, rows, slice_vocab, vocab_total, &any_draw);
+    ShardRows sr;
+    int32_t rc = check_shard_rows(ctx, who, params, params_stride, rows, slice_vocab, vocab_total, &sr);
     if (rc != G4S_OK) return rc;
     DeviceGuard guard(ctx->device);
     if (!guard.ok) return fail(ctx, G4S_ERR_CUDA, "%s: cannot select device %d", who, ctx->device);
@@ -758,9 +781,23 @@ static int32_t shard_lists_core(g4s_ctx *ctx, const void *logits, int32_t dtype,
     a.id_offset = id_offset;
     a.list_out = out_lists;
     a.list_cnt = out_counts;
+    a.softcap = softcap;
+    a.invcap = softcap > 0.0f ? 1.0f / softcap : 0.0f;
     if (staged) a.params = *staged;
     else if ((rc = stage_params(ctx, who, params, params_stride, rows, s, a.params)) != G4S_OK) return rc;
-    cudaError_t e = tc.stream ? launch_topk_stream(a, s) : launch_topk(a, ept, vec, s);
+    cudaError_t e = cudaSuccess;
+    if (sr.any_full) {
+        // full-vocabulary rows: the streaming pass over the slice, then each
+        // row's slice summary into its list slot (the item statistics stay in
+        // the context for g4s_shard_resolve)
+        if ((rc = prepare_full_path(ctx, who, a, dtype, vec, softcap, params, params_stride, s)) != G4S_OK) return rc;
+        SampleArgs af = a;
+        af.stream_only = 1;
+        e = launch_full(af, ept, vec, s);
+        af.shard_mode = 1;
+        if (e == cudaSuccess) e = launch_full_combine(af, vec, s);
+    }
+    if (sr.any_topk && e == cudaSuccess) e = tc.stream ? launch_topk_stream(a, s) : launch_topk(a, ept, vec, s);
     if (e != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "%s: launch failed: %s", who, cudaGetErrorString(e));
     return G4S_OK;
 }
@@ -778,10 +815,10 @@ static int32_t shard_merge_core(g4s_ctx *ctx, const uint64_t *lists, const int32
     if (rows < 1 || rows > ctx->max_rows) return fail(ctx, G4S_ERR_CAPACITY, "%s: rows %d outside [1, %d]", who, rows, ctx->max_rows);
     if (params_stride != 0 && params_stride != 1)
         return fail(ctx, G4S_ERR_ARG, "%s: params_stride must be 0 or 1", who);
-    bool any_draw;
-    int32_t rc = check_shard_rows(ctx, who, params, params_stride, rows, 0, vocab_total, &any_draw);
+    ShardRows sr;
+    int32_t rc = check_shard_rows(ctx, who, params, params_stride, rows, 0, vocab_total, &sr);
     if (rc != G4S_OK) return rc;
-    if (any_draw && !u) return fail(ctx, G4S_ERR_ARG, "%s: u is NULL but a row has temperature > 0", who);
+    if (sr.any_draw && !u) return fail(ctx, G4S_ERR_ARG, "%s: u is NULL but a row has temperature > 0", who);
     g4s_outputs ex;
     memset(&ex, 0, sizeof(ex));
     if (extra) ex = *extra;
@@ -808,6 +845,7 @@ static int32_t shard_merge_core(g4s_ctx *ctx, const uint64_t *lists, const int32
     a.glists = lists;
     a.gcnts = counts;
     a.gworld = world;
+    a.shard_tgt = ctx->shard_tgt;
     if (staged) a.params = *staged;
     else if ((rc = stage_params(ctx, who, params, params_stride, rows, s, a.params)) != G4S_OK) return rc;
     cudaError_t e = launch_shard_merge(a, s);
@@ -817,10 +855,73 @@ static int32_t shard_merge_core(g4s_ctx *ctx, const uint64_t *lists, const int32
 
 int32_t g4s_shard_lists(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t rows, int32_t slice_vocab,
                         int64_t row_stride, int32_t id_offset, int32_t vocab_total, const g4s_params *params,
-                        int32_t params_stride, uint64_t *out_lists, int32_t *out_counts, void *stream)
+                        int32_t params_stride, float softcap, uint64_t *out_lists, int32_t *out_counts, void *stream)
 {
     return shard_lists_core(ctx, logits, dtype, rows, slice_vocab, row_stride, id_offset, vocab_total, params,
-                            params_stride, out_lists, out_counts, stream, nullptr);
+                            params_stride, softcap, out_lists, out_counts, stream, nullptr);
+}
+
+// The full-vocabulary draws shard_tgt assigns to this rank (after
+// g4s_shard_merge on the same context): the crossing item among this slice's
+// item statistics (from g4s_shard_lists on the same context), rescanned from
+// the slice's logits.
+static int32_t shard_resolve_core(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t rows, int32_t slice_vocab,
+                                  int64_t row_stride, int32_t id_offset, int32_t rank, const g4s_params *params,
+                                  int32_t params_stride, float softcap, const double *u, int32_t *out_tokens,
+                                  const g4s_outputs *extra, void *stream, const RowParams *staged)
+{
+    static const char *who = "g4s_shard_resolve";
+    if (!ctx) return fail(nullptr, G4S_ERR_ARG, "%s: ctx is NULL", who);
+    if (!logits || !params || !out_tokens || !u)
+        return fail(ctx, G4S_ERR_ARG, "%s: logits, params, u and out_tokens must be non-NULL", who);
+    if (dtype != G4S_F32 && dtype != G4S_BF16) return fail(ctx, G4S_ERR_ARG, "%s: bad dtype %d", who, dtype);
+    if (rows < 1 || slice_vocab < 1 || rows > ctx->max_rows || slice_vocab > ctx->max_vocab || row_stride < slice_vocab)
+        return fail(ctx, G4S_ERR_CAPACITY, "%s: rows %d / slice %d outside the context (%d / %d)", who, rows,
+                    slice_vocab, ctx->max_rows, ctx->max_vocab);
+    if (params_stride != 0 && params_stride != 1)
+        return fail(ctx, G4S_ERR_ARG, "%s: params_stride must be 0 or 1", who);
+    DeviceGuard guard(ctx->device);
+    if (!guard.ok) return fail(ctx, G4S_ERR_CUDA, "%s: cannot select device %d", who, ctx->device);
+    cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
+    const int esize = dtype == G4S_F32 ? 4 : 2;
+    const bool vec = ((uintptr_t)logits % 16u == 0) && (((int64_t)row_stride * esize) % 16 == 0);
+    g4s_outputs ex;
+    memset(&ex, 0, sizeof(ex));
+    if (extra) ex = *extra;
+    SampleArgs a;
+    memset(&a, 0, sizeof(a));
+    a.logits = logits;
+    a.row_stride = row_stride;
+    a.rows = rows;
+    a.vocab = slice_vocab;
+    a.dtype = dtype;
+    a.softcap = softcap;
+    a.invcap = softcap > 0.0f ? 1.0f / softcap : 0.0f;
+    a.u = u;
+    a.out_tokens = out_tokens;
+    a.token_prob = ex.token_prob;
+    a.row_flags = ex.row_flags;
+    a.id_offset = id_offset;
+    a.istat = ctx->istat;
+    a.rowstat = ctx->rowstat;
+    a.shard_tgt = ctx->shard_tgt;
+    a.shard_mode = 2;
+    a.shard_rank = rank;
+    int32_t rc;
+    if (staged) a.params = *staged;
+    else if ((rc = stage_params(ctx, who, params, params_stride, rows, s, a.params)) != G4S_OK) return rc;
+    const cudaError_t e = launch_full_combine(a, vec, s);
+    if (e != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "%s: launch failed: %s", who, cudaGetErrorString(e));
+    return G4S_OK;
+}
+
+int32_t g4s_shard_resolve(g4s_ctx *ctx, const void *logits_slice, int32_t dtype, int32_t rows, int32_t slice_vocab,
+                          int64_t row_stride, int32_t id_offset, int32_t rank, const g4s_params *params,
+                          int32_t params_stride, float softcap, const double *u, int32_t *out_tokens,
+                          const g4s_outputs *extra, void *stream)
+{
+    return shard_resolve_core(ctx, logits_slice, dtype, rows, slice_vocab, row_stride, id_offset, rank, params,
+                              params_stride, softcap, u, out_tokens, extra, stream, nullptr);
 }
 
 int32_t g4s_shard_merge(g4s_ctx *ctx, const uint64_t *lists, const int32_t *counts, int32_t world, int32_t rows,
@@ -897,8 +998,8 @@ int32_t g4s_shard_sample(g4s_ctx *ctx, const void *logits_slice, int32_t dtype, 
     int32_t *recv_cnt = (int32_t *)(ctx->sh_recv + (size_t)W * ctx->max_rows * KMAX_);
     if (!params || (params_stride != 0 && params_stride != 1))
         return fail(ctx, G4S_ERR_ARG, "%s: params must be non-NULL, params_stride 0 or 1", who);
-    bool any_draw;
-    int32_t rc = check_shard_rows(ctx, who, params, params_stride, rows, n, ctx->shard_vocab, &any_draw);
+    ShardRows sr;
+    int32_t rc = check_shard_rows(ctx, who, params, params_stride, rows, n, ctx->shard_vocab, &sr);
     if (rc != G4S_OK) return rc;
     DeviceGuard guard(ctx->device);
     if (!guard.ok) return fail(ctx, G4S_ERR_CUDA, "%s: cannot select device %d", who, ctx->device);
@@ -907,7 +1008,7 @@ int32_t g4s_shard_sample(g4s_ctx *ctx, const void *logits_slice, int32_t dtype, 
     memset(&rp, 0, sizeof(rp));
     if ((rc = stage_params(ctx, who, params, params_stride, rows, s, rp)) != G4S_OK) return rc;
     rc = shard_lists_core(ctx, logits_slice, dtype, rows, n, row_stride, off, ctx->shard_vocab, params, params_stride,
-                          send, send_cnt, s, &rp);
+                          softcap, send, send_cnt, s, &rp);
     if (rc != G4S_OK) return rc;
     ncclComm_t comm = (ncclComm_t)ctx->nccl_comm;
     ncclResult_t r = g_nccl.GroupStart();
@@ -917,8 +1018,22 @@ int32_t g4s_shard_sample(g4s_ctx *ctx, const void *logits_slice, int32_t dtype, 
     if (r == ncclSuccess) r = r2;
     if (r != ncclSuccess) return fail(ctx, G4S_ERR_NCCL, "%s: all-gather: %s", who, g_nccl.GetErrorString(r));
     // the merge reads list w of row i at recv + w * rows * KMAX + i * KMAX
-    return shard_merge_core(ctx, recv, recv_cnt, W, rows, ctx->shard_vocab, params, params_stride, softcap, u,
-                            out_tokens, extra, s, &rp);
+    rc = shard_merge_core(ctx, recv, recv_cnt, W, rows, ctx->shard_vocab, params, params_stride, softcap, u, out_tokens,
+                          extra, s, &rp);
+    if (rc != G4S_OK || !sr.any_full_draw) return rc;
+    // full-vocabulary draws: the rank whose slice holds the crossing writes the
+    // token, the others keep -1; a max over the ranks gives every rank the token
+    rc = shard_resolve_core(ctx, logits_slice, dtype, rows, n, row_stride, off, ctx->shard_rank, params,
+                            params_stride, softcap, u, out_tokens, extra, s, &rp);
+    if (rc != G4S_OK) return rc;
+    r = g_nccl.GroupStart();
+    if (r == ncclSuccess) r = g_nccl.AllReduce(out_tokens, out_tokens, (size_t)rows, ncclInt32, ncclMax, comm, s);
+    if (r == ncclSuccess && extra && extra->token_prob)
+        r = g_nccl.AllReduce(extra->token_prob, extra->token_prob, (size_t)rows, ncclFloat32, ncclMax, comm, s);
+    const ncclResult_t r3 = g_nccl.GroupEnd();
+    if (r == ncclSuccess) r = r3;
+    if (r != ncclSuccess) return fail(ctx, G4S_ERR_NCCL, "%s: all-reduce: %s", who, g_nccl.GetErrorString(r));
+    return G4S_OK;
 }
 
 }  // extern "C"

@@ -680,15 +680,6 @@ __global__ void etable_kernel(float cap, float invcap, float invT, int use_t, fl
     tab[i] = e;
 }
 
-#ifndef G4S_ETAB_NPOLY
-#define G4S_ETAB_NPOLY 0
-#endif
-// Vectors per lane and item whose weights the polynomial computes instead of
-// the table (the FMA and MUFU pipes then carry part of the work the
-// shared-memory pipe would).
-constexpr int ETAB_NPOLY = G4S_ETAB_NPOLY;
-static_assert(ETAB_NPOLY >= 0 && ETAB_NPOLY < NVEC, "at least one table vector");
-
 // A 4-byte load from this CTA's shared memory at byte address `addr` (no side
 // effects: the compiler may schedule it freely; the table it reads is complete
 // before any item is processed).
@@ -704,102 +695,47 @@ __device__ __forceinline__ void etab_item(const SampleArgs &a, int64_t it, int s
                                           const SParams &sp)
 {
     constexpr int ITEM = Geo<G4S_BF16>::ITEM;
-    constexpr int NTV = NVEC - ETAB_NPOLY;  // table vectors
     const float NEG_INF = -__uint_as_float(0x7f800000u);
     const int lane = threadIdx.x & 31;
     const int n = item_len<G4S_BF16>(a.vocab, sub);
     const uint32_t LO2 = (ETAB_LO << 16) | ETAB_LO;
     uint32_t mx2 = bmax4(rv[0]);
     uint32_t mn2 = min_u16x2(min_u16x2(rv[0].x, rv[0].y), min_u16x2(rv[0].z, rv[0].w));
-    if constexpr (ETAB_NPOLY > 0) {
-#pragma unroll
-        for (int j = 1; j < NTV; j++) {
-            mx2 = bmax2_nan(mx2, bmax4(rv[j]));
-            mn2 = min_u16x2(mn2, min_u16x2(min_u16x2(rv[j].x, rv[j].y), min_u16x2(rv[j].z, rv[j].w)));
-        }
-    }
-    bool ok = n == ITEM;
-    float2 pacc = make_float2(0.0f, 0.0f);
-    float cc = 0.0f, m = NEG_INF;
-    if constexpr (ETAB_NPOLY > 0) {
-        // the polynomial vectors need the item's exponent origin first
-        uint32_t pmx = bmax4(rv[NTV]), pmn = bmin4(rv[NTV]);
-#pragma unroll
-        for (int j = NTV + 1; j < NVEC; j++) {
-            pmx = bmax2_nan(pmx, bmax4(rv[j]));
-            pmn = bmin2_nan(pmn, bmin4(rv[j]));
-        }
-        mx2 = bmax2_nan(mx2, pmx);
-        ok &= (fabsf(__fmul_rn(bf16x2_max_f(pmx), sp.invcap)) <= 1.0f) &
-              (fabsf(__fmul_rn(bf16x2_min_f(pmn), sp.invcap)) <= 1.0f);
-    }
-    float vmax = 0.0f;
-    if constexpr (ETAB_NPOLY > 0) {
-        const float lmx = bf16x2_max_f(mx2);
-        ok &= (lmx == lmx) & (min(mn2 & 0xffffu, mn2 >> 16) >= ETAB_LO);
-        vmax = warp_max_redux(lmx == lmx ? lmx : 0.0f);
-        m = s_of(vmax, sp);
-        cc = __fmul_rn(m, G4_L2E);
-        const float2 ic = make_float2(sp.invcap, sp.invcap), c2 = make_float2(sp.cap, sp.cap);
-        const float2 t2 = make_float2(sp.invT, sp.invT), l2 = make_float2(G4_L2E, G4_L2E), nc = make_float2(-cc, -cc);
-#pragma unroll
-        for (int j = NTV; j < NVEC; j++) {
-            const uint32_t wv[4] = {rv[j].x, rv[j].y, rv[j].z, rv[j].w};
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                float2 v = make_float2(__uint_as_float(__byte_perm(wv[k], 0u, 0x1044)), __uint_as_float(wv[k] & 0xffff0000u));
-                v = __fmul2_rn(tanh_poly2(__fmul2_rn(v, ic)), c2);
-                if (sp.use_t) v = __fmul2_rn(v, t2);
-                const float2 y = __ffma2_rn(v, l2, nc);
-                pacc = __fadd2_rn(pacc, make_float2(ex2_approx(y.x), ex2_approx(y.y)));
-            }
-        }
-    }
     float2 acc0 = make_float2(0.0f, 0.0f), acc1 = acc0;
 #pragma unroll
-    for (int j = 0; j < NTV; j++) {
-        if (ETAB_NPOLY == 0 && j) {
+    for (int j = 0; j < NVEC; j++) {
+        if (j) {
             mx2 = bmax2_nan(mx2, bmax4(rv[j]));
             mn2 = min_u16x2(mn2, min_u16x2(min_u16x2(rv[j].x, rv[j].y), min_u16x2(rv[j].z, rv[j].w)));
         }
         const uint32_t wv[4] = {rv[j].x, rv[j].y, rv[j].z, rv[j].w};
 #pragma unroll
         for (int k = 0; k < 4; k++) {
-            const uint32_t c = max_u16x2(wv[k], LO2);  // positive codes below the table: flagged above
+            const uint32_t c = max_u16x2(wv[k], LO2);  // positive codes below the table: flagged below
             const float2 e = make_float2(lds_f32(tbase + ((c & 0xffffu) << 2)), lds_f32(tbase + ((c >> 16) << 2)));
             if (k & 1) acc1 = __fadd2_rn(acc1, e);
             else acc0 = __fadd2_rn(acc0, e);
         }
     }
+    const float lmx = bf16x2_max_f(mx2);
+    // no NaN, no positive code below the table (negative codes are >= 0x8000)
+    const bool ok = (lmx == lmx) & (min(mn2 & 0xffffu, mn2 >> 16) >= ETAB_LO) & (n == ITEM);
     acc0 = __fadd2_rn(acc0, acc1);
     float S = acc0.x + acc0.y;
-    if constexpr (ETAB_NPOLY > 0) {
-        // the table sums to the item origin cc, per lane, then the polynomial's
-        const float em = lds_f32(tbase + ((__float_as_uint(vmax) >> 16) << 2));
-        const double r = (double)m * (double)G4_L2E - (double)cc;
-        const float scale = (float)((1.0 + r * 0.6931471805599453) / (double)em);
-        S = __fmaf_rn(S, scale, pacc.x + pacc.y);
-    }
-    if constexpr (ETAB_NPOLY == 0) {
-        const float lmx = bf16x2_max_f(mx2);
-        // no NaN, no positive code below the table (negative codes are >= 0x8000)
-        ok &= (lmx == lmx) & (min(mn2 & 0xffffu, mn2 >> 16) >= ETAB_LO);
-        vmax = warp_max_redux(lmx == lmx ? lmx : 0.0f);
-    }
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1) S += __shfl_xor_sync(FULLMASK, S, d);
     const bool redo = !__all_sync(FULLMASK, ok);
+    const float vmax = warp_max_redux(lmx == lmx ? lmx : 0.0f);
     if (lane == 0) {
-        if constexpr (ETAB_NPOLY == 0) {
-            if (!redo) {
-                m = s_of(vmax, sp);
-                cc = __fmul_rn(m, G4_L2E);
-                const float em = lds_f32(tbase + ((__float_as_uint(vmax) >> 16) << 2));
-                const double r = (double)m * (double)G4_L2E - (double)cc;
-                S = (float)((double)__fdiv_rn(S, em) * (1.0 + r * 0.6931471805599453));
-            }
+        float m = NEG_INF, cc = 0.0f;
+        if (!redo) {
+            m = s_of(vmax, sp);
+            cc = __fmul_rn(m, G4_L2E);
+            const float em = lds_f32(tbase + ((__float_as_uint(vmax) >> 16) << 2));
+            const double r = (double)m * (double)G4_L2E - (double)cc;
+            S = (float)((double)__fdiv_rn(S, em) * (1.0 + r * 0.6931471805599453));
         }
-        a.istat[it] = redo ? make_float4(NEG_INF, 0.0f, 0.0f, 1.0f) : make_float4(m, cc, S, 0.0f);
+        a.istat[it] = make_float4(m, cc, S, redo ? 1.0f : 0.0f);
     }
 }
 
@@ -1112,12 +1048,16 @@ __global__ void __launch_bounds__(COMBINE_THREADS) full_combine_kernel(SampleArg
     const int row = blockIdx.x;
     const g4s_params p = a.params.get(row);
     if (!(p.top_k <= 0 || p.top_k >= a.vocab)) return;  // uniform over the CTA
+    // resolve mode: only the draws the merge assigned to this shard
+    if (a.shard_mode == 2 && (!(p.temperature > 0.0f) || a.shard_tgt[row].w != a.shard_rank)) return;
     const SParams sp = make_sparams(a, p, row);
     const int ipr = (a.vocab + ITEM - 1) / ITEM;
     const float4 *st = a.istat + (int64_t)row * ipr;
     const float NEG_INF = -__uint_as_float(0x7f800000u);
     const float4 none = make_float4(NEG_INF, 0.0f, 0.0f, 0.0f);
-    const double u_row = p.temperature > 0.0f ? a.u[row] : 0.0;  // u may be null for greedy calls
+    // u may be null for greedy calls, and is not read for slice summaries
+    // (mode 1) or resolves (mode 2, whose target the merge computed)
+    const double u_row = (p.temperature > 0.0f && a.shard_mode == 0) ? a.u[row] : 0.0;
     // launched as a programmatic dependent of the streaming kernel: everything
     // above reads only the call's inputs; the item statistics are read after
     // the streaming grid has completed and flushed
@@ -1176,7 +1116,7 @@ __global__ void __launch_bounds__(COMBINE_THREADS) full_combine_kernel(SampleArg
             double w, prev;
             const double P = item_P(q0, w);
             const double incl = block_incl_scan_d(P, &prev, &S, sm);
-            target = (double)thr * S;
+            target = a.shard_mode == 2 ? fmin(a.shard_tgt[row].t_loc, S) : (double)thr * S;
             hit = block_min_int(t < ipr && incl >= target ? t : 0x7fffffff, sm);
             if (t == hit) { sm.hit_base = prev; sm.hit_w = w; }
         } else {
@@ -1186,7 +1126,7 @@ __global__ void __launch_bounds__(COMBINE_THREADS) full_combine_kernel(SampleArg
                 block_incl_scan_d(item_P(i < ipr ? st[i] : none, w), &prev, &tot, sm);
                 S += tot;
             }
-            target = (double)thr * S;
+            target = a.shard_mode == 2 ? fmin(a.shard_tgt[row].t_loc, S) : (double)thr * S;
             double base = 0.0;
             for (int b0 = 0; b0 < ipr && hit == 0x7fffffff; b0 += CT) {
                 double w, prev, tot;
@@ -1198,7 +1138,9 @@ __global__ void __launch_bounds__(COMBINE_THREADS) full_combine_kernel(SampleArg
             }
         }
         __syncthreads();
-        if (hit == 0x7fffffff) {
+        if (a.shard_mode == 1) {
+            need_argmax = true;  // the slice summary: S and the first maximum
+        } else if (hit == 0x7fffffff) {
             flags |= G4S_ROW_FALLBACK;
             need_argmax = true;
         } else {
@@ -1268,6 +1210,21 @@ __global__ void __launch_bounds__(COMBINE_THREADS) full_combine_kernel(SampleArg
             const double w = pow2_split((double)q.y - (double)M * (double)G4_L2E);
             tprob = (float)((double)ex2_approx(__fmaf_rn(M, G4_L2E, -q.y)) * w / S);
         }
+    }
+    if (a.shard_mode == 1) {
+        // slice summary (vocabulary-sharded mode): maximum, its first global id,
+        // and the mass sum 2^(s L2E) in units of 2^(M L2E), in the row's list slot
+        if (t == 0) {
+            const uint32_t gid = (uint32_t)(a.id_offset + token);
+            a.list_out[(int64_t)row * KMAX + 0] = (uint64_t)__float_as_uint(M) | ((uint64_t)gid << 32);
+            a.list_out[(int64_t)row * KMAX + 1] = (uint64_t)__double_as_longlong(S);
+            a.list_cnt[row] = -1;
+        }
+        return;
+    }
+    if (a.shard_mode == 2) {
+        token += a.id_offset;
+        tprob = (float)((double)tprob * a.shard_tgt[row].pscale);
     }
     if (t == 0) {
         a.out_tokens[row] = token;
@@ -1427,6 +1384,19 @@ template <int DT>
 static cudaError_t launch_full_dt(const SampleArgs &a, bool vec, cudaStream_t s, bool probs)
 {
     return vec ? launch_full_t<DT, true>(a, s, probs) : launch_full_t<DT, false>(a, s, probs);
+}
+
+template <int DT, bool VEC>
+static cudaError_t launch_combine_t(const SampleArgs &a, cudaStream_t s)
+{
+    full_combine_kernel<DT, VEC><<<(unsigned)a.rows, COMBINE_THREADS, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_full_combine(const SampleArgs &a, bool vec, cudaStream_t s)
+{
+    if (a.dtype == G4S_F32) return vec ? launch_combine_t<G4S_F32, true>(a, s) : launch_combine_t<G4S_F32, false>(a, s);
+    return vec ? launch_combine_t<G4S_BF16, true>(a, s) : launch_combine_t<G4S_BF16, false>(a, s);
 }
 
 int full_item_logits(int dtype) { return dtype == G4S_F32 ? Geo<G4S_F32>::ITEM : Geo<G4S_BF16>::ITEM; }

@@ -27,6 +27,17 @@ struct RowStat {
     int32_t token;
 };
 
+// Vocabulary-sharded full-vocabulary draw of one row, decided by the merge:
+// the shard w whose share of the cumulative mass crosses the threshold, the
+// threshold in that shard's own units, and the factor from its probabilities
+// to the row's.
+struct ShardTarget {
+    int32_t w;
+    int32_t pad;
+    double t_loc;
+    double pscale;
+};
+
 struct SampleArgs {
     const void *logits;
     int64_t row_stride;   // elements
@@ -65,6 +76,11 @@ struct SampleArgs {
     const uint64_t *glists;    // shard merge: gathered lists [gworld][rows][KMAX]
     const int32_t *gcnts;      //   and their lengths [gworld][rows]
     int32_t gworld;
+    int32_t shard_mode;        // full-path combine: 0 sample; 1 write the slice summary of each
+                               //   full-vocabulary row to list_out (count -1); 2 resolve the draws
+                               //   shard_tgt assigns to shard_rank
+    int32_t shard_rank;
+    ShardTarget *shard_tgt;    // [rows]
     int *err;                  // device error flag: a bounded wait ran out (nullable)
     const float *sc_table;     // full path, bf16 rows: the softcap table of `softcap` (nullable)
     const float *e_table;      // full path, bf16 rows, one temperature: the E table (nullable; see full_etab_kernel)
@@ -99,6 +115,8 @@ inline int current_device()
 int topk_stream_blocks_per_sm();
 cudaError_t launch_full(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
 cudaError_t launch_full_probs(const SampleArgs &a, int ept, bool vec, cudaStream_t s);
+// The per-row combine alone (its streaming pass already ran), for the sharded modes.
+cudaError_t launch_full_combine(const SampleArgs &a, bool vec, cudaStream_t s);
 cudaError_t launch_largek(const SampleArgs &a, cudaStream_t s);
 cudaError_t launch_topk_cluster(const SampleArgs &a, bool vec, cudaStream_t s);
 // LM head (config C4): Q4_0 weights repacked to nibble / scale planes, fp16

@@ -413,6 +413,64 @@ __device__ int top_sorted(TopkSmem &sm, int cnt, int K)
     return cnt < K ? cnt : K;
 }
 
+// sm.L[0..off[nseg]) holds nseg segments sorted descending (segment s at
+// [off[s], off[s+1]), each at most K long; nseg <= 32).  Pairwise merge rounds
+// (merge-path: each output element finds its split by a binary search), every
+// merged segment cut to its first K, leave the K largest of all, sorted
+// descending, in sm.L[0..kw); returns kw.  off needs 2 * 33 ints.
+__device__ int merge_segments(TopkSmem &sm, int *off, int nseg, int K)
+{
+    const int tid = threadIdx.x;
+    uint64_t *src = sm.L, *dst = sm.L + CAP2 / 2;
+    int *noff = off + 33;
+    while (nseg > 1) {
+        const int nn = (nseg + 1) / 2;
+        if (tid == 0) {
+            int o = 0;
+            for (int t = 0; t < nn; t++) {
+                noff[t] = o;
+                const int la = off[2 * t + 1] - off[2 * t];
+                const int lb = 2 * t + 1 < nseg ? off[2 * t + 2] - off[2 * t + 1] : 0;
+                o += min(la + lb, K);
+            }
+            noff[nn] = o;
+        }
+        __syncthreads();
+        const int total = noff[nn];
+        for (int g = tid; g < total; g += NTHREADS) {
+            int t = 0;
+            while (t + 1 < nn && noff[t + 1] <= g) t++;
+            const int i = g - noff[t];
+            const uint64_t *A = src + off[2 * t];
+            const int na = off[2 * t + 1] - off[2 * t];
+            const uint64_t *B = src + off[2 * t + 1];
+            const int nb = 2 * t + 1 < nseg ? off[2 * t + 2] - off[2 * t + 1] : 0;
+            // x = how many of the first i outputs come from A (composites are unique)
+            int lo = max(0, i - nb), hi = min(i, na);
+            while (lo < hi) {
+                const int mid = (lo + hi) >> 1;
+                if (A[mid] > B[i - 1 - mid]) lo = mid + 1;
+                else hi = mid;
+            }
+            const int x = lo, y = i - lo;
+            dst[g] = (x < na && (y >= nb || A[x] > B[y])) ? A[x] : B[y];
+        }
+        __syncthreads();
+        if (tid <= nn) off[tid] = noff[tid];
+        uint64_t *tmp = src;
+        src = dst;
+        dst = tmp;
+        nseg = nn;
+        __syncthreads();
+    }
+    const int kw = min(off[1] - off[0], K);
+    if (src != sm.L) {
+        for (int i = tid; i < kw; i += NTHREADS) sm.L[i] = src[i];
+        __syncthreads();
+    }
+    return kw;
+}
+
 // Merge of nch descending candidate lists (list c: C + c * lstride, length
 // CC[c * cstride]) into the top min(K, entries) composites, sorted descending in
 // sm.L[0..kw).  With j = ceil(K / nch), the ceil(K/j)-th largest of the lists'
@@ -444,6 +502,8 @@ __device__ int merge_lists(int K, TopkSmem &sm, const uint64_t *C, int64_t lstri
                 sm.L[i] = __ldcg(&C[lo * lstride + (i - loff[lo])]);
             }
             __syncthreads();
+            // few sorted lists: merge them (lists never hold more than K)
+            if (nch <= 32 && total <= CAP2 / 2) return merge_segments(sm, loff, nch, K);
             return top_sorted(sm, total, K);
         }
     }
@@ -578,13 +638,88 @@ __device__ __forceinline__ void finish_single_chunk(const SampleArgs &a, int row
 // Vocabulary-sharded mode, after the all-gather: one CTA per row merges the
 // shards' sorted lists (exact: the row's top K lie in the union of the
 // shards' top K) and runs the sampling tail.
+// A full-vocabulary row in the sharded mode, from the W slice summaries
+// (maximum M_w, its first global id, mass Z_w in units of 2^(M_w L2E); list
+// count -1).  Thread 0 only.  The first maximum (lowest id: the slices are in
+// id order) decides greedy rows; a draw sums S = sum_w Z_w 2^((M_w - M) L2E)
+// in fp64, then walks the slices in order to the one whose share crosses
+// fl32(u * top_p) * S: its rank resolves the draw in its own slice (shard_tgt;
+// the token stays -1 here), or, when rounding leaves the threshold past the
+// last mass, the row keeps its argmax -- DoSampleTopP's fallback
+// (src/Gemma4.Model.pas:2691-2737).
+__device__ void shard_full_row(const SampleArgs &a, int row, const g4s_params &p)
+{
+    const float NEG_INF = -__uint_as_float(0x7f800000u);
+    const int W = a.gworld;
+    float M = NEG_INF;
+    int arg = 0;
+    bool ok = true;
+    for (int w = 0; w < W; w++) {
+        ok &= __ldcg(&a.gcnts[(int64_t)w * a.rows + row]) == -1;
+        const uint64_t r0 = __ldcg(&a.glists[((int64_t)w * a.rows + row) * KMAX]);
+        const float Mw = __uint_as_float((uint32_t)r0);
+        if (Mw > M) {
+            M = Mw;
+            arg = (int)(uint32_t)(r0 >> 32);
+        }
+    }
+    const bool draw = p.temperature > 0.0f;
+    int32_t flags = G4S_ROW_FULL_PATH | (draw ? 0 : G4S_ROW_GREEDY);
+    int token = ok ? (M > NEG_INF ? arg : 0) : -1;
+    float tprob = 0.0f;
+    ShardTarget tg;
+    tg.w = -1;
+    tg.pad = 0;
+    tg.t_loc = 0.0;
+    tg.pscale = 0.0;
+    if (ok && draw && M > NEG_INF) {
+        const double Ml = (double)M * (double)G4_L2E;
+        double S = 0.0;
+        for (int w = 0; w < W; w++) {
+            const int64_t o = ((int64_t)w * a.rows + row) * KMAX;
+            const float Mw = __uint_as_float((uint32_t)__ldcg(&a.glists[o]));
+            if (Mw > NEG_INF) S += __longlong_as_double((long long)__ldcg(&a.glists[o + 1])) * exp2((double)Mw * (double)G4_L2E - Ml);
+        }
+        const float thr = __double2float_rn(a.u[row] * (double)p.top_p);
+        const double target = (double)thr * S;
+        double cum = 0.0;
+        for (int w = 0; w < W && tg.w < 0; w++) {
+            const int64_t o = ((int64_t)w * a.rows + row) * KMAX;
+            const float Mw = __uint_as_float((uint32_t)__ldcg(&a.glists[o]));
+            if (!(Mw > NEG_INF)) continue;
+            const double sc = exp2((double)Mw * (double)G4_L2E - Ml);
+            const double zs = __longlong_as_double((long long)__ldcg(&a.glists[o + 1])) * sc;
+            if (zs > 0.0 && cum + zs >= target) {
+                tg.w = w;
+                tg.t_loc = (target - cum) / sc;
+                tg.pscale = zs / S;
+            }
+            cum += zs;
+        }
+        if (tg.w >= 0) {
+            token = -1;  // resolved by rank tg.w
+        } else {
+            flags |= G4S_ROW_FALLBACK;
+            tprob = (float)(1.0 / S);  // the maximum's share: 2^0 / S
+        }
+    }
+    a.shard_tgt[row] = tg;
+    a.out_tokens[row] = token;
+    if (a.token_prob) a.token_prob[row] = tprob;
+    if (a.row_flags) a.row_flags[row] = flags;
+}
+
 __global__ void __launch_bounds__(NTHREADS) shard_merge_kernel(SampleArgs a)
 {
     __shared__ TopkSmem sm;
     const int row = blockIdx.x;
     const g4s_params p = a.params.get(row);
     const int K = p.top_k;
-    if (!(K > 0 && K <= KMAX)) return;  // the host admits top-K rows only
+    if (K <= 0 || K >= a.vocab) {
+        if (threadIdx.x == 0) shard_full_row(a, row, p);
+        return;
+    }
+    if (K > KMAX) return;  // the host admits top-K rows up to KMAX only
     const int kw = merge_lists(K, sm, a.glists + (int64_t)row * KMAX, (int64_t)a.rows * KMAX, a.gcnts + row,
                                a.rows, a.gworld);
     finish_row(a, row, p, kw, sm);

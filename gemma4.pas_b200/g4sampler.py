@@ -79,7 +79,10 @@ SIGNATURES = {
                                     c_int32, POINTER(Params), c_int32, c_float, c_void_p, c_void_p,
                                     POINTER(Outputs), c_void_p, c_void_p]),
     "g4s_shard_lists": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int64, c_int32, c_int32,
-                                  POINTER(Params), c_int32, c_void_p, c_void_p, c_void_p]),
+                                  POINTER(Params), c_int32, c_float, c_void_p, c_void_p, c_void_p]),
+    "g4s_shard_resolve": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int64, c_int32, c_int32,
+                                    POINTER(Params), c_int32, c_float, c_void_p, c_void_p, POINTER(Outputs),
+                                    c_void_p]),
     "g4s_shard_merge": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, POINTER(Params),
                                   c_int32, c_float, c_void_p, c_void_p, POINTER(Outputs), c_void_p]),
     "g4s_shard_unique_id": (c_int32, [c_void_p]),
@@ -228,12 +231,24 @@ class Sampler:
         return params_array(params), 1
 
     def shard_lists(self, logits_ptr: int, dtype: int, rows: int, slice_vocab: int, row_stride: int,
-                    id_offset: int, vocab_total: int, params, lists_ptr: int, counts_ptr: int,
+                    id_offset: int, vocab_total: int, params, softcap: float, lists_ptr: int, counts_ptr: int,
                     stream: int | None = None, check: bool = True) -> int:
         parr, pstride = self._params(params, rows)
         rc = self.lib.g4s_shard_lists(self.h, c_void_p(logits_ptr), dtype, rows, slice_vocab, row_stride, id_offset,
-                                      vocab_total, parr, pstride, c_void_p(lists_ptr), c_void_p(counts_ptr),
-                                      c_void_p(stream) if stream else None)
+                                      vocab_total, parr, pstride, softcap, c_void_p(lists_ptr),
+                                      c_void_p(counts_ptr), c_void_p(stream) if stream else None)
+        if check:
+            self._check(rc)
+        return rc
+
+    def shard_resolve(self, logits_ptr: int, dtype: int, rows: int, slice_vocab: int, row_stride: int,
+                      id_offset: int, rank: int, params, softcap: float, u_ptr: int, out_ptr: int,
+                      outputs: Outputs | None = None, stream: int | None = None, check: bool = True) -> int:
+        parr, pstride = self._params(params, rows)
+        rc = self.lib.g4s_shard_resolve(self.h, c_void_p(logits_ptr), dtype, rows, slice_vocab, row_stride,
+                                        id_offset, rank, parr, pstride, softcap, c_void_p(u_ptr), c_void_p(out_ptr),
+                                        ctypes.byref(outputs) if outputs is not None else None,
+                                        c_void_p(stream) if stream else None)
         if check:
             self._check(rc)
         return rc

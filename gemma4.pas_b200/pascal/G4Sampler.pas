@@ -19,7 +19,7 @@ interface
 const
   G4SLib = 'libg4sampler.so';
 
-  G4S_ABI_VERSION = 1;
+  G4S_ABI_VERSION = 2;
 
   G4S_OK              = 0;
   G4S_ERR_ARG         = -1;
@@ -137,12 +137,16 @@ function g4s_lmhead_sample(Ctx: PG4SCtx; Hidden: PSingle; Rows, HiddenSize: Int3
 { Vocabulary-sharded mode: compute phases (any collective) and the NCCL form. }
 function g4s_shard_lists(Ctx: PG4SCtx; Logits: Pointer; DType, Rows, SliceVocab: Int32;
   RowStride: Int64; IdOffset, VocabTotal: Int32; Params: PG4SParams;
-  ParamsStride: Int32; OutLists: Pointer; OutCounts: PInt32;
+  ParamsStride: Int32; Softcap: Single; OutLists: Pointer; OutCounts: PInt32;
   Stream: Pointer): Int32; cdecl; external G4SLib;
 function g4s_shard_merge(Ctx: PG4SCtx; Lists: Pointer; Counts: PInt32;
   World, Rows, VocabTotal: Int32; Params: PG4SParams; ParamsStride: Int32;
   Softcap: Single; U: PDouble; OutTokens: PInt32; Extra: PG4SOutputs;
   Stream: Pointer): Int32; cdecl; external G4SLib;
+function g4s_shard_resolve(Ctx: PG4SCtx; LogitsSlice: Pointer; DType, Rows,
+  SliceVocab: Int32; RowStride: Int64; IdOffset, Rank: Int32; Params: PG4SParams;
+  ParamsStride: Int32; Softcap: Single; U: PDouble; OutTokens: PInt32;
+  Extra: PG4SOutputs; Stream: Pointer): Int32; cdecl; external G4SLib;
 function g4s_shard_unique_id(Uid: PByte): Int32; cdecl; external G4SLib;
 function g4s_shard_init(Ctx: PG4SCtx; World, Rank, VocabTotal: Int32;
   Uid: PByte): Int32; cdecl; external G4SLib;

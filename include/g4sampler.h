@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define G4S_ABI_VERSION 1
+#define G4S_ABI_VERSION 2
 
 /* Byte-compatible with TSamplingParams (src/Gemma4.Model.pas:70-76):
    four 4-byte fields at offsets 0/4/8/12.  repetition_penalty is declared
@@ -241,22 +241,37 @@ int32_t g4s_lmhead_sample(g4s_ctx *ctx, const float *hidden, int32_t rows, int32
 /*
  * Vocabulary-sharded mode (no counterpart in the reference, which samples one
  * row on one host thread).  Each of W ranks holds a contiguous slice of every
- * row's logits; rows must have 0 < top_k <= 256 below the slice length (full-
- * vocabulary rows are sampled with a row split: plain g4s_sample per rank on
- * its own rows).  The row's top K lie in the union of the slices' top K, so
- * the merge is exact and every rank draws the same token as g4s_sample on the
- * whole row (ties at the K-th place to the lower global id).
+ * row's logits.  A row is a top-K row (0 < top_k <= 256, below the slice
+ * length) or a full-vocabulary row (top_k <= 0 or >= vocab_total; bf16 or f32,
+ * softcap as in g4s_sample).  A top-K row's top K lie in the union of the
+ * slices' top K, so its merge is exact and every rank draws the same token as
+ * g4s_sample on the whole row (ties at the K-th place to the lower global id).
+ * A full-vocabulary row travels as a slice summary (maximum, its first global
+ * id, the slice's mass in units of 2^(maximum log2 e), fp64; count -1): the
+ * merge takes the first global maximum for greedy rows, and for draws finds
+ * the slice whose share of the mass crosses fl32(u * top_p) * S; that rank
+ * resolves the draw inside its slice.  The token equals g4s_sample's on the
+ * whole row except where the draw lands within fp64 rounding of a token
+ * boundary.
  *
- * Two compute phases, usable with any collective:
- *   g4s_shard_lists  one slice -> per row the slice's top-K composites sorted
- *                    descending: out_lists [rows][G4S_SHARD_LIST] uint64
- *                    (value key << 32 | ~global_id), out_counts [rows] int32
- *   g4s_shard_merge  the W ranks' lists gathered as lists [W][rows][G4S_SHARD_LIST]
- *                    and counts [W][rows] -> tokens (and the optional outputs
- *                    of g4s_sample_ex for top-K rows)
+ * Three compute phases, usable with any collective:
+ *   g4s_shard_lists   one slice -> per row the slice's top-K composites sorted
+ *                     descending: out_lists [rows][G4S_SHARD_LIST] uint64
+ *                     (value key << 32 | ~global_id), out_counts [rows] int32;
+ *                     a full-vocabulary row's summary in its first two slots
+ *   g4s_shard_merge   the W ranks' lists gathered as lists [W][rows][G4S_SHARD_LIST]
+ *                     and counts [W][rows] -> tokens (and the optional outputs
+ *                     of g4s_sample_ex); a full-vocabulary draw is left -1
+ *                     when another phase must resolve it
+ *   g4s_shard_resolve (only when some row is a full-vocabulary draw) on every
+ *                     rank, same context as its lists and merge: writes the
+ *                     tokens the merge assigned to this rank; an element-wise
+ *                     max of out_tokens (and token_prob) over the ranks then
+ *                     gives every rank every token
  * and the NCCL form: g4s_shard_unique_id on one rank, the 128 bytes passed to
  * every rank, g4s_shard_init on each, then g4s_shard_sample per step (lists,
- * two ncclAllGather over NVLink, merge; stream-ordered, asynchronous).  Every
+ * two ncclAllGather over NVLink, merge, and for full-vocabulary draws the
+ * resolve and an ncclAllReduce(max); stream-ordered, asynchronous).  Every
  * rank passes the same rows, params, softcap and u.  NCCL is loaded at the
  * first g4s_shard_unique_id / g4s_shard_init (libnccl.so.2).
  */
@@ -265,11 +280,20 @@ int32_t g4s_lmhead_sample(g4s_ctx *ctx, const float *hidden, int32_t rows, int32
 
 int32_t g4s_shard_lists(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t rows, int32_t slice_vocab,
                         int64_t row_stride, int32_t id_offset, int32_t vocab_total, const g4s_params *params,
-                        int32_t params_stride, uint64_t *out_lists, int32_t *out_counts, void *stream);
+                        int32_t params_stride, float softcap, uint64_t *out_lists, int32_t *out_counts,
+                        void *stream);
 
 int32_t g4s_shard_merge(g4s_ctx *ctx, const uint64_t *lists, const int32_t *counts, int32_t world, int32_t rows,
                         int32_t vocab_total, const g4s_params *params, int32_t params_stride, float softcap,
                         const double *u, int32_t *out_tokens, const g4s_outputs *extra, void *stream);
+
+/* rank = this slice's index in the gathered lists; logits_slice, dtype,
+   slice_vocab, row_stride, id_offset, params and softcap as given to
+   g4s_shard_lists on ctx; u as given to g4s_shard_merge on ctx. */
+int32_t g4s_shard_resolve(g4s_ctx *ctx, const void *logits_slice, int32_t dtype, int32_t rows, int32_t slice_vocab,
+                          int64_t row_stride, int32_t id_offset, int32_t rank, const g4s_params *params,
+                          int32_t params_stride, float softcap, const double *u, int32_t *out_tokens,
+                          const g4s_outputs *extra, void *stream);
 
 /* 128 bytes (an ncclUniqueId) to hand to every rank's g4s_shard_init. */
 int32_t g4s_shard_unique_id(uint8_t *uid);

@@ -28,7 +28,7 @@ def test_every_declared_symbol_is_exported(g4):
 
 def test_version_and_defaults(g4):
     lib = g4.load()
-    assert lib.g4s_version() == 1
+    assert lib.g4s_version() == 2
     p = g4.Params()
     lib.g4s_params_defaults(ctypes.byref(p))
     # TSamplingParams.SetDefaults (src/Gemma4.Model.pas:346-352)
