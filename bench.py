@@ -72,7 +72,7 @@ def load_peak():
 
 def profiled_traffic():
     """DRAM bytes per launch of the full-path streaming kernel from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "full_tab_kernel_c3.md")
+    path = os.path.join(ROOT, "profiles", "full_etab_kernel_c3.md")
     try:
         m = re.search(r"dram_bytes_per_launch:\s*([0-9]+)", open(path).read())
         return int(m.group(1)) if m else None
@@ -779,9 +779,9 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": profiled_traffic(),
                          "traffic_source": "static: dram__bytes_read + dram__bytes_write of one launch in the "
-                                           "committed ncu capture (profiles/full_tab_kernel_c3.md), not measured "
+                                           "committed ncu capture (profiles/full_etab_kernel_c3.md), not measured "
                                            "in this run",
-                         "kernel": "full_stream_kernel<bf16>, timed alone (phase_mask = stream only), "
+                         "kernel": "full_etab_kernel (bf16 weight-table streaming pass), timed alone (phase_mask = stream only), "
                                    "CUDA events over K launches",
                          "kernel_mean_us": stream_us,
                          "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json), burst copy",
