@@ -10,7 +10,9 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <chrono>
 #include <string>
+#include <thread>
 
 #include "g4s_kernels.cuh"
 #include "g4sampler.h"
@@ -63,6 +65,8 @@ struct g4s_ctx {
     // vocabulary-sharded mode (g4s_shard_init)
     void *nccl_comm = nullptr;
     int shard_world = 0, shard_rank = 0, shard_vocab = 0, shard_slice = 0;
+    int64_t shard_timeout_ms = G4S_SHARD_TIMEOUT_MS_DEFAULT;  // host deadline of rendezvous and waits
+    cudaEvent_t shard_ev = nullptr;                           // g4s_shard_wait's marker
     uint64_t *sh_send = nullptr;  // [max_rows][KMAX] this rank's lists, then [max_rows] counts
     uint64_t *sh_recv = nullptr;  // [world][max_rows][KMAX], then [world][max_rows] counts
     // LM head workspace (first g4s_lmhead_sample call): fp32 logits and fp16 hidden
@@ -154,7 +158,8 @@ struct NcclApi {
     bool tried = false, ok = false;
     std::string why;
     ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
-    ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommInitRankConfig)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
     ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
     ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
@@ -181,7 +186,8 @@ static bool nccl_load()
         if (!fn) ok = false;
     };
     sym(g_nccl.GetUniqueId, "ncclGetUniqueId");
-    sym(g_nccl.CommInitRank, "ncclCommInitRank");
+    sym(g_nccl.CommInitRankConfig, "ncclCommInitRankConfig");
+    sym(g_nccl.CommGetAsyncError, "ncclCommGetAsyncError");
     sym(g_nccl.CommDestroy, "ncclCommDestroy");
     sym(g_nccl.CommAbort, "ncclCommAbort");
     sym(g_nccl.AllGather, "ncclAllGather");
@@ -194,14 +200,64 @@ static bool nccl_load()
     return ok;
 }
 
-static void shard_release(g4s_ctx *ctx)
+// Ends the context's sharded state: the communicator destroyed (or aborted,
+// which also ends its kernels still waiting on a peer), the exchange buffers
+// freed once the context's own stream is idle.
+static void shard_release(g4s_ctx *ctx, bool abort = false)
 {
-    if (ctx->nccl_comm && g_nccl.ok) g_nccl.CommDestroy((ncclComm_t)ctx->nccl_comm);
+    if (ctx->nccl_comm && g_nccl.ok) {
+        if (abort) g_nccl.CommAbort((ncclComm_t)ctx->nccl_comm);
+        else g_nccl.CommDestroy((ncclComm_t)ctx->nccl_comm);
+    }
     ctx->nccl_comm = nullptr;
     if (ctx->sh_send) cudaFree(ctx->sh_send);
     if (ctx->sh_recv) cudaFree(ctx->sh_recv);
     ctx->sh_send = ctx->sh_recv = nullptr;
     ctx->shard_world = 0;
+}
+
+// Polls a non-blocking communicator until its state leaves ncclInProgress, at
+// most limit_ms of host time (*timed_out then set).  Returns the state, or the
+// query's own error.
+static ncclResult_t nccl_settle(ncclComm_t comm, int64_t limit_ms, bool *timed_out)
+{
+    const auto t0 = std::chrono::steady_clock::now();
+    *timed_out = false;
+    for (;;) {
+        ncclResult_t st = ncclInProgress;
+        const ncclResult_t r = g_nccl.CommGetAsyncError(comm, &st);
+        if (r != ncclSuccess) return r;
+        if (st != ncclInProgress) return st;
+        const int64_t ms =
+            std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+        if (ms >= limit_ms) {
+            *timed_out = true;
+            return ncclInProgress;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(100));
+    }
+}
+
+// After a group of collectives on the context's communicator: a non-blocking
+// communicator may still be enqueueing them (ncclInProgress); wait for that
+// within the shard deadline, aborting the communicator when it passes.
+static int32_t nccl_group_done(g4s_ctx *ctx, const char *who, const char *what, ncclResult_t r)
+{
+    if (r == ncclInProgress) {
+        bool to = false;
+        r = nccl_settle((ncclComm_t)ctx->nccl_comm, ctx->shard_timeout_ms, &to);
+        if (to) {
+            shard_release(ctx, true);
+            return fail(ctx, G4S_ERR_TIMEOUT, "%s: %s not enqueued within %lld ms; communicator aborted", who, what,
+                        (long long)ctx->shard_timeout_ms);
+        }
+    }
+    if (r != ncclSuccess) {
+        const char *why = g_nccl.GetErrorString(r);
+        shard_release(ctx, true);
+        return fail(ctx, G4S_ERR_NCCL, "%s: %s: %s; communicator aborted", who, what, why);
+    }
+    return G4S_OK;
 }
 
 // Per-row parameters into the launch arguments: a broadcast record travels in
@@ -475,6 +531,19 @@ int32_t g4s_destroy(g4s_ctx *ctx)
 {
     if (!ctx) return G4S_OK;
     DeviceGuard guard(ctx->device);
+    if (ctx->nccl_comm && g_nccl.ok && ctx->stream && ctx->shard_ev &&
+        cudaEventRecord(ctx->shard_ev, ctx->stream) == cudaSuccess) {
+        // a sharded step still waiting on a peer ends by an abort after the
+        // shard deadline, so that the synchronisation below returns
+        const auto t0 = std::chrono::steady_clock::now();
+        while (cudaEventQuery(ctx->shard_ev) == cudaErrorNotReady &&
+               std::chrono::steady_clock::now() - t0 < std::chrono::milliseconds(ctx->shard_timeout_ms))
+            std::this_thread::sleep_for(std::chrono::microseconds(200));
+        if (cudaEventQuery(ctx->shard_ev) == cudaErrorNotReady) {
+            g_nccl.CommAbort((ncclComm_t)ctx->nccl_comm);
+            ctx->nccl_comm = nullptr;
+        }
+    }
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     for (int k = 0; k < PSLOTS; k++)
         if (ctx->params_ev[k]) cudaEventDestroy(ctx->params_ev[k]);
@@ -485,6 +554,7 @@ int32_t g4s_destroy(g4s_ctx *ctx)
     if (ctx->h_u) cudaFree(ctx->h_u);
     if (ctx->h_tok) cudaFree(ctx->h_tok);
     shard_release(ctx);
+    if (ctx->shard_ev) cudaEventDestroy(ctx->shard_ev);
     if (ctx->lm_logits) cudaFree(ctx->lm_logits);
     if (ctx->lm_xh) cudaFree(ctx->lm_xh);
     delete ctx;
@@ -954,6 +1024,7 @@ int32_t g4s_shard_init(g4s_ctx *ctx, int32_t world, int32_t rank, int32_t vocab_
     if (slice > ctx->max_vocab)
         return fail(ctx, G4S_ERR_CAPACITY, "%s: slice %d exceeds the context's max_vocab %d", who, slice, ctx->max_vocab);
     if (ctx->nccl_comm) return fail(ctx, G4S_ERR_STATE, "%s: the context is already sharded", who);
+    if (ctx->sh_send || ctx->sh_recv) shard_release(ctx);  // buffers kept by an abort whose stream was busy
     if (!nccl_load()) return fail(ctx, G4S_ERR_UNAVAILABLE, "%s: %s", who, g_nccl.why.c_str());
     DeviceGuard guard(ctx->device);
     if (!guard.ok) return fail(ctx, G4S_ERR_CUDA, "%s: cannot select device %d", who, ctx->device);
@@ -964,13 +1035,34 @@ int32_t g4s_shard_init(g4s_ctx *ctx, int32_t world, int32_t rank, int32_t vocab_
         shard_release(ctx);
         return fail(ctx, G4S_ERR_NOMEM, "%s: cannot allocate the exchange buffers", who);
     }
+    if (!ctx->shard_ev && cudaEventCreateWithFlags(&ctx->shard_ev, cudaEventDisableTiming) != cudaSuccess) {
+        cudaGetLastError();
+        shard_release(ctx);
+        return fail(ctx, G4S_ERR_CUDA, "%s: cannot create the wait event", who);
+    }
     ncclUniqueId id;
     memcpy(&id, uid, sizeof(id));
+    // non-blocking communicator: the rendezvous runs in NCCL's threads while
+    // this thread polls it against the deadline, so a rank that never joins
+    // ends the call with G4S_ERR_TIMEOUT instead of blocking it for good
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
     ncclComm_t comm = nullptr;
-    const ncclResult_t r = g_nccl.CommInitRank(&comm, world, id, rank);
-    if (r != ncclSuccess) {
+    ncclResult_t r = g_nccl.CommInitRankConfig(&comm, world, id, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        if (comm) g_nccl.CommAbort(comm);
         shard_release(ctx);
-        return fail(ctx, G4S_ERR_NCCL, "%s: ncclCommInitRank: %s", who, g_nccl.GetErrorString(r));
+        return fail(ctx, G4S_ERR_NCCL, "%s: ncclCommInitRankConfig: %s", who, g_nccl.GetErrorString(r));
+    }
+    bool to = false;
+    r = nccl_settle(comm, ctx->shard_timeout_ms, &to);
+    if (to || r != ncclSuccess) {
+        g_nccl.CommAbort(comm);
+        shard_release(ctx);
+        if (to)
+            return fail(ctx, G4S_ERR_TIMEOUT, "%s: the %d ranks did not meet within %lld ms (a rank did not join)", who,
+                        world, (long long)ctx->shard_timeout_ms);
+        return fail(ctx, G4S_ERR_NCCL, "%s: communicator set-up: %s", who, g_nccl.GetErrorString(r));
     }
     ctx->nccl_comm = comm;
     ctx->shard_world = world;
@@ -1011,12 +1103,24 @@ int32_t g4s_shard_sample(g4s_ctx *ctx, const void *logits_slice, int32_t dtype, 
                           softcap, send, send_cnt, s, &rp);
     if (rc != G4S_OK) return rc;
     ncclComm_t comm = (ncclComm_t)ctx->nccl_comm;
+    {
+        // an error the communicator raised since the last step (a peer that
+        // failed) ends the sharded state before anything more is queued
+        ncclResult_t st = ncclSuccess;
+        if (g_nccl.CommGetAsyncError(comm, &st) == ncclSuccess && st != ncclSuccess && st != ncclInProgress) {
+            shard_release(ctx, true);
+            return fail(ctx, G4S_ERR_NCCL, "%s: communicator error: %s; communicator aborted", who,
+                        g_nccl.GetErrorString(st));
+        }
+    }
+    // a call of a non-blocking communicator succeeds or is still in progress
+    auto ok = [](ncclResult_t x) { return x == ncclSuccess || x == ncclInProgress; };
     ncclResult_t r = g_nccl.GroupStart();
-    if (r == ncclSuccess) r = g_nccl.AllGather(send, recv, (size_t)rows * KMAX_, ncclUint64, comm, s);
-    if (r == ncclSuccess) r = g_nccl.AllGather(send_cnt, recv_cnt, (size_t)rows, ncclInt32, comm, s);
+    if (ok(r)) r = g_nccl.AllGather(send, recv, (size_t)rows * KMAX_, ncclUint64, comm, s);
+    if (ok(r)) r = g_nccl.AllGather(send_cnt, recv_cnt, (size_t)rows, ncclInt32, comm, s);
     const ncclResult_t r2 = g_nccl.GroupEnd();
-    if (r == ncclSuccess) r = r2;
-    if (r != ncclSuccess) return fail(ctx, G4S_ERR_NCCL, "%s: all-gather: %s", who, g_nccl.GetErrorString(r));
+    if (ok(r)) r = r2;
+    if ((rc = nccl_group_done(ctx, who, "all-gather", r)) != G4S_OK) return rc;
     // the merge reads list w of row i at recv + w * rows * KMAX + i * KMAX
     rc = shard_merge_core(ctx, recv, recv_cnt, W, rows, ctx->shard_vocab, params, params_stride, softcap, u, out_tokens,
                           extra, s, &rp);
@@ -1027,12 +1131,79 @@ int32_t g4s_shard_sample(g4s_ctx *ctx, const void *logits_slice, int32_t dtype, 
                             params_stride, softcap, u, out_tokens, extra, s, &rp);
     if (rc != G4S_OK) return rc;
     r = g_nccl.GroupStart();
-    if (r == ncclSuccess) r = g_nccl.AllReduce(out_tokens, out_tokens, (size_t)rows, ncclInt32, ncclMax, comm, s);
-    if (r == ncclSuccess && extra && extra->token_prob)
+    if (ok(r)) r = g_nccl.AllReduce(out_tokens, out_tokens, (size_t)rows, ncclInt32, ncclMax, comm, s);
+    if (ok(r) && extra && extra->token_prob)
         r = g_nccl.AllReduce(extra->token_prob, extra->token_prob, (size_t)rows, ncclFloat32, ncclMax, comm, s);
     const ncclResult_t r3 = g_nccl.GroupEnd();
-    if (r == ncclSuccess) r = r3;
-    if (r != ncclSuccess) return fail(ctx, G4S_ERR_NCCL, "%s: all-reduce: %s", who, g_nccl.GetErrorString(r));
+    if (ok(r)) r = r3;
+    return nccl_group_done(ctx, who, "all-reduce", r);
+}
+
+int32_t g4s_shard_set_timeout(g4s_ctx *ctx, int64_t ms)
+{
+    if (!ctx) return fail(nullptr, G4S_ERR_ARG, "g4s_shard_set_timeout: ctx is NULL");
+    if (ms < 0) return fail(ctx, G4S_ERR_ARG, "g4s_shard_set_timeout: negative deadline %lld", (long long)ms);
+    ctx->shard_timeout_ms = ms ? ms : G4S_SHARD_TIMEOUT_MS_DEFAULT;
+    return G4S_OK;
+}
+
+int32_t g4s_shard_wait(g4s_ctx *ctx, void *stream, int64_t timeout_ms)
+{
+    static const char *who = "g4s_shard_wait";
+    if (!ctx) return fail(nullptr, G4S_ERR_ARG, "%s: ctx is NULL", who);
+    if (!ctx->nccl_comm) return fail(ctx, G4S_ERR_STATE, "%s: the context is not sharded", who);
+    DeviceGuard guard(ctx->device);
+    if (!guard.ok) return fail(ctx, G4S_ERR_CUDA, "%s: cannot select device %d", who, ctx->device);
+    cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
+    if (cudaEventRecord(ctx->shard_ev, s) != cudaSuccess) {
+        const cudaError_t e = cudaGetLastError();
+        return fail(ctx, G4S_ERR_CUDA, "%s: event record: %s", who, cudaGetErrorString(e));
+    }
+    const int64_t limit = timeout_ms > 0 ? timeout_ms : ctx->shard_timeout_ms;
+    const auto t0 = std::chrono::steady_clock::now();
+    auto elapsed_ms = [&]() {
+        return (int64_t)std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0)
+            .count();
+    };
+    ncclComm_t comm = (ncclComm_t)ctx->nccl_comm;
+    for (;;) {
+        const cudaError_t q = cudaEventQuery(ctx->shard_ev);
+        if (q == cudaSuccess) return G4S_OK;
+        if (q != cudaErrorNotReady) return fail(ctx, G4S_ERR_CUDA, "%s: %s", who, cudaGetErrorString(q));
+        ncclResult_t st = ncclSuccess;
+        const ncclResult_t r = g_nccl.CommGetAsyncError(comm, &st);
+        const bool failed = r != ncclSuccess || (st != ncclSuccess && st != ncclInProgress);
+        const bool late = elapsed_ms() >= limit;
+        if (failed || late) {
+            // the abort ends the communicator's kernels that still wait on a
+            // peer; the stream then drains (bounded), and the exchange buffers go
+            const char *why = g_nccl.GetErrorString(r != ncclSuccess ? r : st);
+            g_nccl.CommAbort(comm);
+            ctx->nccl_comm = nullptr;
+            const auto t1 = std::chrono::steady_clock::now();
+            while (cudaEventQuery(ctx->shard_ev) == cudaErrorNotReady &&
+                   std::chrono::steady_clock::now() - t1 < std::chrono::milliseconds(limit))
+                std::this_thread::sleep_for(std::chrono::microseconds(200));
+            const bool drained = cudaEventQuery(ctx->shard_ev) == cudaSuccess;
+            if (drained) shard_release(ctx);
+            if (late)
+                return fail(ctx, G4S_ERR_TIMEOUT,
+                            "%s: the step did not finish within %lld ms (a rank stalled or left); communicator "
+                            "aborted%s",
+                            who, (long long)limit, drained ? "" : ", stream still busy");
+            return fail(ctx, G4S_ERR_NCCL, "%s: communicator error: %s; communicator aborted", who, why);
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+int32_t g4s_shard_abort(g4s_ctx *ctx)
+{
+    if (!ctx) return fail(nullptr, G4S_ERR_ARG, "g4s_shard_abort: ctx is NULL");
+    if (!ctx->nccl_comm) return G4S_OK;
+    DeviceGuard guard(ctx->device);
+    if (!guard.ok) return fail(ctx, G4S_ERR_CUDA, "g4s_shard_abort: cannot select device %d", ctx->device);
+    shard_release(ctx, true);
     return G4S_OK;
 }
 

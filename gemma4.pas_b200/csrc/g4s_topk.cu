@@ -485,7 +485,10 @@ __device__ int merge_lists(int K, TopkSmem &sm, const uint64_t *C, int64_t lstri
         // with coalesced loads, then one selection there -- no chains of
         // dependent global loads
         int *loff = reinterpret_cast<int *>(sm.hist);  // list start offsets (nch + 1 <= 256 ints)
-        const int cc = tid < nch ? __ldcg(&CC[tid * cstride]) : 0;
+        // counts clamped to a list's capacity: a list slot never holds more,
+        // and an exchange cut short (an aborted collective) cannot send a read
+        // past it
+        const int cc = tid < nch ? min(max(__ldcg(&CC[tid * cstride]), 0), KMAX) : 0;
         int total;
         const int off = block_excl_scan(cc, &total, sm.scan);
         if (total <= CAP2) {
@@ -512,7 +515,7 @@ __device__ int merge_lists(int K, TopkSmem &sm, const uint64_t *C, int64_t lstri
     // lower bound t2: the mm-th largest of the lists' j-th entries
     for (int c = tid; c < nch; c += NTHREADS) {
         uint64_t h = 0;
-        if (__ldcg(&CC[c * cstride]) >= j) h = __ldcg(&C[c * lstride + j - 1]);
+        if (min(__ldcg(&CC[c * cstride]), KMAX) >= j) h = __ldcg(&C[c * lstride + j - 1]);
         sm.L[c] = h;
     }
     __syncthreads();
@@ -546,7 +549,7 @@ __device__ int merge_lists(int K, TopkSmem &sm, const uint64_t *C, int64_t lstri
 #pragma unroll
     for (int r = 0; r < CPT; r++) {
         const int c = tid * CPT + r;
-        pc[r] = c < nch ? prefix_at_least(C + c * lstride, __ldcg(&CC[c * cstride]), t2) : 0;
+        pc[r] = c < nch ? prefix_at_least(C + c * lstride, min(__ldcg(&CC[c * cstride]), KMAX), t2) : 0;
         cnt += pc[r];
     }
     const int slots = nch * K;

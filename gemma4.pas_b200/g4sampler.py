@@ -86,6 +86,9 @@ SIGNATURES = {
     "g4s_shard_merge": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, POINTER(Params),
                                   c_int32, c_float, c_void_p, c_void_p, POINTER(Outputs), c_void_p]),
     "g4s_shard_unique_id": (c_int32, [c_void_p]),
+    "g4s_shard_set_timeout": (c_int32, [c_void_p, c_int64]),
+    "g4s_shard_wait": (c_int32, [c_void_p, c_void_p, c_int64]),
+    "g4s_shard_abort": (c_int32, [c_void_p]),
     "g4s_shard_init": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_void_p]),
     "g4s_shard_sample": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int64, POINTER(Params), c_int32,
                                    c_float, c_void_p, c_void_p, POINTER(Outputs), c_void_p]),
@@ -265,17 +268,39 @@ class Sampler:
             self._check(rc)
         return rc
 
-    def shard_init(self, world: int, rank: int, vocab_total: int, uid: bytes) -> None:
+    def shard_init(self, world: int, rank: int, vocab_total: int, uid: bytes, check: bool = True) -> int:
         buf = ctypes.create_string_buffer(bytes(uid), SHARD_UID_BYTES)
-        self._check(self.lib.g4s_shard_init(self.h, world, rank, vocab_total, buf))
+        rc = self.lib.g4s_shard_init(self.h, world, rank, vocab_total, buf)
+        if check:
+            self._check(rc)
+        return rc
+
+    def shard_set_timeout(self, ms: int) -> None:
+        """Host deadline (ms) of the rendezvous and of shard_wait; 0 restores the default."""
+        self._check(self.lib.g4s_shard_set_timeout(self.h, ms))
+
+    def shard_wait(self, stream: int | None = None, timeout_ms: int = 0, check: bool = True) -> int:
+        """Waits for the queued sharded work; aborts the communicator when a peer
+        stalls past the deadline (ERR_TIMEOUT) or fails (ERR_NCCL)."""
+        rc = self.lib.g4s_shard_wait(self.h, c_void_p(stream) if stream else None, timeout_ms)
+        if check:
+            self._check(rc)
+        return rc
+
+    def shard_abort(self) -> None:
+        self._check(self.lib.g4s_shard_abort(self.h))
 
     def shard_sample(self, logits_ptr: int, dtype: int, rows: int, row_stride: int, params, softcap: float,
-                     u_ptr: int, out_ptr: int, outputs: Outputs | None = None, stream: int | None = None) -> None:
+                     u_ptr: int, out_ptr: int, outputs: Outputs | None = None, stream: int | None = None,
+                     check: bool = True) -> int:
         parr, pstride = self._params(params, rows)
-        self._check(self.lib.g4s_shard_sample(self.h, c_void_p(logits_ptr), dtype, rows, row_stride, parr, pstride,
-                                              softcap, c_void_p(u_ptr), c_void_p(out_ptr),
-                                              ctypes.byref(outputs) if outputs is not None else None,
-                                              c_void_p(stream) if stream else None))
+        rc = self.lib.g4s_shard_sample(self.h, c_void_p(logits_ptr), dtype, rows, row_stride, parr, pstride,
+                                       softcap, c_void_p(u_ptr), c_void_p(out_ptr),
+                                       ctypes.byref(outputs) if outputs is not None else None,
+                                       c_void_p(stream) if stream else None)
+        if check:
+            self._check(rc)
+        return rc
 
     def lmhead_sample(self, hidden_ptr: int, rows: int, hidden: int, nib_ptr: int, scales_ptr: int, vocab: int,
                       params, softcap: float, u_ptr: int, out_ptr: int, outputs: Outputs | None = None,

@@ -148,6 +148,10 @@ function g4s_shard_resolve(Ctx: PG4SCtx; LogitsSlice: Pointer; DType, Rows,
   ParamsStride: Int32; Softcap: Single; U: PDouble; OutTokens: PInt32;
   Extra: PG4SOutputs; Stream: Pointer): Int32; cdecl; external G4SLib;
 function g4s_shard_unique_id(Uid: PByte): Int32; cdecl; external G4SLib;
+function g4s_shard_set_timeout(Ctx: PG4SCtx; Ms: Int64): Int32; cdecl; external G4SLib;
+function g4s_shard_wait(Ctx: PG4SCtx; Stream: Pointer; TimeoutMs: Int64): Int32;
+  cdecl; external G4SLib;
+function g4s_shard_abort(Ctx: PG4SCtx): Int32; cdecl; external G4SLib;
 function g4s_shard_init(Ctx: PG4SCtx; World, Rank, VocabTotal: Int32;
   Uid: PByte): Int32; cdecl; external G4SLib;
 function g4s_shard_sample(Ctx: PG4SCtx; LogitsSlice: Pointer; DType, Rows: Int32;

@@ -303,10 +303,33 @@ int32_t g4s_shard_unique_id(uint8_t *uid);
 int32_t g4s_shard_init(g4s_ctx *ctx, int32_t world, int32_t rank, int32_t vocab_total, const uint8_t *uid);
 
 /* One sharded step: logits_slice is this rank's slice (rows x row_stride
-   elements, device memory); u and out_tokens are device pointers. */
+   elements, device memory); u and out_tokens are device pointers.  An error
+   the communicator reported since the previous step ends the sharded state
+   (communicator aborted, G4S_ERR_NCCL) before anything is queued. */
 int32_t g4s_shard_sample(g4s_ctx *ctx, const void *logits_slice, int32_t dtype, int32_t rows, int64_t row_stride,
                          const g4s_params *params, int32_t params_stride, float softcap, const double *u,
                          int32_t *out_tokens, const g4s_outputs *extra, void *stream);
+
+/*
+ * Failure handling of the NCCL form.  The communicator is non-blocking: every
+ * host-side wait on the other ranks has a deadline (default
+ * G4S_SHARD_TIMEOUT_MS_DEFAULT, per context).  g4s_shard_init returns
+ * G4S_ERR_TIMEOUT when the W ranks do not meet in time (a rank that never
+ * joins).  g4s_shard_wait waits for the work queued on `stream` (NULL: the
+ * context stream) up to timeout_ms (<= 0: the context's deadline), watching
+ * the communicator's asynchronous error; when a peer stalled or left (deadline
+ * passed: G4S_ERR_TIMEOUT) or the communicator failed (G4S_ERR_NCCL), it
+ * aborts the communicator -- which ends its kernels still waiting on a peer --
+ * and leaves the context unsharded; the step's tokens are then invalid, the
+ * context's other entry points keep working, and g4s_shard_init may be called
+ * again with a new unique id.  g4s_shard_abort does the same on a rank that
+ * learned of a failure elsewhere (a heartbeat, a store).  g4s_destroy waits at
+ * most the deadline for a sharded step on the context stream, then aborts.
+ */
+#define G4S_SHARD_TIMEOUT_MS_DEFAULT 60000
+int32_t g4s_shard_set_timeout(g4s_ctx *ctx, int64_t ms);   /* 0: back to the default */
+int32_t g4s_shard_wait(g4s_ctx *ctx, void *stream, int64_t timeout_ms);
+int32_t g4s_shard_abort(g4s_ctx *ctx);
 
 /*
  * Weight archive (the reference's VPK, read by TWeightStore,

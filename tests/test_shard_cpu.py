@@ -151,5 +151,8 @@ def test_shard_abi_rejects_bad_calls(g4):
     assert lib.g4s_shard_merge(None, None, None, 2, 1, 1000, bp, 0, 30.0, None, None, None, None) == g4.ERR_ARG
     assert lib.g4s_shard_init(None, 2, 0, 262144, None) == g4.ERR_ARG
     assert lib.g4s_shard_unique_id(None) == g4.ERR_ARG
+    assert lib.g4s_shard_set_timeout(None, 1000) == g4.ERR_ARG
+    assert lib.g4s_shard_wait(None, None, 1000) == g4.ERR_ARG
+    assert lib.g4s_shard_abort(None) == g4.ERR_ARG
     assert lib.g4s_shard_sample(None, None, 0, 1, 1000, bp, 0, 30.0, None, None, None, None) == g4.ERR_ARG
     assert b"ctx is NULL" in lib.g4s_last_error(None)
