@@ -334,28 +334,37 @@ def run_c4(dev, peak, steps=20):
     p = g4.make_params(1.0, 64, 0.95)
     cap = torch.cuda.Stream(device=dev)
 
-    def call(st=None):
+    def call(st=None, mask=0):
+        o = g4.Outputs()
+        o.phase_mask = mask
         s.lmhead_sample(hd.data_ptr(), rows, H, nib.data_ptr(), sc.data_ptr(), VOCAB, p, SOFTCAP, u.data_ptr(),
-                        out.data_ptr(), stream=st)
+                        out.data_ptr(), outputs=o, stream=st)
 
-    for _ in range(3):
-        call()
-    torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=cap):
-        for _ in range(steps):
-            call(cap.cuda_stream)
-    g.replay()
-    torch.cuda.synchronize()
-    ts = []
-    for _ in range(5):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
+    def timed(mask):
+        for _ in range(3):
+            call(mask=mask)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap):
+            for _ in range(steps):
+                call(cap.cuda_stream, mask)
         g.replay()
-        b.record()
-        b.synchronize()
-        ts.append(a.elapsed_time(b) * 1e3 / steps)
-    del g
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(5):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()  # replay runs on the current stream
+            g.replay()
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b) * 1e3 / steps)
+        del g
+        return ts, out.cpu().numpy().copy()
+
+    # default: top-K selection in the LM head's epilogue; unfused: the logits
+    # written to memory and sampled by the top-K kernels
+    ts, tok_fused = timed(0)
+    ts_unfused, tok_unfused = timed(g4.PHASE_LMHEAD_UNFUSED)
     # agreement with the reference's own LM-head arithmetic on a few rows: the
     # fp32 CpuMatVecQ4 and the Q8_1 + DP4A path of its GPU shaders, each
     # followed by the oracle's DoSample
@@ -383,10 +392,13 @@ def run_c4(dev, peak, steps=20):
     return {"us_per_step": us, "rows_per_s": rows / (us * 1e-6), "weight_gbs": wbytes / (us * 1e-6) / 1e9,
             "hbm_frac_of_peak": wbytes / (us * 1e-6) / 1e9 / peak,
             "tflops": 2.0 * rows * VOCAB * H / (us * 1e-6) / 1e12,
+            "unfused_us_per_step": statistics.median(ts_unfused),
+            "tokens_fused_equal_unfused": int((tok_fused == tok_unfused).sum()),
             "agreement_with_reference_lmhead": agree,
             "config": "C4: hidden 64 x 2560 fp32 -> LM head 262144 x 2560 Q4_0 (tcgen05 fp16 MMA, dequantized "
-                      "weights in TMEM, fp32 accumulate) -> top_k 64, T=1, top_p 0.95; median of 5 replays of a "
-                      "20-call CUDA graph"}
+                      "weights in TMEM, fp32 accumulate) with top-K selection in its epilogue -> top_k 64, T=1, "
+                      "top_p 0.95; median of 5 replays of a 20-call CUDA graph; unfused_us_per_step: the same "
+                      "with the logits written to memory and sampled by the top-K kernels"}
 
 
 def run_c5(rank, world, local, dev, peak, steps=50):

@@ -75,6 +75,8 @@ struct g4s_ctx {
     int *dev_err = nullptr;  // device error flag in the workspace (a bounded wait that ran out), read by g4s_device_status
     int64_t wait_limit = 0;  // g4s_set_wait_limit (test hook; 0 = the kernels' own limits)
     size_t lm_logits_n = 0, lm_xh_n = 0;
+    void *lm_fused = nullptr;  // fused LM head: candidates, counts, thresholds, sample logits
+    size_t lm_fused_n = 0;
     // g4s_sample_host staging
     void *h_logits = nullptr;
     double *h_u = nullptr;
@@ -557,6 +559,7 @@ int32_t g4s_destroy(g4s_ctx *ctx)
     if (ctx->shard_ev) cudaEventDestroy(ctx->shard_ev);
     if (ctx->lm_logits) cudaFree(ctx->lm_logits);
     if (ctx->lm_xh) cudaFree(ctx->lm_xh);
+    if (ctx->lm_fused) cudaFree(ctx->lm_fused);
     delete ctx;
     return G4S_OK;
 }
@@ -720,6 +723,101 @@ int32_t g4s_q4_repack(const uint8_t *blocks, int32_t vocab, int32_t hidden, uint
     return G4S_OK;
 }
 
+// The LM head with top-K selection in its epilogue: taken when the caller
+// wants no logits and every row is a top-K row (0 < top_k <= KMAX, below the
+// vocabulary) of a vocabulary of at least two waves of tiles; returns
+// G4S_ERR_UNAVAILABLE (nothing launched, no error recorded) for other calls.
+// Launches: activations to fp16 tiles; the LM head over the sample tiles (one
+// per SM) into the sample buffer and its group maxima; per row the threshold
+// and the sample's candidates; the LM head over the other tiles with the
+// candidate epilogue; per row the exact top K and the sampling tail.  The
+// middle three are a chain of programmatic dependents: the last one's CTAs
+// take the SMs' free slots during the sample pass and wait for the
+// thresholds only in their epilogue.
+static int32_t lmhead_sample_fused(g4s_ctx *ctx, const char *who, const float *hidden, int rows, int H,
+                                   const float *norm_weight, float norm_eps, const uint8_t *nibbles,
+                                   const uint16_t *scales, int vocab, const g4s_params *params, int params_stride,
+                                   float softcap, const double *u, int32_t *out_tokens, const g4s_outputs *extra,
+                                   cudaStream_t s)
+{
+    g4s_outputs ex;
+    memset(&ex, 0, sizeof(ex));
+    if (extra) ex = *extra;
+    const int ntiles = (vocab + LMHEAD_TILE - 1) / LMHEAD_TILE;
+    const int nA = ctx->sm_count;
+    if (ex.full_probs || (ex.phase_mask & G4S_PHASE_LMHEAD_UNFUSED) || ntiles < 2 * nA || nA * LMHEAD_TILE / 32 > 2048)
+        return G4S_ERR_UNAVAILABLE;
+    bool any_draw = false;
+    int max_k = 0;
+    for (int r = 0; r < (params_stride ? rows : 1); r++) {
+        const g4s_params &p = params[r];
+        if (p.temperature != p.temperature || p.top_p != p.top_p)
+            return fail(ctx, G4S_ERR_ARG, "%s: NaN temperature/top_p in params[%d]", who, r);
+        if (p.top_k <= 0 || p.top_k > KMAX_ || p.top_k >= vocab) return G4S_ERR_UNAVAILABLE;
+        any_draw |= p.temperature > 0.0f;
+        max_k = std::max(max_k, (int)p.top_k);
+    }
+    if (any_draw && !u) return fail(ctx, G4S_ERR_ARG, "%s: u is NULL but a row has temperature > 0", who);
+    if ((ex.cand_ids || ex.cand_probs) && ex.cand_stride < max_k)
+        return fail(ctx, G4S_ERR_ARG, "%s: cand_stride %d < largest top_k %d", who, ex.cand_stride, max_k);
+    // workspace: candidates [rows][vocab] (a row can never hold more), counts,
+    // thresholds, sample logits [rows][ns]
+    const int ns = nA * LMHEAD_TILE;
+    auto al = [](size_t x) { return (x + 255u) & ~(size_t)255u; };
+    const size_t o_cnt = al((size_t)rows * vocab * sizeof(uint64_t));
+    const size_t o_thr = o_cnt + al((size_t)rows * sizeof(int32_t));
+    const size_t o_smp = o_thr + al((size_t)rows * sizeof(uint64_t));
+    const size_t o_gmx = o_smp + al((size_t)rows * ns * sizeof(float));
+    const size_t need = o_gmx + al((size_t)rows * (ns / 32) * sizeof(uint32_t));
+    if (ctx->lm_fused_n < need) {
+        if (ctx->lm_fused) cudaFree(ctx->lm_fused);
+        ctx->lm_fused = nullptr;
+        ctx->lm_fused_n = 0;
+        if (cudaMalloc(&ctx->lm_fused, need) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(ctx, G4S_ERR_NOMEM, "%s: cannot allocate %zu bytes of candidate lists", who, need);
+        }
+        ctx->lm_fused_n = need;
+    }
+    char *base = (char *)ctx->lm_fused;
+    LmCand c;
+    c.cand = (uint64_t *)base;
+    c.cnt = (int32_t *)(base + o_cnt);
+    c.thr = (uint64_t *)(base + o_thr);
+    c.cap = vocab;
+    c.sample = (float *)(base + o_smp);
+    c.gmax = (uint32_t *)(base + o_gmx);
+    c.ns = ns;
+    SampleArgs a;
+    memset(&a, 0, sizeof(a));
+    a.rows = rows;
+    a.vocab = vocab;
+    a.dtype = G4S_F32;
+    a.softcap = softcap;
+    a.invcap = softcap > 0.0f ? 1.0f / softcap : 0.0f;
+    a.u = u;
+    a.out_tokens = out_tokens;
+    a.token_prob = ex.token_prob;
+    a.row_flags = ex.row_flags;
+    a.cand_ids = ex.cand_ids;
+    a.cand_probs = ex.cand_probs;
+    a.cand_stride = ex.cand_stride;
+    a.err = ctx->dev_err;
+    int32_t rc = stage_params(ctx, who, params, params_stride, rows, s, a.params);
+    if (rc != G4S_OK) return rc;
+    __half *xh = (__half *)ctx->lm_xh;
+    cudaError_t e = launch_lmhead_prep(hidden, rows, H, norm_weight, norm_eps, xh, s);
+    if (e == cudaSuccess)
+        e = launch_lmhead_part(xh, rows, H, nibbles, scales, vocab, 0, nA, nullptr, 0, 1, &c, ctx->dev_err, s);
+    if (e == cudaSuccess) e = launch_lm_threshold(a, c, s);
+    if (e == cudaSuccess)
+        e = launch_lmhead_part(xh, rows, H, nibbles, scales, vocab, nA, ntiles - nA, nullptr, 0, 2, &c, ctx->dev_err,
+                               s);
+    if (e == cudaSuccess) e = launch_lm_finish(a, c, s);
+    if (e != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "%s: launch failed: %s", who, cudaGetErrorString(e));
+    return G4S_OK;
+}
+
 int32_t g4s_lmhead_sample(g4s_ctx *ctx, const float *hidden, int32_t rows, int32_t hidden_size,
                           const float *norm_weight, float norm_eps, const uint8_t *nibbles, const uint16_t *scales,
                           int32_t vocab, const g4s_params *params, int32_t params_stride, float softcap,
@@ -742,17 +840,7 @@ int32_t g4s_lmhead_sample(g4s_ctx *ctx, const float *hidden, int32_t rows, int32
     if (!guard.ok) return fail(ctx, G4S_ERR_CUDA, "%s: cannot select device %d", who, ctx->device);
     cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
     float *logits = out_logits;
-    const size_t need_l = (size_t)rows * vocab, need_x = (size_t)LMHEAD_MAX_ROWS * hidden_size;
-    if (!logits && ctx->lm_logits_n < need_l) {
-        if (ctx->lm_logits) cudaFree(ctx->lm_logits);
-        ctx->lm_logits = nullptr;
-        ctx->lm_logits_n = 0;
-        if (cudaMalloc(&ctx->lm_logits, need_l * sizeof(float)) != cudaSuccess) {
-            cudaGetLastError();
-            return fail(ctx, G4S_ERR_NOMEM, "%s: cannot allocate %zu bytes of logits", who, need_l * sizeof(float));
-        }
-        ctx->lm_logits_n = need_l;
-    }
+    const size_t need_x = (size_t)LMHEAD_MAX_ROWS * hidden_size;
     if (ctx->lm_xh_n < need_x) {
         if (ctx->lm_xh) cudaFree(ctx->lm_xh);
         ctx->lm_xh = nullptr;
@@ -763,7 +851,23 @@ int32_t g4s_lmhead_sample(g4s_ctx *ctx, const float *hidden, int32_t rows, int32
         }
         ctx->lm_xh_n = need_x;
     }
-    if (!logits) logits = ctx->lm_logits;
+    if (!logits) {
+        int32_t rc = lmhead_sample_fused(ctx, who, hidden, rows, hidden_size, norm_weight, norm_eps, nibbles, scales,
+                                         vocab, params, params_stride, softcap, u, out_tokens, extra, s);
+        if (rc != G4S_ERR_UNAVAILABLE) return rc;  // else: a call the fused path does not take
+        const size_t need_l = (size_t)rows * vocab;
+        if (ctx->lm_logits_n < need_l) {
+            if (ctx->lm_logits) cudaFree(ctx->lm_logits);
+            ctx->lm_logits = nullptr;
+            ctx->lm_logits_n = 0;
+            if (cudaMalloc(&ctx->lm_logits, need_l * sizeof(float)) != cudaSuccess) {
+                cudaGetLastError();
+                return fail(ctx, G4S_ERR_NOMEM, "%s: cannot allocate %zu bytes of logits", who, need_l * sizeof(float));
+            }
+            ctx->lm_logits_n = need_l;
+        }
+        logits = ctx->lm_logits;
+    }
     const cudaError_t e = launch_lmhead(hidden, rows, hidden_size, norm_weight, norm_eps, nibbles, scales, vocab,
                                         (__half *)ctx->lm_xh, logits, ctx->dev_err, s);
     if (e != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "%s: launch failed: %s", who, cudaGetErrorString(e));

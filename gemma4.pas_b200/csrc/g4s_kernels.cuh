@@ -129,6 +129,41 @@ cudaError_t launch_q4_repack(const uint8_t *blocks, int vocab, int hidden, uint8
 cudaError_t launch_lmhead(const float *hidden, int rows, int H, const float *norm_w, float eps, const uint8_t *nib,
                           const uint16_t *scales, int vocab, __half *xh, float *logits, int *err, cudaStream_t s);
 constexpr int LMHEAD_MAX_ROWS = 64;
+constexpr int LMHEAD_TILE = 256;  // vocab rows per CTA of the LM head
+
+// LM head with top-K selection in its epilogue (no logits round trip).  The
+// vocabulary's first sample_tiles tiles go first, their logits into a small
+// sample buffer [rows][ns]; per row, the K-th largest of the sample's 32-id
+// group maxima is a lower bound of the row's K-th largest logit (at least K
+// sample logits lie at or above it), so every logit of the final top K is at
+// or above it: the sample's logits there, and the rest of the vocabulary's
+// from the fused epilogue of the second part, are appended as composites to
+// the row's candidate list (capacity: the whole vocabulary, so it never
+// overflows), from which the exact top K is selected.
+struct LmCand {
+    uint64_t *cand;        // [rows][cap] candidate composites (unordered)
+    int32_t *cnt;          // [rows] candidates appended
+    uint64_t *thr;         // [rows] threshold composite
+    int64_t cap;           // candidates per row (>= vocab)
+    float *sample;         // [rows][ns] logits of the sample tiles
+    uint32_t *gmax;        // [rows][ns / 32] the sample's 32-id group maxima (keys; 0: none valid)
+    int ns;                // sample length (sample_tiles * LMHEAD_TILE)
+};
+// Part of the LM head: tiles [tile0, tile0 + ntiles).  mode 0: logits to
+// `logits` (row stride ldl); mode 1: the sample tiles (logits to c.sample,
+// group maxima to c.gmax); mode 2: the candidate epilogue (waits for the
+// preceding kernel, the threshold pass, before its epilogue: launched as its
+// programmatic dependent, so its main loop overlaps the sample pass).
+cudaError_t launch_lmhead_part(const __half *xh, int rows, int H, const uint8_t *nib, const uint16_t *scales,
+                               int vocab, int tile0, int ntiles, float *logits, int ldl, int mode,
+                               const LmCand *c, int *err, cudaStream_t s);
+cudaError_t launch_lmhead_prep(const float *hidden, int rows, int H, const float *norm_w, float eps, __half *xh,
+                               cudaStream_t s);
+// per row: the threshold from the sample's group maxima, the sample's candidates
+// appended (a programmatic dependent of the sample pass)
+cudaError_t launch_lm_threshold(const SampleArgs &a, const LmCand &c, cudaStream_t s);
+// per row: the exact top K among the candidates, then the sampling tail
+cudaError_t launch_lm_finish(const SampleArgs &a, const LmCand &c, cudaStream_t s);
 
 // Vocabulary-sharded mode: the gathered per-shard lists merged into each row's
 // top-K, then the sampling tail (one CTA per row).

@@ -12,6 +12,8 @@
 //   scales  [hidden/64][vocab][2]      fp16 bits
 #include <cuda_fp16.h>
 
+#include <cstring>
+
 #include "g4s_device.cuh"
 #include "g4s_kernels.cuh"
 
@@ -115,7 +117,10 @@ constexpr int TC_RAW_BYTES = TC_ROWS * 16 * TC_G;  // 8 KB of nibbles per stage
 constexpr int TC_SC_BYTES = TC_ROWS * 2 * TC_G;    // 1 KB of scales per stage
 constexpr int TC_RAW_STAGE = TC_RAW_BYTES + TC_SC_BYTES;
 constexpr int TC_NBARS = 2 * TC_RS + 2 * TC_BS + 4 * TC_AS;
-constexpr int TC_SMEM = TC_BS * TC_B_BYTES + TC_RS * TC_RAW_STAGE + 8 * TC_NBARS + 16;  // + mbarriers, TMEM address
+constexpr int TC_THR_BYTES = 64 * 12;          // the fused epilogue's per-row thresholds (composite, value)
+constexpr int TC_STG_CAP = 32;                  // fused epilogue: staged candidates per batch row
+constexpr int TC_SMEM = TC_BS * TC_B_BYTES + TC_RS * TC_RAW_STAGE + 8 * TC_NBARS + 16 + TC_THR_BYTES;  // + mbarriers,
+                                                                                               // TMEM address
 // TMEM columns: accumulators [mt][64 batch columns] at 0..127, dequantized A
 // operands at 128 + (stage * 2 + mt) * 32 (32 columns = 64 fp16 k-values per lane)
 static_assert(TC_TMEM_A + TC_AS * 2 * (TC_KC / 2) <= TC_TMEM_COLS, "A stages exceed the TMEM allocation");
@@ -123,6 +128,7 @@ static_assert(TC_TMEM_A + TC_AS * 2 * (TC_KC / 2) <= TC_TMEM_COLS, "A stages exc
 // consumed before the slot is refilled, and a stage's A slot is rewritten only
 // after the MMAs of stage c - TC_AS, which follow the previous stage's.
 static_assert(TC_RS > TC_AS && TC_BS > TC_AS, "pipeline depths");
+static_assert(256 + 64 * TC_STG_CAP * 8 <= TC_RS * TC_RAW_STAGE, "candidate staging fits the nibble ring");
 // TC_CPS CTAs share the SM's 512 TMEM columns; the launch asks for enough
 // shared memory that one more cannot become resident and wait in tcgen05.alloc.
 constexpr int TC_SMEM_MIN = (228 * 1024) / (TC_CPS + 1) - 1023;
@@ -225,15 +231,28 @@ __device__ __forceinline__ void tc_arrive(uint32_t bar)
 // A wait for the u-th completion of a barrier uses parity u & 1; a wait for a
 // slot to be released before its first use uses parity 1, which a fresh
 // barrier reports as complete.
+//
+// The CTA's tile is tile0 + blockIdx.x.  Epilogue by MODE:
+//   0  the logits, row b of the batch at logits + b * ldl, indexed by vocab id;
+//   1  (sample tiles) the same into fc.sample, plus per batch row the largest
+//      key of each warp's 32 consecutive ids into fc.gmax;
+//   2  per batch row b, every logit whose composite is at or above the row's
+//      threshold fc.thr[b] appended to the row's candidate list (slots from
+//      fc.cnt[b]); a float compare against the threshold's value screens the
+//      logits first (it passes a superset: equal values, and -0 against +0).
+//      The thresholds come from the preceding kernel, so this mode waits for
+//      it (griddepcontrol.wait) after its main loop.
+template <int MODE>
 __global__ void __launch_bounds__(TC_THREADS_ALL, TC_CPS) lmhead_tc_kernel(const __half *__restrict__ xt,
                                                                       const uint8_t *__restrict__ nib,
                                                                       const uint16_t *__restrict__ scales, int rows,
-                                                                      int vocab, int H, float *__restrict__ logits,
-                                                                      int *__restrict__ err)
+                                                                      int vocab, int H, int tile0,
+                                                                      float *__restrict__ logits, int ldl,
+                                                                      LmCand fc, int *__restrict__ err)
 {
     extern __shared__ __align__(1024) uint8_t tc_raw[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int v0 = blockIdx.x * TC_ROWS;
+    const int v0 = (tile0 + blockIdx.x) * TC_ROWS;
     const int nch = H / TC_KC;
     const int nrows = min(TC_ROWS, vocab - v0);  // a multiple of 8 (vocab is)
     const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(tc_raw);
@@ -247,6 +266,10 @@ __global__ void __launch_bounds__(TC_THREADS_ALL, TC_CPS) lmhead_tc_kernel(const
     auto a_full = [&](int mt, int i) { return bars + 8 * (2 * TC_RS + 2 * TC_BS + mt * TC_AS + i); };
     auto ab_empty = [&](int mt, int i) { return bars + 8 * (2 * TC_RS + 2 * TC_BS + 2 * TC_AS + mt * TC_AS + i); };
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(rawbase + TC_RS * TC_RAW_STAGE + 8 * TC_NBARS);
+    uint64_t *thr_s = reinterpret_cast<uint64_t *>(rawbase + TC_RS * TC_RAW_STAGE + 8 * TC_NBARS + 16);
+    float *thrf_s = reinterpret_cast<float *>(thr_s + 64);
+    // the next kernel in the stream (a programmatic dependent) may start now
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (warp == TC_MMA_WARP) {
         const uint32_t slot = (uint32_t)__cvta_generic_to_shared(tmem_slot);
@@ -417,6 +440,19 @@ __global__ void __launch_bounds__(TC_THREADS_ALL, TC_CPS) lmhead_tc_kernel(const
         // this M-tile's last MMAs (and so all of them) completed: read the accumulators
         if (!failed && !tc_wait(ab_empty(mt, (nch - 1) % TC_AS), ((nch - 1) / TC_AS) & 1)) failed = true;
     }
+    if constexpr (MODE == 2) {
+        // the thresholds: written by the preceding kernel, complete and visible
+        // after the wait
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (tid < 64) {
+            const uint64_t t = tid < rows ? __ldcg(&fc.thr[tid]) : ~0ull;
+            const uint32_t tk = comp_key(t);
+            thr_s[tid] = t;
+            // keys below 2^23 stand for no float (NaN bit patterns): every valid
+            // logit (> -1e30) passes the screen then; rows past `rows` never
+            thrf_s[tid] = tid >= rows ? __uint_as_float(0x7f800000u) : tk >= 0x00800000u ? key2f(tk) : -3.0e38f;
+        }
+    }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     const bool bad = __syncthreads_or(failed);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -438,10 +474,84 @@ __global__ void __launch_bounds__(TC_THREADS_ALL, TC_CPS) lmhead_tc_kernel(const
         }
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         const int v = v0 + mt * 128 + 32 * q + lane;
-        if (v < vocab) {
+        if constexpr (MODE == 2) {
+            // candidates staged per batch row in the (now idle) nibble ring:
+            // shared-memory slot counters in the loop, then one global
+            // atomicAdd per row for the CTA's whole block of them
+            int *cnt_s = reinterpret_cast<int *>(rawbase);
+            uint64_t *stg = reinterpret_cast<uint64_t *>(rawbase + 256);
+            if (tid < 64) cnt_s[tid] = 0;
+            // the screen as straight-line code: one bit per batch row whose
+            // logit reaches the row's threshold value
+            uint32_t m[2] = {0u, 0u};
+            const float4 *tf4 = reinterpret_cast<const float4 *>(thrf_s);
 #pragma unroll
-            for (int b = 0; b < 64; b++)
-                if (b < rows) logits[(int64_t)b * vocab + v] = __uint_as_float(d[b]);
+            for (int b4 = 0; b4 < 16; b4++) {
+                const float4 t = tf4[b4];
+                const uint32_t bits = (uint32_t)(__uint_as_float(d[4 * b4]) >= t.x) |
+                                      ((uint32_t)(__uint_as_float(d[4 * b4 + 1]) >= t.y) << 1) |
+                                      ((uint32_t)(__uint_as_float(d[4 * b4 + 2]) >= t.z) << 2) |
+                                      ((uint32_t)(__uint_as_float(d[4 * b4 + 3]) >= t.w) << 3);
+                m[b4 >> 3] |= bits << (4 * (b4 & 7));
+            }
+            if (v >= vocab) m[0] = m[1] = 0u;
+            asm volatile("bar.sync 1, %0;" ::"n"(TC_DQ_WARPS * 32) : "memory");
+            // the few rows any lane flagged: their column re-read from TMEM by
+            // the whole warp (a compact loop: this code runs once per CTA)
+#pragma unroll 1
+            for (int hh = 0; hh < 2; hh++) {
+                const uint32_t mine = hh ? m[1] : m[0];
+                uint32_t w = __reduce_or_sync(0xffffffffu, mine);
+                while (w) {
+                    const int bit = __ffs(w) - 1;
+                    w &= w - 1u;
+                    const int b = 32 * hh + bit;
+                    uint32_t xr;
+                    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(xr) : "r"(taddr + b));
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                    if ((mine >> bit) & 1u) {
+                        const uint32_t k = cand_key(__uint_as_float(xr));
+                        const uint64_t c = composite(k, (uint32_t)v);
+                        if (k != 0u && c >= thr_s[b]) {
+                            const int slot = atomicAdd(&cnt_s[b], 1);
+                            if (slot < TC_STG_CAP) stg[b * TC_STG_CAP + slot] = c;
+                            else fc.cand[(int64_t)b * fc.cap + atomicAdd(&fc.cnt[b], 1)] = c;  // overflow: rare
+                        }
+                    }
+                }
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(TC_DQ_WARPS * 32) : "memory");
+            if (tid < rows) {
+                const int n = min(cnt_s[tid], TC_STG_CAP);
+                if (n > 0) {
+                    const int base = atomicAdd(&fc.cnt[tid], n);
+                    for (int i = 0; i < n; i++) fc.cand[(int64_t)tid * fc.cap + base + i] = stg[tid * TC_STG_CAP + i];
+                }
+            }
+        } else {
+            float *out = MODE == 1 ? fc.sample : logits;
+            const int ld = MODE == 1 ? fc.ns : ldl;
+            if (v < vocab) {
+#pragma unroll
+                for (int b = 0; b < 64; b++)
+                    if (b < rows) out[(int64_t)b * ld + v] = __uint_as_float(d[b]);
+            }
+            if constexpr (MODE == 1) {
+                // the warp's 32 ids form one group: its largest key, batch row b
+                // by lane b % 32 (two rounds), one coalesced store per round
+                const int grp = (v0 + mt * 128 + 32 * q) >> 5, ng = fc.ns >> 5;
+                uint32_t mine[2] = {0u, 0u};
+#pragma unroll
+                for (int b = 0; b < 64; b++) {
+                    const uint32_t k = v < vocab ? cand_key(__uint_as_float(d[b])) : 0u;
+                    uint32_t mk;
+                    asm("redux.sync.max.u32 %0, %1, 0xffffffff;" : "=r"(mk) : "r"(k));
+                    if ((b & 31) == lane) mine[b >> 5] = mk;
+                }
+#pragma unroll
+                for (int h = 0; h < 2; h++)
+                    if (32 * h + lane < rows) fc.gmax[(int64_t)(32 * h + lane) * ng + grp] = mine[h];
+            }
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -460,22 +570,66 @@ cudaError_t launch_q4_repack(const uint8_t *blocks, int vocab, int hidden, uint8
     return cudaGetLastError();
 }
 
-cudaError_t launch_lmhead(const float *hidden, int rows, int H, const float *norm_w, float eps, const uint8_t *nib,
-                          const uint16_t *scales, int vocab, __half *xh, float *logits, int *err, cudaStream_t s)
+template <int MODE>
+static cudaError_t set_lmhead_attr()
 {
     static bool attr[MAX_DEVICES] = {};
     const int dev = current_device();
-    if (dev < 0 || dev >= MAX_DEVICES || !attr[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(lmhead_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_LAUNCH);
-        if (e != cudaSuccess) return e;
-        if (dev >= 0 && dev < MAX_DEVICES) attr[dev] = true;
-    }
+    if (dev >= 0 && dev < MAX_DEVICES && attr[dev]) return cudaSuccess;
+    const cudaError_t e =
+        cudaFuncSetAttribute(lmhead_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_LAUNCH);
+    if (e == cudaSuccess && dev >= 0 && dev < MAX_DEVICES) attr[dev] = true;
+    return e;
+}
+
+cudaError_t launch_lmhead_prep(const float *hidden, int rows, int H, const float *norm_w, float eps, __half *xh,
+                               cudaStream_t s)
+{
     lmhead_prep_tc_kernel<<<64, 256, 0, s>>>(hidden, rows, H, norm_w, eps, xh);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    lmhead_tc_kernel<<<(unsigned)((vocab + TC_ROWS - 1) / TC_ROWS), TC_THREADS_ALL, TC_SMEM_LAUNCH, s>>>(xh, nib, scales, rows,
-                                                                                              vocab, H, logits, err);
     return cudaGetLastError();
+}
+
+cudaError_t launch_lmhead_part(const __half *xh, int rows, int H, const uint8_t *nib, const uint16_t *scales,
+                               int vocab, int tile0, int ntiles, float *logits, int ldl, int mode,
+                               const LmCand *c, int *err, cudaStream_t s)
+{
+    static_assert(TC_ROWS == LMHEAD_TILE, "tile size in the launch interface");
+    if (ntiles <= 0) return cudaSuccess;
+    LmCand fc;
+    memset(&fc, 0, sizeof(fc));
+    if (c) fc = *c;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ntiles);
+    cfg.blockDim = dim3(TC_THREADS_ALL);
+    cfg.dynamicSmemBytes = TC_SMEM_LAUNCH;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaError_t e;
+    if (mode == 2) {
+        if ((e = set_lmhead_attr<2>()) != cudaSuccess) return e;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, lmhead_tc_kernel<2>, xh, nib, scales, rows, vocab, H, tile0, (float *)nullptr,
+                                  0, fc, err);
+    }
+    if (mode == 1) {
+        if ((e = set_lmhead_attr<1>()) != cudaSuccess) return e;
+        return cudaLaunchKernelEx(&cfg, lmhead_tc_kernel<1>, xh, nib, scales, rows, vocab, H, tile0, (float *)nullptr,
+                                  0, fc, err);
+    }
+    if ((e = set_lmhead_attr<0>()) != cudaSuccess) return e;
+    return cudaLaunchKernelEx(&cfg, lmhead_tc_kernel<0>, xh, nib, scales, rows, vocab, H, tile0, logits, ldl, fc, err);
+}
+
+cudaError_t launch_lmhead(const float *hidden, int rows, int H, const float *norm_w, float eps, const uint8_t *nib,
+                          const uint16_t *scales, int vocab, __half *xh, float *logits, int *err, cudaStream_t s)
+{
+    cudaError_t e = launch_lmhead_prep(hidden, rows, H, norm_w, eps, xh, s);
+    if (e != cudaSuccess) return e;
+    return launch_lmhead_part(xh, rows, H, nib, scales, vocab, 0, (vocab + TC_ROWS - 1) / TC_ROWS, logits, vocab, 0,
+                              nullptr, err, s);
 }
 
 }  // namespace g4s

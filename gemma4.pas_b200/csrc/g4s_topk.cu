@@ -728,6 +728,124 @@ __global__ void __launch_bounds__(NTHREADS) shard_merge_kernel(SampleArgs a)
     finish_row(a, row, p, kw, sm);
 }
 
+// ---------------------------------------------------------------------------
+// LM head with top-K selection in its epilogue (g4s_lmhead_sample without
+// logits output): the two per-row steps around the fused LM head launch.
+// ---------------------------------------------------------------------------
+
+// Warp-aggregated append of this lane's composite c (when `pass`) to the list
+// `out` at the slot counter *cnt.
+__device__ __forceinline__ void warp_append(bool pass, uint64_t c, uint64_t *out, int *cnt)
+{
+    const int lane = threadIdx.x & 31;
+    const unsigned m = __ballot_sync(FULLMASK, pass);
+    if (!m) return;
+    int base = 0;
+    if (lane == 0) base = atomicAdd(cnt, __popc(m));
+    base = __shfl_sync(FULLMASK, base, 0);
+    if (pass) out[base + __popc(m & ((1u << lane) - 1u))] = c;
+}
+
+// One CTA per row, a programmatic dependent of the sample pass.  The sample's
+// logits come in 32-id groups whose largest keys the sample pass wrote; a key
+// t with at least K group maxima at or above it (the lower edge of the
+// histogram bin holding the K-th largest, refined while many more remain) is
+// the row's threshold: K groups hold a logit at or above it, so the row's K-th
+// largest logit is too.  Only groups whose maximum reaches t can hold sample
+// logits at or above it; theirs start the row's candidate list.  Fewer than K
+// valid maxima (logits at or below -1e30, NaNs): t = 1, every valid logit a
+// candidate.  The threshold composite is t << 32 (every id of key t).
+constexpr int LMT_PER = 8;  // group maxima per thread (sample groups <= 2048)
+__global__ void __launch_bounds__(NTHREADS) lm_threshold_kernel(SampleArgs a, LmCand c)
+{
+    __shared__ TopkSmem sm;
+    __shared__ int napp, ngrp;
+    __shared__ int grp[2048];
+    const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = a.params.get(row).top_k;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the sample pass is complete
+    const float *x = c.sample + (int64_t)row * c.ns;
+    const int ng = c.ns / 32;  // c.ns is a multiple of LMHEAD_TILE
+    uint32_t gk[LMT_PER];
+#pragma unroll
+    for (int j = 0; j < LMT_PER; j++) {
+        const int g = tid + j * NTHREADS;
+        gk[j] = g < ng ? __ldcg(&c.gmax[(int64_t)row * ng + g]) : 0u;
+    }
+    if (tid == 0) napp = ngrp = 0;
+    const uint32_t t = hist_select(
+        [&](auto fn) {
+#pragma unroll
+            for (int j = 0; j < LMT_PER; j++) fn(gk[j]);
+        },
+        K, K + 64, sm);
+    // the groups to rescan
+#pragma unroll
+    for (int j = 0; j < LMT_PER; j++)
+        if (gk[j] >= t) grp[atomicAdd(&ngrp, 1)] = tid + j * NTHREADS;
+    __syncthreads();
+    const int n = ngrp;
+    uint64_t *out = c.cand + (int64_t)row * c.cap;
+    // warp w rescans groups w, w + NWARPS, ...: four loads in flight per lane
+    for (int i0 = warp; i0 < n; i0 += 4 * NWARPS) {
+        float v[4];
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            const int i = i0 + r * NWARPS;
+            v[r] = i < n ? __ldcg(&x[grp[i] * 32 + lane]) : 0.0f;
+        }
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            const int i = i0 + r * NWARPS;
+            const uint32_t k = cand_key(v[r]);
+            const uint32_t id = i < n ? (uint32_t)(grp[i] * 32 + lane) : 0u;
+            warp_append(i < n && k >= t, composite(k, id), out, &napp);
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        c.cnt[row] = napp;
+        c.thr[row] = (uint64_t)t << 32;
+    }
+}
+
+// One CTA per row: the exact top K of the candidate list (composites are
+// unique), then the same tail as every top-K path.  Lists longer than the
+// shared-memory buffer (heavy ties at the threshold) take an exact radix
+// selection over global memory.
+__global__ void __launch_bounds__(NTHREADS) lm_finish_kernel(SampleArgs a, LmCand c)
+{
+    __shared__ TopkSmem sm;
+    __shared__ int ngot;
+    const int row = blockIdx.x, tid = threadIdx.x;
+    const g4s_params p = a.params.get(row);
+    const int K = p.top_k;
+    const int n = (int)min((int64_t)max(__ldcg(&c.cnt[row]), 0), c.cap);
+    const uint64_t *C = c.cand + (int64_t)row * c.cap;
+    int kw;
+    if (n <= CAP2) {
+        for (int i = tid; i < n; i += NTHREADS) sm.L[i] = __ldcg(&C[i]);
+        __syncthreads();
+        kw = top_sorted(sm, n, K);
+    } else {
+        const uint64_t kth = radix_kth(
+            [&](auto fn) {
+                for (int i = tid; i < n; i += NTHREADS) fn(__ldcg(&C[i]));
+            },
+            K, sm);
+        if (tid == 0) ngot = 0;
+        __syncthreads();
+        for (int i = tid; i < n; i += NTHREADS) {
+            const uint64_t v = __ldcg(&C[i]);
+            if (v >= kth) sm.L[atomicAdd(&ngot, 1)] = v;
+        }
+        __syncthreads();
+        kw = top_sorted(sm, ngot, K);
+    }
+    finish_row(a, row, p, kw, sm);
+}
+
 // Heavy ties in a chunk (more than CAP1 keys at or above the bound): exact
 // radix selection of the K-th largest composite, then the K largest sorted.
 // Out of line and rare: it rereads the chunk from global memory in rolled
@@ -1339,6 +1457,26 @@ static cudaError_t launch_cluster_t(const SampleArgs &a, cudaStream_t s)
 cudaError_t launch_shard_merge(const SampleArgs &a, cudaStream_t s)
 {
     shard_merge_kernel<<<a.rows, NTHREADS, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_lm_threshold(const SampleArgs &a, const LmCand &c, cudaStream_t s)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)a.rows);
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, lm_threshold_kernel, a, c);
+}
+
+cudaError_t launch_lm_finish(const SampleArgs &a, const LmCand &c, cudaStream_t s)
+{
+    lm_finish_kernel<<<a.rows, NTHREADS, 0, s>>>(a, c);
     return cudaGetLastError();
 }
 

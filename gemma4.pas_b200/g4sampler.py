@@ -19,6 +19,7 @@ F32, BF16 = 0, 1
 OK, ERR_ARG, ERR_CUDA, ERR_NOMEM, ERR_CAPACITY, ERR_NCCL, ERR_TIMEOUT, ERR_STATE, ERR_UNAVAILABLE = (
     0, -1, -2, -3, -4, -5, -6, -7, -8)
 ROW_FALLBACK, ROW_EMPTY, ROW_FULL_PATH, ROW_GREEDY = 1, 2, 4, 8
+PHASE_FULL_STREAM_ONLY, PHASE_LMHEAD_UNFUSED = 1, 2
 FLAG_HOST_STAGING = 1
 
 

@@ -42,6 +42,7 @@ const
   G4S_ROW_GREEDY    = 8;
 
   G4S_PHASE_FULL_STREAM_ONLY = 1;
+  G4S_PHASE_LMHEAD_UNFUSED = 2;
 
   G4S_NOALLOC_MAX_ROWS  = 64;
   G4S_NOALLOC_MAX_LISTS = 1024;

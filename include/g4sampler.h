@@ -80,7 +80,7 @@ enum g4s_row_flag {
 };
 
 /* g4s_outputs.phase_mask bits */
-enum g4s_phase { G4S_PHASE_FULL_STREAM_ONLY = 1 };
+enum g4s_phase { G4S_PHASE_FULL_STREAM_ONLY = 1, G4S_PHASE_LMHEAD_UNFUSED = 2 };
 
 /* Optional per-row outputs (all device pointers; any may be NULL). */
 typedef struct g4s_outputs {
@@ -92,7 +92,10 @@ typedef struct g4s_outputs {
     int32_t  cand_stride;  /* >= largest top_k of the top-K rows when cand_* used  */
     int32_t  phase_mask;   /* 0 (normal).  G4S_PHASE_FULL_STREAM_ONLY: measurement
                               hook, runs only the streaming pass of full-path rows
-                              (no tokens written) so its bandwidth can be timed alone */
+                              (no tokens written) so its bandwidth can be timed alone.
+                              G4S_PHASE_LMHEAD_UNFUSED: g4s_lmhead_sample writes
+                              the logits to its buffer and samples them (the path
+                              taken with out_logits), for comparison */
     float   *full_probs;   /* [rows * vocab] full-path rows: every probability (a
                               second pass; meant for verification)                 */
 } g4s_outputs;
@@ -214,8 +217,16 @@ int32_t g4s_sample_topk_noalloc(const void *logits, int32_t dtype, int32_t rows,
  * first, CpuRmsNorm (src/Gemma4.Layers.pas:142-175) with eps norm_eps (1e-6 in
  * the reference, src/Gemma4.Types.pas:48), fused into the activation
  * prologue.  out_logits (device, rows x vocab fp32) receives the logits when
- * non-NULL; otherwise they stay in a context buffer allocated by the first
- * call.
+ * non-NULL.  Without out_logits, when every row is a top-K row (1 <= top_k <=
+ * 256, below vocab) and the vocabulary spans at least two waves of 256-row
+ * tiles (2 x the SM count), the top-K selection runs in the LM head's
+ * epilogue: the first wave of tiles (one per SM) writes its logits to a small
+ * sample buffer, each row's threshold is the K-th largest of that sample's
+ * 32-id group maxima, and the rest of the vocabulary's LM head appends only
+ * the logits at or above the threshold (by value, then lower id) to the row's
+ * candidate list, from which the exact top K is taken -- the logits never go
+ * to memory, and the tokens equal those of the unfused path.  Other calls
+ * keep the logits in a context buffer allocated by the first call.
  */
 /* Waits for the device, then reports whether a kernel of this context gave up
    a bounded wait (G4S_ERR_TIMEOUT; the flag is cleared) since the last check. */

@@ -170,3 +170,116 @@ def test_lmhead_agreement_with_reference_paths(g4, torch_cuda, oracle):
     print("C4 agreement with the reference's LM-head arithmetic:", stats)
     assert stats["ids_f32"] >= 0.95 * stats["rows"], stats
     assert stats["ids_q8"] >= 0.5 * stats["rows"], stats
+
+
+# ---------------------------------------------------------------------------
+# top-K selection in the LM head's epilogue (no logits output): the same
+# tokens, probabilities and survivor lists as the unfused path, which writes
+# the logits and samples them.
+# ---------------------------------------------------------------------------
+def _both_paths(g4, torch, h, blocks, vocab, hidden, prm, u, rows, kmax=256, with_outputs=True, norm=None):
+    bd = torch.from_numpy(blocks).cuda()
+    nib = torch.empty(vocab * hidden // 2, dtype=torch.uint8, device="cuda")
+    sc = torch.empty(vocab * hidden // 32, dtype=torch.int16, device="cuda")
+    g4.q4_repack(bd.data_ptr(), vocab, hidden, nib.data_ptr(), sc.data_ptr())
+    hd = torch.from_numpy(h).cuda()
+    ud = torch.from_numpy(u).cuda()
+    nd = torch.from_numpy(norm).cuda() if norm is not None else None
+    res = []
+    s = g4.Sampler(0, 64, vocab)
+    try:
+        for mask in (0, g4.PHASE_LMHEAD_UNFUSED):
+            out = torch.full((rows,), -5, dtype=torch.int32, device="cuda")
+            tp = torch.full((rows,), -1.0, dtype=torch.float32, device="cuda")
+            fl = torch.zeros(rows, dtype=torch.int32, device="cuda")
+            ci = torch.full((rows, kmax), -7, dtype=torch.int32, device="cuda")
+            cp = torch.full((rows, kmax), -7.0, dtype=torch.float32, device="cuda")
+            o = g4.Outputs()
+            o.phase_mask = mask
+            if with_outputs:
+                o.token_prob, o.row_flags = tp.data_ptr(), fl.data_ptr()
+                o.cand_ids, o.cand_probs, o.cand_stride = ci.data_ptr(), cp.data_ptr(), kmax
+            s.lmhead_sample(hd.data_ptr(), rows, hidden, nib.data_ptr(), sc.data_ptr(), vocab, prm, CAP,
+                            ud.data_ptr(), out.data_ptr(), outputs=o, norm_ptr=nd.data_ptr() if nd is not None else 0)
+            torch.cuda.synchronize()
+            assert s.lib.g4s_device_status(s.h) == g4.OK, s.last_error()
+            res.append({"tok": out.cpu().numpy(), "tp": tp.cpu().numpy(), "fl": fl.cpu().numpy(),
+                        "ci": ci.cpu().numpy(), "cp": cp.cpu().numpy()})
+    finally:
+        s.close()
+    return res
+
+
+def _assert_same(a, b):
+    for k in a:
+        np.testing.assert_array_equal(a[k], b[k], err_msg=k)
+
+
+def test_fused_epilogue_matches_unfused_c4(g4, torch_cuda):
+    # config C4 (64 x 2560 hidden, 262144 x 2560 Q4_0) with per-row params:
+    # K from 1 to 256, draws and greedy rows
+    rows, hidden, vocab = 64, 2560, 262144
+    h, blocks = synth.c4_inputs(rows, hidden, vocab)
+    ks = [1, 2, 20, 40, 64, 100, 200, 256]
+    prm = [(0.0 if r % 7 == 3 else 0.5 + 0.1 * (r % 9), ks[r % len(ks)], 0.5 + 0.5 * ((r * 37) % 100) / 100)
+           for r in range(rows)]
+    u = synth.uniforms(rows, 0xF4)
+    fused, unfused = _both_paths(g4, torch_cuda, h, blocks, vocab, hidden, prm, u, rows)
+    _assert_same(fused, unfused)
+    assert (fused["tok"] >= 0).all()
+
+
+def test_fused_epilogue_small_batches_and_norm(g4, torch_cuda):
+    # fewer rows, a vocabulary just above the fused path's minimum (two waves
+    # of 256-row tiles), broadcast params, the final RMSNorm in the prologue
+    dev = torch_cuda.cuda.get_device_properties(0)
+    vocab = 2 * dev.multi_processor_count * 256 + 8 * 37
+    hidden = 1024
+    for rows in (1, 7):
+        h, blocks = synth.c4_inputs(rows, hidden, vocab, seed=rows)
+        norm = (1.0 + 0.1 * np.random.default_rng(rows).standard_normal(hidden)).astype(np.float32)
+        u = synth.uniforms(rows, 0xF5, rows)
+        fused, unfused = _both_paths(g4, torch_cuda, h * 3.0, blocks, vocab, hidden, g4.make_params(0.8, 50, 0.9),
+                                     u, rows, norm=norm)
+        _assert_same(fused, unfused)
+
+
+def _blocks_const(vocab, hidden, scale_bits, nibble):
+    nblk = vocab * (hidden // 32)
+    b = np.empty((nblk, 18), dtype=np.uint8)
+    sb = np.broadcast_to(np.asarray(scale_bits, dtype=np.uint16).reshape(-1, 1), (vocab, hidden // 32)).reshape(-1)
+    b[:, 0] = (sb & 0xFF).astype(np.uint8)
+    b[:, 1] = (sb >> 8).astype(np.uint8)
+    b[:, 2:] = np.uint8(nibble | (nibble << 4))
+    return b.reshape(-1)
+
+
+def test_fused_epilogue_heavy_ties(g4, torch_cuda):
+    # every weight 0: every logit of every row equals 0, so the candidates are
+    # the ids up to the threshold group's first id (more than the shared-memory
+    # list for K = 200: the exact radix selection over global memory)
+    rows, hidden, vocab = 4, 512, 131072
+    blocks = _blocks_const(vocab, hidden, 0x3C00, 8)  # nibble 8 = value 0
+    h = np.ones((rows, hidden), np.float32)
+    prm = [(1.0, 200, 1.0), (0.0, 64, 0.9), (0.7, 256, 0.5), (1.0, 3, 1.0)]
+    u = synth.uniforms(rows, 0xF6)
+    fused, unfused = _both_paths(g4, torch_cuda, h, blocks, vocab, hidden, prm, u, rows)
+    _assert_same(fused, unfused)
+    for r, (_, K, _) in enumerate(prm):
+        assert fused["tok"][r] < K  # ties: the K lowest ids survive
+        np.testing.assert_array_equal(fused["ci"][r, :K], np.arange(K))
+
+
+def test_fused_epilogue_logits_rising_with_id(g4, torch_cuda):
+    # logit(v) grows with v: the sample (the lowest ids) gives a threshold that
+    # nearly the whole rest of the vocabulary passes -- every row's candidate
+    # list holds ~all ids (the exact radix path); tokens still equal
+    rows, hidden, vocab = 3, 256, 131072
+    sc = (np.linspace(0.001, 0.01, vocab).astype(np.float16)).view(np.uint16)
+    blocks = _blocks_const(vocab, hidden, sc, 9)  # nibble 9 = value 1
+    h = np.ones((rows, hidden), np.float32)
+    prm = [(1.0, 64, 0.95), (0.0, 10, 0.9), (2.0, 256, 1.0)]
+    u = synth.uniforms(rows, 0xF7)
+    fused, unfused = _both_paths(g4, torch_cuda, h, blocks, vocab, hidden, prm, u, rows)
+    _assert_same(fused, unfused)
+    assert (fused["tok"] > vocab - 600).all()
