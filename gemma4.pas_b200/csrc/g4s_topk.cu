@@ -480,10 +480,12 @@ __device__ int merge_lists(int K, TopkSmem &sm, const uint64_t *C, int64_t lstri
                            int64_t cstride, int nch)
 {
     const int tid = threadIdx.x;
-    if (nch < 256 && nch <= NTHREADS) {
-        // few entries in all (the usual case): every list read whole into sm.L
-        // with coalesced loads, then one selection there -- no chains of
-        // dependent global loads
+    if (nch <= 8) {
+        // a few lists (the shards of the sharded mode, the long chunks of the
+        // streaming pass): every list read whole into sm.L with coalesced
+        // loads, then merged there -- no chains of dependent global loads.
+        // More lists (the chunked pass's 32 per row): the bound below keeps
+        // the copy to about K entries, cheaper than merging them all
         int *loff = reinterpret_cast<int *>(sm.hist);  // list start offsets (nch + 1 <= 256 ints)
         // counts clamped to a list's capacity: a list slot never holds more,
         // and an exchange cut short (an aborted collective) cannot send a read
