@@ -823,6 +823,9 @@ __global__ void __launch_bounds__(NTHREADS) lm_finish_kernel(SampleArgs a, LmCan
     const int row = blockIdx.x, tid = threadIdx.x;
     const g4s_params p = a.params.get(row);
     const int K = p.top_k;
+    // a programmatic dependent of the candidate pass: its launch overlaps that
+    // pass's last wave; the candidates are read once it has completed
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int n = (int)min((int64_t)max(__ldcg(&c.cnt[row]), 0), c.cap);
     const uint64_t *C = c.cand + (int64_t)row * c.cap;
     int kw;
@@ -1478,8 +1481,16 @@ cudaError_t launch_lm_threshold(const SampleArgs &a, const LmCand &c, cudaStream
 
 cudaError_t launch_lm_finish(const SampleArgs &a, const LmCand &c, cudaStream_t s)
 {
-    lm_finish_kernel<<<a.rows, NTHREADS, 0, s>>>(a, c);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)a.rows);
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, lm_finish_kernel, a, c);
 }
 
 cudaError_t launch_topk_cluster(const SampleArgs &a, bool vec, cudaStream_t s)
