@@ -76,3 +76,13 @@ def test_create_without_gpu_reports_unavailable(g4):
     assert b"no CUDA device" in lib.g4s_last_error(None)
     with pytest.raises(g4.G4SError):
         g4.Sampler(0, 8, 1000)
+
+
+def test_pascal_unit_declares_every_symbol():
+    # the binding a maintainer adds to the reference (not compiled here: no FPC)
+    # names every entry point of the header, with the header's ABI version
+    pas = open(os.path.join(ROOT, "gemma4.pas_b200", "pascal", "G4Sampler.pas")).read()
+    for s in declared_symbols():
+        assert re.search(r"(function|procedure)\s+" + s + r"\b", pas), s
+    ver = re.search(r"#define G4S_ABI_VERSION (\d+)", open(HEADER).read()).group(1)
+    assert re.search(r"G4S_ABI_VERSION\s*=\s*" + ver + r"\s*;", pas)
