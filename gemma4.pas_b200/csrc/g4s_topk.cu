@@ -28,6 +28,8 @@
 //            transcription.
 #include <cooperative_groups.h>
 
+#include <algorithm>
+
 #include "g4s_device.cuh"
 #include "g4s_kernels.cuh"
 
@@ -757,58 +759,63 @@ __device__ __forceinline__ void warp_append(bool pass, uint64_t c, uint64_t *out
 // logits at or above it; theirs start the row's candidate list.  Fewer than K
 // valid maxima (logits at or below -1e30, NaNs): t = 1, every valid logit a
 // candidate.  The threshold composite is t << 32 (every id of key t).
-constexpr int LMT_PER = 8;  // group maxima per thread (sample groups <= 2048)
+constexpr int LMT_PER = 8;     // group maxima per thread (sample groups <= 2048)
+constexpr int LMT_CTAS = LMHEAD_MAX_ROWS;  // one row per CTA: the candidate part's CTAs
+                                          // wait for this pass, so its latency counts
 __global__ void __launch_bounds__(NTHREADS) lm_threshold_kernel(SampleArgs a, LmCand c)
 {
     __shared__ TopkSmem sm;
     __shared__ int napp, ngrp;
     __shared__ int grp[2048];
-    const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int K = a.params.get(row).top_k;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the sample pass is complete
-    const float *x = c.sample + (int64_t)row * c.ns;
     const int ng = c.ns / 32;  // c.ns is a multiple of LMHEAD_TILE
-    uint32_t gk[LMT_PER];
+    for (int row = blockIdx.x; row < a.rows; row += gridDim.x) {
+        const int K = a.params.get(row).top_k;
+        const float *x = c.sample + (int64_t)row * c.ns;
+        uint32_t gk[LMT_PER];
 #pragma unroll
-    for (int j = 0; j < LMT_PER; j++) {
-        const int g = tid + j * NTHREADS;
-        gk[j] = g < ng ? __ldcg(&c.gmax[(int64_t)row * ng + g]) : 0u;
-    }
-    if (tid == 0) napp = ngrp = 0;
-    const uint32_t t = hist_select(
-        [&](auto fn) {
-#pragma unroll
-            for (int j = 0; j < LMT_PER; j++) fn(gk[j]);
-        },
-        K, K + 64, sm);
-    // the groups to rescan
-#pragma unroll
-    for (int j = 0; j < LMT_PER; j++)
-        if (gk[j] >= t) grp[atomicAdd(&ngrp, 1)] = tid + j * NTHREADS;
-    __syncthreads();
-    const int n = ngrp;
-    uint64_t *out = c.cand + (int64_t)row * c.cap;
-    // warp w rescans groups w, w + NWARPS, ...: four loads in flight per lane
-    for (int i0 = warp; i0 < n; i0 += 4 * NWARPS) {
-        float v[4];
-#pragma unroll
-        for (int r = 0; r < 4; r++) {
-            const int i = i0 + r * NWARPS;
-            v[r] = i < n ? __ldcg(&x[grp[i] * 32 + lane]) : 0.0f;
+        for (int j = 0; j < LMT_PER; j++) {
+            const int g = tid + j * NTHREADS;
+            gk[j] = g < ng ? __ldcg(&c.gmax[(int64_t)row * ng + g]) : 0u;
         }
+        if (tid == 0) napp = ngrp = 0;
+        const uint32_t t = hist_select(
+            [&](auto fn) {
 #pragma unroll
-        for (int r = 0; r < 4; r++) {
-            const int i = i0 + r * NWARPS;
-            const uint32_t k = cand_key(v[r]);
-            const uint32_t id = i < n ? (uint32_t)(grp[i] * 32 + lane) : 0u;
-            warp_append(i < n && k >= t, composite(k, id), out, &napp);
+                for (int j = 0; j < LMT_PER; j++) fn(gk[j]);
+            },
+            K, K + 64, sm);
+        // the groups to rescan
+#pragma unroll
+        for (int j = 0; j < LMT_PER; j++)
+            if (gk[j] >= t) grp[atomicAdd(&ngrp, 1)] = tid + j * NTHREADS;
+        __syncthreads();
+        const int n = ngrp;
+        uint64_t *out = c.cand + (int64_t)row * c.cap;
+        // warp w rescans groups w, w + NWARPS, ...: four loads in flight per lane
+        for (int i0 = warp; i0 < n; i0 += 4 * NWARPS) {
+            float v[4];
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                const int i = i0 + r * NWARPS;
+                v[r] = i < n ? __ldcg(&x[grp[i] * 32 + lane]) : 0.0f;
+            }
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                const int i = i0 + r * NWARPS;
+                const uint32_t k = cand_key(v[r]);
+                const uint32_t id = i < n ? (uint32_t)(grp[i] * 32 + lane) : 0u;
+                warp_append(i < n && k >= t, composite(k, id), out, &napp);
+            }
         }
-    }
-    __syncthreads();
-    if (tid == 0) {
-        c.cnt[row] = napp;
-        c.thr[row] = (uint64_t)t << 32;
+        __syncthreads();
+        if (tid == 0) {
+            c.cnt[row] = napp;
+            c.thr[row] = (uint64_t)t << 32;
+        }
+        __syncthreads();  // napp, ngrp and grp are reused by the next row
     }
 }
 
@@ -1468,7 +1475,7 @@ cudaError_t launch_shard_merge(const SampleArgs &a, cudaStream_t s)
 cudaError_t launch_lm_threshold(const SampleArgs &a, const LmCand &c, cudaStream_t s)
 {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)a.rows);
+    cfg.gridDim = dim3((unsigned)std::min(a.rows, LMT_CTAS));
     cfg.blockDim = dim3(NTHREADS);
     cfg.stream = s;
     cudaLaunchAttribute at[1];
