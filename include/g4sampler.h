@@ -226,7 +226,10 @@ int32_t g4s_sample_topk_noalloc(const void *logits, int32_t dtype, int32_t rows,
  * the logits at or above the threshold (by value, then lower id) to the row's
  * candidate list, from which the exact top K is taken -- the logits never go
  * to memory, and the tokens equal those of the unfused path.  Other calls
- * keep the logits in a context buffer allocated by the first call.
+ * keep the logits in a context buffer.  Either path's buffers are allocated
+ * by the first call that needs them (make it outside stream capture; later
+ * calls of the same or smaller shape allocate nothing and may be captured
+ * with broadcast params).
  */
 /* Waits for the device, then reports whether a kernel of this context gave up
    a bounded wait (G4S_ERR_TIMEOUT; the flag is cleared) since the last check. */
