@@ -422,7 +422,8 @@ def run_c5(rank, world, local, dev, peak, steps=50):
 
     rows = 1024
     full = synth.c5_logits(rows)  # identical on every rank
-    prm = g4.params_array(synth.c5_params(rows))  # converted once, reused every step
+    c5p = synth.c5_params(rows)
+    prm = g4.params_array(c5p)  # converted once, reused every step
     u = torch.from_numpy(synth.uniforms(rows, synth.SEEDS["c5"])).to(dev)
     out = torch.empty(rows, dtype=torch.int32, device=dev)
     # a stream of our own: the events below are recorded on it, and its handle
@@ -522,7 +523,8 @@ def run_c5(rank, world, local, dev, peak, steps=50):
                 "per_gpu_hbm_frac_of_peak": rows * n * 4 / (us * 1e-6) / 1e9 / peak,
                 "phases_us": {"lists": us_lists, "merge": us_merge, "exchange": max(0.0, us - us_lists - us_merge)},
                 "lists_hbm_frac_of_peak": rows * n * 4 / (us_lists * 1e-6) / 1e9 / peak,
-                "allgather_bytes_per_rank": rows * (g4.SHARD_LIST * 8 + 4),
+                # each row's own slots (its top_k; 2 for a full-vocabulary row), packed, plus the counts
+                "allgather_bytes_per_rank": sum(2 if (k <= 0 or k >= VOCAB) else k for _, k, _ in c5p) * 8 + rows * 4,
                 "config": f"C5 sharded: B=1024 x V=262144 fp32, a {n}-id slice per rank; per-row T~U[0.3,1.5], "
                           "K in {1,20,64,200}, P~U[0.5,1]; lists -> ncclAllGather x2 -> merge; "
                           f"{steps} steps, host loop, CUDA events, max over ranks; phases timed alone"})

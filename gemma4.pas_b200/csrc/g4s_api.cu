@@ -69,6 +69,7 @@ struct g4s_ctx {
     cudaEvent_t shard_ev = nullptr;                           // g4s_shard_wait's marker
     uint64_t *sh_send = nullptr;  // [max_rows][KMAX] this rank's lists, then [max_rows] counts
     uint64_t *sh_recv = nullptr;  // [world][max_rows][KMAX], then [world][max_rows] counts
+    int32_t *sh_off = nullptr;    // [max_rows] packed list offsets of a g4s_shard_sample step
     // LM head workspace (first g4s_lmhead_sample call): fp32 logits and fp16 hidden
     float *lm_logits = nullptr;
     void *lm_xh = nullptr;
@@ -214,7 +215,9 @@ static void shard_release(g4s_ctx *ctx, bool abort = false)
     ctx->nccl_comm = nullptr;
     if (ctx->sh_send) cudaFree(ctx->sh_send);
     if (ctx->sh_recv) cudaFree(ctx->sh_recv);
+    if (ctx->sh_off) cudaFree(ctx->sh_off);
     ctx->sh_send = ctx->sh_recv = nullptr;
+    ctx->sh_off = nullptr;
     ctx->shard_world = 0;
 }
 
@@ -909,7 +912,7 @@ int32_t g4s_device_status(g4s_ctx *ctx)
 static int32_t shard_lists_core(g4s_ctx *ctx, const void *logits, int32_t dtype, int32_t rows, int32_t slice_vocab,
                                 int64_t row_stride, int32_t id_offset, int32_t vocab_total, const g4s_params *params,
                                 int32_t params_stride, float softcap, uint64_t *out_lists, int32_t *out_counts,
-                                void *stream, const RowParams *staged)
+                                void *stream, const RowParams *staged, const int32_t *list_off = nullptr)
 {
     static const char *who = "g4s_shard_lists";
     if (!ctx) return fail(nullptr, G4S_ERR_ARG, "%s: ctx is NULL", who);
@@ -955,6 +958,7 @@ static int32_t shard_lists_core(g4s_ctx *ctx, const void *logits, int32_t dtype,
     a.id_offset = id_offset;
     a.list_out = out_lists;
     a.list_cnt = out_counts;
+    a.list_off = list_off;
     a.softcap = softcap;
     a.invcap = softcap > 0.0f ? 1.0f / softcap : 0.0f;
     if (staged) a.params = *staged;
@@ -979,7 +983,8 @@ static int32_t shard_lists_core(g4s_ctx *ctx, const void *logits, int32_t dtype,
 static int32_t shard_merge_core(g4s_ctx *ctx, const uint64_t *lists, const int32_t *counts, int32_t world,
                                 int32_t rows, int32_t vocab_total, const g4s_params *params, int32_t params_stride,
                                 float softcap, const double *u, int32_t *out_tokens, const g4s_outputs *extra,
-                                void *stream, const RowParams *staged)
+                                void *stream, const RowParams *staged, const int32_t *list_off = nullptr,
+                                int64_t list_total = 0)
 {
     static const char *who = "g4s_shard_merge";
     if (!ctx) return fail(nullptr, G4S_ERR_ARG, "%s: ctx is NULL", who);
@@ -1019,6 +1024,8 @@ static int32_t shard_merge_core(g4s_ctx *ctx, const uint64_t *lists, const int32
     a.glists = lists;
     a.gcnts = counts;
     a.gworld = world;
+    a.list_off = list_off;
+    a.list_total = list_total;
     a.shard_tgt = ctx->shard_tgt;
     if (staged) a.params = *staged;
     else if ((rc = stage_params(ctx, who, params, params_stride, rows, s, a.params)) != G4S_OK) return rc;
@@ -1134,7 +1141,8 @@ int32_t g4s_shard_init(g4s_ctx *ctx, int32_t world, int32_t rank, int32_t vocab_
     if (!guard.ok) return fail(ctx, G4S_ERR_CUDA, "%s: cannot select device %d", who, ctx->device);
     const size_t per_rank = (size_t)ctx->max_rows * (KMAX_ + 1) * sizeof(uint64_t);
     if (cudaMalloc(&ctx->sh_send, per_rank) != cudaSuccess ||
-        cudaMalloc(&ctx->sh_recv, per_rank * (size_t)world) != cudaSuccess) {
+        cudaMalloc(&ctx->sh_recv, per_rank * (size_t)world) != cudaSuccess ||
+        cudaMalloc(&ctx->sh_off, (size_t)ctx->max_rows * sizeof(int32_t)) != cudaSuccess) {
         cudaGetLastError();
         shard_release(ctx);
         return fail(ctx, G4S_ERR_NOMEM, "%s: cannot allocate the exchange buffers", who);
@@ -1203,8 +1211,22 @@ int32_t g4s_shard_sample(g4s_ctx *ctx, const void *logits_slice, int32_t dtype, 
     RowParams rp;
     memset(&rp, 0, sizeof(rp));
     if ((rc = stage_params(ctx, who, params, params_stride, rows, s, rp)) != G4S_OK) return rc;
+    // the exchange carries each row's own slots (its top_k; 2 for a
+    // full-vocabulary row's summary) packed back to back: every rank computes
+    // the same offsets from the same params
+    int64_t P = 0;
+    for (int r = 0; r < rows; r++) P += shard_slots(params[params_stride ? r : 0].top_k, ctx->shard_vocab);
+    {
+        SampleArgs ao;
+        memset(&ao, 0, sizeof(ao));
+        ao.rows = rows;
+        ao.vocab = ctx->shard_vocab;
+        ao.params = rp;
+        const cudaError_t e = launch_shard_offsets(ao, ctx->sh_off, s);
+        if (e != cudaSuccess) return fail(ctx, G4S_ERR_CUDA, "%s: launch failed: %s", who, cudaGetErrorString(e));
+    }
     rc = shard_lists_core(ctx, logits_slice, dtype, rows, n, row_stride, off, ctx->shard_vocab, params, params_stride,
-                          softcap, send, send_cnt, s, &rp);
+                          softcap, send, send_cnt, s, &rp, ctx->sh_off);
     if (rc != G4S_OK) return rc;
     ncclComm_t comm = (ncclComm_t)ctx->nccl_comm;
     {
@@ -1220,14 +1242,14 @@ int32_t g4s_shard_sample(g4s_ctx *ctx, const void *logits_slice, int32_t dtype, 
     // a call of a non-blocking communicator succeeds or is still in progress
     auto ok = [](ncclResult_t x) { return x == ncclSuccess || x == ncclInProgress; };
     ncclResult_t r = g_nccl.GroupStart();
-    if (ok(r)) r = g_nccl.AllGather(send, recv, (size_t)rows * KMAX_, ncclUint64, comm, s);
+    if (ok(r)) r = g_nccl.AllGather(send, recv, (size_t)P, ncclUint64, comm, s);
     if (ok(r)) r = g_nccl.AllGather(send_cnt, recv_cnt, (size_t)rows, ncclInt32, comm, s);
     const ncclResult_t r2 = g_nccl.GroupEnd();
     if (ok(r)) r = r2;
     if ((rc = nccl_group_done(ctx, who, "all-gather", r)) != G4S_OK) return rc;
-    // the merge reads list w of row i at recv + w * rows * KMAX + i * KMAX
+    // the merge reads list w of row i at recv + w * P + offset[i]
     rc = shard_merge_core(ctx, recv, recv_cnt, W, rows, ctx->shard_vocab, params, params_stride, softcap, u, out_tokens,
-                          extra, s, &rp);
+                          extra, s, &rp, ctx->sh_off, P);
     if (rc != G4S_OK || !sr.any_full_draw) return rc;
     // full-vocabulary draws: the rank whose slice holds the crossing writes the
     // token, the others keep -1; a max over the ranks gives every rank the token

@@ -1216,8 +1216,8 @@ __global__ void __launch_bounds__(COMBINE_THREADS) full_combine_kernel(SampleArg
         // and the mass sum 2^(s L2E) in units of 2^(M L2E), in the row's list slot
         if (t == 0) {
             const uint32_t gid = (uint32_t)(a.id_offset + token);
-            a.list_out[(int64_t)row * KMAX + 0] = (uint64_t)__float_as_uint(M) | ((uint64_t)gid << 32);
-            a.list_out[(int64_t)row * KMAX + 1] = (uint64_t)__double_as_longlong(S);
+            a.list_out[list_pos(a, row) + 0] = (uint64_t)__float_as_uint(M) | ((uint64_t)gid << 32);
+            a.list_out[list_pos(a, row) + 1] = (uint64_t)__double_as_longlong(S);
             a.list_cnt[row] = -1;
         }
         return;

@@ -76,6 +76,8 @@ struct SampleArgs {
     const uint64_t *glists;    // shard merge: gathered lists [gworld][rows][KMAX]
     const int32_t *gcnts;      //   and their lengths [gworld][rows]
     int32_t gworld;
+    const int32_t *list_off;   // non-null: lists packed, row r's at list_off[r] (slots: its top_k,
+    int64_t list_total;        //   2 for a full-vocabulary row), list_total slots per rank
     int32_t shard_mode;        // full-path combine: 0 sample; 1 write the slice summary of each
                                //   full-vocabulary row to list_out (count -1); 2 resolve the draws
                                //   shard_tgt assigns to shard_rank
@@ -87,6 +89,24 @@ struct SampleArgs {
     int64_t wait_limit;        // 0: the kernels' own poll limits; > 0: test hook, every
                                //   bounded wait gives up after this many non-blocking polls
 };
+
+// Position of row r's list in list_out (this rank) and in the gathered glists
+// (rank w): [rows][KMAX] slots, or packed at list_off[r] with list_total slots
+// per rank.
+__host__ __device__ __forceinline__ int64_t list_pos(const SampleArgs &a, int r)
+{
+    return a.list_off ? (int64_t)a.list_off[r] : (int64_t)r * 256;
+}
+__host__ __device__ __forceinline__ int64_t glist_pos(const SampleArgs &a, int w, int r)
+{
+    return a.list_off ? (int64_t)w * a.list_total + a.list_off[r] : ((int64_t)w * a.rows + r) * 256;
+}
+// the packed slots of a row: its top_k, 2 for a full-vocabulary row (its summary)
+__host__ __device__ __forceinline__ int shard_slots(int top_k, int vocab_total)
+{
+    return (top_k <= 0 || top_k >= vocab_total) ? 2 : top_k;
+}
+cudaError_t launch_shard_offsets(const SampleArgs &a, int32_t *off, cudaStream_t s);
 
 // Single-row latency path of the top-K selection: one cluster of TOPK_CLUSTER
 // CTAs (16384 ids each) per row; used for a few rows with vocab <= 262144.

@@ -36,6 +36,7 @@
 namespace g4s {
 
 constexpr int HB = 2048;  // bins of one hist_level (11 bits of the keys), kept in sm.L
+static_assert(KMAX == 256, "list_pos / glist_pos lay lists out in KMAX slots");
 
 struct TopkSmem {
     alignas(16) uint64_t L[CAP2];
@@ -479,7 +480,7 @@ __device__ int merge_segments(TopkSmem &sm, int *off, int nseg, int K)
 // j-th entries is a lower bound on the K-th largest; the entries above it are
 // gathered (a prefix of each list), sorted and cut to K.  Returns kw.
 __device__ int merge_lists(int K, TopkSmem &sm, const uint64_t *C, int64_t lstride, const int32_t *CC,
-                           int64_t cstride, int nch)
+                           int64_t cstride, int nch, int cmax = KMAX)
 {
     const int tid = threadIdx.x;
     if (nch <= 8) {
@@ -489,10 +490,10 @@ __device__ int merge_lists(int K, TopkSmem &sm, const uint64_t *C, int64_t lstri
         // More lists (the chunked pass's 32 per row): the bound below keeps
         // the copy to about K entries, cheaper than merging them all
         int *loff = reinterpret_cast<int *>(sm.hist);  // list start offsets (nch + 1 <= 256 ints)
-        // counts clamped to a list's capacity: a list slot never holds more,
+        // counts clamped to a list's capacity (cmax): a list never holds more,
         // and an exchange cut short (an aborted collective) cannot send a read
         // past it
-        const int cc = tid < nch ? min(max(__ldcg(&CC[tid * cstride]), 0), KMAX) : 0;
+        const int cc = tid < nch ? min(max(__ldcg(&CC[tid * cstride]), 0), cmax) : 0;
         int total;
         const int off = block_excl_scan(cc, &total, sm.scan);
         if (total <= CAP2) {
@@ -519,7 +520,7 @@ __device__ int merge_lists(int K, TopkSmem &sm, const uint64_t *C, int64_t lstri
     // lower bound t2: the mm-th largest of the lists' j-th entries
     for (int c = tid; c < nch; c += NTHREADS) {
         uint64_t h = 0;
-        if (min(__ldcg(&CC[c * cstride]), KMAX) >= j) h = __ldcg(&C[c * lstride + j - 1]);
+        if (min(__ldcg(&CC[c * cstride]), cmax) >= j) h = __ldcg(&C[c * lstride + j - 1]);
         sm.L[c] = h;
     }
     __syncthreads();
@@ -553,7 +554,7 @@ __device__ int merge_lists(int K, TopkSmem &sm, const uint64_t *C, int64_t lstri
 #pragma unroll
     for (int r = 0; r < CPT; r++) {
         const int c = tid * CPT + r;
-        pc[r] = c < nch ? prefix_at_least(C + c * lstride, min(__ldcg(&CC[c * cstride]), KMAX), t2) : 0;
+        pc[r] = c < nch ? prefix_at_least(C + c * lstride, min(__ldcg(&CC[c * cstride]), cmax), t2) : 0;
         cnt += pc[r];
     }
     const int slots = nch * K;
@@ -588,20 +589,20 @@ __device__ int merge_lists(int K, TopkSmem &sm, const uint64_t *C, int64_t lstri
         [&](auto fn) {
             for (int s = tid; s < slots; s += NTHREADS) {
                 const int c = s / K, i = s - c * K;
-                if (i < __ldcg(&CC[c * cstride])) fn(__ldcg(&C[c * lstride + i]));
+                if (i < min(__ldcg(&CC[c * cstride]), cmax)) fn(__ldcg(&C[c * lstride + i]));
             }
         },
         K, sm);
     int c2 = 0;
     for (int s = tid; s < slots; s += NTHREADS) {
         const int c = s / K, i = s - c * K;
-        if (i < __ldcg(&CC[c * cstride]) && __ldcg(&C[c * lstride + i]) >= kth) c2++;
+        if (i < min(__ldcg(&CC[c * cstride]), cmax) && __ldcg(&C[c * lstride + i]) >= kth) c2++;
     }
     int tot2;
     int o2 = block_excl_scan(c2, &tot2, sm.scan);
     for (int s = tid; s < slots; s += NTHREADS) {
         const int c = s / K, i = s - c * K;
-        if (i < __ldcg(&CC[c * cstride])) {
+        if (i < min(__ldcg(&CC[c * cstride]), cmax)) {
             const uint64_t v = __ldcg(&C[c * lstride + i]);
             if (v >= kth) sm.L[o2++] = v;
         }
@@ -620,7 +621,7 @@ __device__ void topk_merge(const SampleArgs &a, int row, const g4s_params &p, To
                                a.cand_cnt + (int64_t)row * nch, 1, nch);
     if (a.list_out) {
         __syncthreads();
-        for (int i = tid; i < kw; i += NTHREADS) a.list_out[(int64_t)row * KMAX + i] = sm.L[i];
+        for (int i = tid; i < kw; i += NTHREADS) a.list_out[list_pos(a, row) + i] = sm.L[i];
         if (tid == 0) a.list_cnt[row] = kw;
     } else {
         finish_row(a, row, p, kw, sm);
@@ -635,7 +636,7 @@ __device__ __forceinline__ void finish_single_chunk(const SampleArgs &a, int row
 {
     const int tid = threadIdx.x;
     if (a.list_out) {
-        for (int i = tid; i < m; i += NTHREADS) a.list_out[(int64_t)row * KMAX + i] = sm.L[i];
+        for (int i = tid; i < m; i += NTHREADS) a.list_out[list_pos(a, row) + i] = sm.L[i];
         if (tid == 0) a.list_cnt[row] = m;
     } else {
         finish_row(a, row, p, m, sm);
@@ -663,7 +664,7 @@ __device__ void shard_full_row(const SampleArgs &a, int row, const g4s_params &p
     bool ok = true;
     for (int w = 0; w < W; w++) {
         ok &= __ldcg(&a.gcnts[(int64_t)w * a.rows + row]) == -1;
-        const uint64_t r0 = __ldcg(&a.glists[((int64_t)w * a.rows + row) * KMAX]);
+        const uint64_t r0 = __ldcg(&a.glists[glist_pos(a, w, row)]);
         const float Mw = __uint_as_float((uint32_t)r0);
         if (Mw > M) {
             M = Mw;
@@ -683,7 +684,7 @@ __device__ void shard_full_row(const SampleArgs &a, int row, const g4s_params &p
         const double Ml = (double)M * (double)G4_L2E;
         double S = 0.0;
         for (int w = 0; w < W; w++) {
-            const int64_t o = ((int64_t)w * a.rows + row) * KMAX;
+            const int64_t o = glist_pos(a, w, row);
             const float Mw = __uint_as_float((uint32_t)__ldcg(&a.glists[o]));
             if (Mw > NEG_INF) S += __longlong_as_double((long long)__ldcg(&a.glists[o + 1])) * exp2((double)Mw * (double)G4_L2E - Ml);
         }
@@ -691,7 +692,7 @@ __device__ void shard_full_row(const SampleArgs &a, int row, const g4s_params &p
         const double target = (double)thr * S;
         double cum = 0.0;
         for (int w = 0; w < W && tg.w < 0; w++) {
-            const int64_t o = ((int64_t)w * a.rows + row) * KMAX;
+            const int64_t o = glist_pos(a, w, row);
             const float Mw = __uint_as_float((uint32_t)__ldcg(&a.glists[o]));
             if (!(Mw > NEG_INF)) continue;
             const double sc = exp2((double)Mw * (double)G4_L2E - Ml);
@@ -727,9 +728,34 @@ __global__ void __launch_bounds__(NTHREADS) shard_merge_kernel(SampleArgs a)
         return;
     }
     if (K > KMAX) return;  // the host admits top-K rows up to KMAX only
-    const int kw = merge_lists(K, sm, a.glists + (int64_t)row * KMAX, (int64_t)a.rows * KMAX, a.gcnts + row,
-                               a.rows, a.gworld);
+    const int kw = merge_lists(K, sm, a.glists + glist_pos(a, 0, row), a.list_off ? a.list_total : (int64_t)a.rows * KMAX,
+                               a.gcnts + row, a.rows, a.gworld, K);
     finish_row(a, row, p, kw, sm);
+}
+
+// Packed list offsets of the sharded exchange: row r's list starts after the
+// slots of the rows before it (its top_k; 2 for a full-vocabulary row).  One
+// CTA: each thread sums a run of consecutive rows, a block scan places the runs.
+__global__ void __launch_bounds__(1024) shard_offsets_kernel(SampleArgs a, int32_t *off)
+{
+    __shared__ int wsum[32];
+    const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+    const int per = (a.rows + 1023) / 1024;
+    const int r0 = t * per;
+    int sum = 0;
+    for (int i = 0; i < per; i++)
+        if (r0 + i < a.rows) sum += shard_slots(a.params.get(r0 + i).top_k, a.vocab);
+    const int inc = warp_incl_scan(sum);
+    if (lane == 31) wsum[w] = inc;
+    __syncthreads();
+    if (w == 0) wsum[lane] = warp_incl_scan(wsum[lane]);
+    __syncthreads();
+    int run = (w ? wsum[w - 1] : 0) + inc - sum;
+    for (int i = 0; i < per; i++)
+        if (r0 + i < a.rows) {
+            off[r0 + i] = run;
+            run += shard_slots(a.params.get(r0 + i).top_k, a.vocab);
+        }
 }
 
 // ---------------------------------------------------------------------------
@@ -1469,6 +1495,12 @@ static cudaError_t launch_cluster_t(const SampleArgs &a, cudaStream_t s)
 cudaError_t launch_shard_merge(const SampleArgs &a, cudaStream_t s)
 {
     shard_merge_kernel<<<a.rows, NTHREADS, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_shard_offsets(const SampleArgs &a, int32_t *off, cudaStream_t s)
+{
+    shard_offsets_kernel<<<1, 1024, 0, s>>>(a, off);
     return cudaGetLastError();
 }
 

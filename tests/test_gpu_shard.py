@@ -228,6 +228,29 @@ def _nccl_rank(rank, world, uid_path, x, prm, u, out_path):
     s.close()
 
 
+def test_nccl_one_rank_packed_exchange(g4, torch_cuda, tmp_path):
+    # the NCCL form on a one-rank communicator (one GPU is enough): its
+    # exchange packs each row's own slots; mixed top-K and full rows, per-row
+    # params, must equal g4s_sample on the whole rows
+    torch = torch_cuda
+    import torch.multiprocessing as mp
+
+    V, rows = 262144, 24
+    x = synth.c5_logits(rows, step=78)
+    prm = _full_params(rows)
+    u = synth.uniforms(rows, 0x78)
+    uid_path = str(tmp_path / "uid.bin")
+    open(uid_path, "wb").write(g4.shard_unique_id())
+    out_path = str(tmp_path / "tok%d.npy")
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.spawn(_nccl_rank, args=(1, uid_path, x, prm, u, out_path), nprocs=1, join=True)
+    got = np.load(out_path % 0)
+    xd = torch.from_numpy(x).cuda()
+    ud = torch.from_numpy(u).cuda()
+    want, _ = _unsharded(g4, torch, xd, F32, rows, V, prm, ud)
+    np.testing.assert_array_equal(got, want)
+
+
 @pytest.mark.parametrize("mixed", [False, True])
 def test_nccl_ranks(g4, torch_cuda, oracle, tmp_path, mixed):
     # top-K rows, and (mixed) full-vocabulary rows with the resolve and the
