@@ -284,7 +284,7 @@ static int32_t stage_params(g4s_ctx *ctx, const char *who, const g4s_params *par
         ctx->params_slot = (k + 1) % PSLOTS;
         if (ctx->params_ev_pending[k] && cudaEventSynchronize(ctx->params_ev[k]) != cudaSuccess)
             return fail(ctx, G4S_ERR_CUDA, "%s: waiting on an earlier params copy failed", who);
-        const size_t slot_bytes = (size_t)ctx->max_rows * (sizeof(g4s_params) + sizeof(float));
+        const size_t slot_bytes = (size_t)ctx->max_rows * (sizeof(g4s_params) + sizeof(float) + sizeof(int32_t));
         g4s_params *hp = (g4s_params *)((char *)ctx->params_pinned + k * slot_bytes);
         g4s_params *dp = (g4s_params *)((char *)ctx->params_dev + k * slot_bytes);
         memcpy(hp, params, (size_t)rows * sizeof(g4s_params));
@@ -293,7 +293,26 @@ static int32_t stage_params(g4s_ctx *ctx, const char *who, const g4s_params *par
             const float T = params[r].temperature;
             inv_t[r] = (T > 0.0f && T != 1.0f) ? 1.0f / T : 1.0f;
         }
-        if (cudaMemcpyAsync(dp, hp, (size_t)rows * (sizeof(g4s_params) + sizeof(float)), cudaMemcpyHostToDevice, s) !=
+        // launch order of the streaming top-K pass: its CTAs take longer the
+        // larger the row's top_k, so the rows go by descending top_k (rows of
+        // other paths last) and the short ones fill the last partial wave
+        int32_t *ord = (int32_t *)(inv_t + rows);
+        {
+            int cnt[KMAX_ + 2] = {};
+            auto bucket = [&](int r) {
+                const int k = params[r].top_k;
+                return (k > 0 && k <= KMAX_) ? KMAX_ - k : KMAX_ + 1;  // descending top_k
+            };
+            for (int r = 0; r < rows; r++) cnt[bucket(r)]++;
+            int o = 0;
+            for (int b = 0; b < KMAX_ + 2; b++) {
+                const int c = cnt[b];
+                cnt[b] = o;
+                o += c;
+            }
+            for (int r = 0; r < rows; r++) ord[cnt[bucket(r)]++] = r;
+        }
+        if (cudaMemcpyAsync(dp, hp, (size_t)rows * (sizeof(g4s_params) + sizeof(float) + sizeof(int32_t)), cudaMemcpyHostToDevice, s) !=
                 cudaSuccess ||
             cudaEventRecord(ctx->params_ev[k], s) != cudaSuccess) {
             cudaError_t e = cudaGetLastError();
@@ -302,8 +321,10 @@ static int32_t stage_params(g4s_ctx *ctx, const char *who, const g4s_params *par
         ctx->params_ev_pending[k] = true;
         out.dev = dp;
         out.inv_t_dev = (const float *)(dp + rows);
+        out.order_dev = (const int32_t *)(out.inv_t_dev + rows);
     } else {
         out.dev = nullptr;
+        out.order_dev = nullptr;
         out.p0 = params[0];
         const float T = params[0].temperature;
         out.inv_t0 = (T > 0.0f && T != 1.0f) ? 1.0f / T : 1.0f;
@@ -487,7 +508,7 @@ int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t
     const size_t o_rs = off; off = align(off + (size_t)max_rows * sizeof(RowStat));
     const size_t o_li = off; off = align(off + (size_t)LK_SLOTS * max_vocab * sizeof(int32_t));
     const size_t o_lv = off; off = align(off + (size_t)LK_SLOTS * max_vocab * sizeof(float));
-    const size_t o_pd = off; off = align(off + (size_t)PSLOTS * max_rows * (sizeof(g4s_params) + sizeof(float)));
+    const size_t o_pd = off; off = align(off + (size_t)PSLOTS * max_rows * (sizeof(g4s_params) + sizeof(float) + sizeof(int32_t)));
     const size_t o_err = off; off = align(off + sizeof(int));
     const size_t o_tab = off; off = align(off + (size_t)SC_TABLE_BYTES);
     const size_t o_etab = off; off = align(off + (size_t)ETAB_TABLE_BYTES);
@@ -513,7 +534,7 @@ int32_t g4s_create(int32_t device, int32_t max_rows, int32_t max_vocab, uint32_t
     ctx->shard_tgt = (ShardTarget *)(base + o_stg);
     if (cudaMemset(ctx->ws, 0, off) != cudaSuccess ||
         cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaHostAlloc((void **)&ctx->params_pinned, (size_t)PSLOTS * max_rows * (sizeof(g4s_params) + sizeof(float)),
+        cudaHostAlloc((void **)&ctx->params_pinned, (size_t)PSLOTS * max_rows * (sizeof(g4s_params) + sizeof(float) + sizeof(int32_t)),
                       cudaHostAllocDefault) != cudaSuccess ||
         !create_param_events(ctx)) {
         cudaGetLastError();

@@ -16,6 +16,8 @@ struct RowParams {
     const float *inv_t_dev; // [rows] fl32(1/temperature), when dev != nullptr
     g4s_params p0;          // used when dev == nullptr
     float inv_t0;           // fl32(1/p0.temperature)
+    const int32_t *order_dev;  // [rows] with dev: the rows by descending top_k (launch order of
+                               //   the streaming top-K pass), or nullptr for row order
     __device__ __forceinline__ g4s_params get(int r) const { return dev ? dev[r] : p0; }
     __device__ __forceinline__ float inv_t(int r) const { return dev ? inv_t_dev[r] : inv_t0; }
 };

@@ -1235,7 +1235,10 @@ __global__ void __launch_bounds__(NTHREADS, 3) topk_stream_kernel(SampleArgs a)
 {
     __shared__ TopkSmem sm;
     extern __shared__ __align__(128) uint8_t stream_ring[];  // STREAM_DYN_SMEM: tile ring + mbarriers
-    const int row = blockIdx.y, chunk = blockIdx.x, tid = threadIdx.x;
+    // CTAs are dispatched in block order: with per-row params the rows come by
+    // descending top_k (a permutation of the rows)
+    const int row = a.params.order_dev ? a.params.order_dev[blockIdx.y] : (int)blockIdx.y;
+    const int chunk = blockIdx.x, tid = threadIdx.x;
     const g4s_params p = a.params.get(row);
     const int K = p.top_k;
     if (!(K > 0 && K < a.vocab && K <= KMAX)) return;
